@@ -1,0 +1,473 @@
+#!/usr/bin/env python
+"""Benchmark: fused INT4 paged flash-decode attention on B200 (+ quantizer GB/s).
+
+One step = one decode-attention pass of BASELINE config 0 per GPU
+(8 sequences x 32 heads x d128 x 2048 tokens, 16-token pages in a seeded
+random block table, INT4 keys with per-(128-token group, head, channel)
+scale/zp, fp32 values), inputs resident in HBM. With N GPUs every rank owns
+its own config-0 batch (batch x heads sharded, no collective): weak scaling.
+
+Prints ONE JSON line (rank 0). `value` = algorithmic HBM bytes of all ranks
+per step / step time (max over ranks), in GB/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own CPU implementation of the path
+(the NumPy oracle restated in oracle/, all host cores) on the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "int4-kv-cache-quantization-cuda-triton-pallas_b200"
+METRIC = "INT4 paged decode-attn µs & HBM GB/s (frac of ~8 TB/s); quantizer GB/s"
+FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg0")
+    ap.add_argument("--e2e-steps", type=int, default=300)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-quantizer", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "paged_decode_cfg0.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+def workload_config(shape, name, world):
+    return {"workload": f"{name}: decode step, batch {shape.batch} x {shape.heads} heads x "
+                        f"d{shape.head_dim} x {shape.seq_lens[0]} tokens per GPU, 16-token pages "
+                        "(seeded random block table), INT4 keys / 128-token groups, fp32 q and values",
+            "batch_per_gpu": shape.batch, "global_batch": shape.batch * world,
+            "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": shape.seq_lens[0],
+            "page_tokens": 16, "group_tokens": shape.group_tokens,
+            "l2": "flushed (256 MiB write, untimed) before every timed step; inputs "
+                  f"{shape.algorithmic_bytes() / 1e6:.1f} MB/GPU > 126 MB L2",
+            "parallelism": f"dp{world} (batch x heads sharded, no collective)"}
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons in a background thread."""
+
+    def __init__(self, index, period=0.01):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        self._mark = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self.period = period
+
+    def _reasons(self):
+        nv = self._nv
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        names = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+                 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+        return [n for bit, n in names.items() if r & bit]
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM)
+                self.samples.append((time.perf_counter(), mhz, self._reasons()))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def mark(self, t0, t1):
+        self._mark = (t0, t1)
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        t0, t1 = self._mark if self._mark else (-1e30, 1e30)
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        use = inside if len(inside) >= 3 else self.samples
+        reasons = sorted({r for s in use for r in s[2]} - {"gpu_idle"})
+        return {"sm_mhz": statistics.median(s[1] for s in use), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(use),
+                "window": "timed region" if use is inside else "warmup + timed region"}
+
+
+def _all_reduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(arrays, streams, bytes_per_stream, seconds_target=2.0):
+    """Time the oracle (spawn pool, all host cores) on a bounded sample of streams."""
+    from oracle.cpu_pool import OraclePool
+    pool = OraclePool(arrays)
+    try:
+        reps, wall = 0, 0.0
+        while wall < seconds_target or reps == 0:
+            dt, outs = pool.run(streams)
+            wall += dt
+            reps += 1
+    finally:
+        pool.close()
+    gbs = reps * len(streams) * bytes_per_stream / wall / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": pool.procs, "kind": "port",
+            "sample": f"{len(streams)} of the config's (sequence, head) streams x {reps} reps, "
+                      f"oracle online softmax per stream (NumPy, 1 BLAS thread per process, "
+                      f"{pool.procs} spawn processes), {wall:.2f} s wall",
+            "ms_per_stream": round(1e3 * wall / (reps * len(streams)) * pool.procs, 3)}, outs
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+
+def run_ours(args):
+    import ctypes
+    import importlib
+    import torch
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    importlib.import_module(PKG + "._build").build()
+    W = importlib.import_module(PKG + ".workloads")
+    C = importlib.import_module(PKG + "._C")
+    lib = importlib.import_module(PKG + "._lib").load()
+
+    shape = W.config_shape(args.config)
+    prob = W.torch_build_cache(shape, seed=7 + 1000 * rank)
+    cache, query = prob["cache"], prob["query"]
+    ids = list(range(shape.batch))
+    bt, sl = cache.block_table(ids)
+    d, h = shape.head_dim, shape.heads
+    out = torch.empty_like(query)
+    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, h, h, d)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    maxp, npages = bt.shape[1], cache.num_pages
+
+    def call_args(q_ptr, out_ptr, ev0=None, ev1=None):
+        return (q_ptr, cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), cache.sz_pool.data_ptr(),
+                bt.data_ptr(), sl.data_ptr(), shape.batch, h, h, d, 16, shape.group_tokens, maxp,
+                npages, out_ptr, ws.data_ptr(), ws_bytes, None, stream.cuda_stream, ev0, ev1)
+
+    # correctness gate before timing: a sample of streams against the exact evaluation
+    C.paged_decode(query, cache.k_pool, cache.v_pool, cache.sz_pool, bt, sl, shape.group_tokens,
+                   out=out, workspace=ws)
+    torch.cuda.synchronize()
+    import oracle
+    host = {"query": query.cpu().numpy(), "k_pool": cache.k_pool.cpu().numpy(),
+            "v_pool": cache.v_pool.cpu().numpy(), "sz_pool": cache.sz_pool.cpu().numpy(),
+            "block_table": bt.cpu().numpy(), "seq_lens": sl.cpu().numpy()}
+    rng = np.random.default_rng(rank)
+    gate_streams = [(int(b), int(hh)) for b, hh in zip(rng.integers(0, shape.batch, 4),
+                                                       rng.integers(0, h, 4))]
+    ex = oracle.decode_paged(host["query"], host["k_pool"], host["v_pool"], host["sz_pool"],
+                             host["block_table"], host["seq_lens"], method="exact",
+                             streams=gate_streams)
+    o_host = out.cpu().numpy()
+    gate_err = max(float(np.abs(o_host[b, hh] - ex[b, hh]).max()) for b, hh in gate_streams)
+    if not (np.isfinite(o_host).all() and gate_err <= 1e-6):
+        raise RuntimeError(f"decode failed its correctness gate (max err {gate_err}); not timing")
+
+    flush = torch.empty((L2_FLUSH_BYTES,), dtype=torch.uint8, device="cuda")
+    K, Wm = args.steps, args.warmup
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for e in ev:  # materialise the CUDA events so their handles can go through the C ABI
+        for x in e:
+            x.record()
+    torch.cuda.synchronize()
+    fn = lib.int4kv_paged_decode_profiled
+    for i in range(Wm):
+        flush.fill_(i & 255)
+        rc = fn(*call_args(query.data_ptr(), out.data_ptr()))
+        if rc:
+            raise RuntimeError(f"decode launch failed: cudaError {rc}")
+    sampler = ClockSampler(local)
+    sampler.start()
+    torch.cuda.synchronize()
+    _barrier(world)
+    torch.cuda.synchronize()
+    t_wall0 = time.perf_counter()
+    for i in range(K):
+        flush.fill_(i & 255)
+        e0, e1, e2, e3 = ev[i]
+        e0.record()
+        rc = fn(*call_args(query.data_ptr(), out.data_ptr(), ctypes.c_void_p(e1.cuda_event),
+                           ctypes.c_void_p(e2.cuda_event)))
+        e3.record()
+        if rc:
+            raise RuntimeError(f"decode launch failed: cudaError {rc}")
+    torch.cuda.synchronize()
+    t_wall1 = time.perf_counter()
+    _barrier(world)
+    torch.cuda.synchronize()
+    sampler.mark(t_wall0, t_wall1)
+    step_ms = [e[0].elapsed_time(e[3]) for e in ev]
+    kern_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    mean_step = _all_reduce_max(sum(step_ms) / K, world)
+    mean_kern = _all_reduce_max(sum(kern_ms) / K, world)
+
+    # ---- end to end through the C ABI with host buffers ----
+    q_host = torch.empty_like(query, device="cpu").pin_memory()
+    q_host.copy_(query.cpu())
+    bt_host = bt.cpu().pin_memory()
+    sl_host = sl.cpu().pin_memory()
+    out_host = torch.empty_like(query, device="cpu").pin_memory()
+    q_dev = torch.empty_like(query)
+    bt_dev = torch.empty_like(bt)
+    sl_dev = torch.empty_like(sl)
+    KE = max(1, min(args.e2e_steps, K))
+    ee = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(KE)]
+
+    def e2e_args():
+        a = list(call_args(q_dev.data_ptr(), out.data_ptr()))
+        a[4], a[5] = bt_dev.data_ptr(), sl_dev.data_ptr()
+        return a
+
+    ea = e2e_args()
+    torch.cuda.synchronize()
+    _barrier(world)
+    for i in range(KE):
+        flush.fill_(i & 255)
+        ee[i][0].record()
+        q_dev.copy_(q_host, non_blocking=True)
+        bt_dev.copy_(bt_host, non_blocking=True)
+        sl_dev.copy_(sl_host, non_blocking=True)
+        rc = fn(*ea)
+        out_host.copy_(out, non_blocking=True)
+        ee[i][1].record()
+        if rc:
+            raise RuntimeError(f"decode launch failed: cudaError {rc}")
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_ms = _all_reduce_max(sum(a.elapsed_time(b) for a, b in ee) / KE, world)
+    if not torch.equal(out_host, out.cpu()):
+        raise RuntimeError("end-to-end output differs from the device-resident output")
+
+    # ---- quantizer GB/s, rank-local ----
+    quant = None
+    if not args.no_quantizer:
+        quant = {}
+        for n_tok in (2048, 8192, 32768, 131072):
+            kv = torch.randn((n_tok, 32, 128), device="cuda")
+            C.quantize_int4_grouped(kv, 128)
+            evq = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(20)]
+            for a, b in evq:
+                flush.fill_(1)
+                a.record()
+                C.quantize_int4_grouped(kv, 128)
+                b.record()
+            torch.cuda.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in evq) / len(evq)
+            nbytes = n_tok * 32 * 128 * 4.5 + 2 * 4 * ((n_tok + 127) // 128) * 32 * 128
+            quant[str(n_tok)] = {"us": round(ms * 1e3, 2), "gbs": round(nbytes / ms / 1e6, 1)}
+            del kv
+    sampler.stop()
+
+    # ---- CPU baseline: the oracle on a bounded sample (rank 0, N == 1) ----
+    bytes_step = shape.algorithmic_bytes()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        per_stream = bytes_step / (shape.batch * h)
+        sample = [(b, hh) for b in range(shape.batch) for hh in range(h)][::4]
+        cpu, outs = cpu_baseline(host, sample, per_stream)
+        cpu["max_abs_gpu_vs_oracle_fp32"] = float(max(np.abs(o_host[b, hh] - o).max()
+                                                      for (b, hh), o in outs.items()))
+
+    peak, peak_kind = measured_peak()
+    total_bytes = bytes_step * world
+    value = total_bytes / (mean_step * 1e-3) / 1e9
+    achieved = bytes_step / (mean_kern * 1e-3) / 1e9
+    traffic = profile_traffic()
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": K, "warmup": Wm, "ms_per_step": round(mean_step, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (fp64 logits), int4 keys",
+        "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
+        "config": workload_config(shape, args.config, world),
+        "decode_us": round(mean_step * 1e3, 2),
+        "hbm_frac_of_peak": round(value / world / peak, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "paged_decode_kernel<128,4,2>", "kernel_us": round(mean_kern * 1e3, 2),
+                     "algorithmic_bytes_per_launch": bytes_step,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
+                     "measured" else "fallback 6.65 TB/s"},
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5), "steps": KE,
+                "h2d_bytes_per_step": int(query.numel() * 4 + bt.numel() * 4 + sl.numel() * 4),
+                "d2h_bytes_per_step": int(out.numel() * 4),
+                "path": "ctypes -> int4kv_paged_decode (C ABI); H2D of query/block table/lengths "
+                        "from pinned host, D2H of the output; KV pools resident in HBM"},
+        "gpu_launches": 2 * K,
+        "clocks": sampler.summary(),
+        "parity": {"gate_streams": len(gate_streams), "max_abs_vs_exact": gate_err},
+        "quantizer": quant,
+    }
+    if cpu is not None:
+        result["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
+# reference arm: the reference's CPU implementation (oracle port), host cores
+# --------------------------------------------------------------------------
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    sys.path.insert(0, ROOT)
+    import importlib
+    import oracle
+    W = importlib.import_module(PKG + ".workloads")
+    shape = W.config_shape(args.config)
+    h, d = shape.heads, shape.head_dim
+    rng = np.random.default_rng(7)
+    bt = W.np_block_table(rng, shape.seq_lens, shape.pool_pages)
+    k_pool = np.zeros((shape.pool_pages, h, 16, d // 2), np.uint8)
+    v_pool = np.zeros((shape.pool_pages, h, 16, d), np.float32)
+    sz_pool = np.zeros((shape.pool_pages, h, 2, d), np.float32)
+    gp = shape.group_tokens // 16
+    for b, n in enumerate(shape.seq_lens):
+        keys = W.np_anchor_keys(rng, n, h, d)
+        vals = rng.standard_normal((n, h, d)).astype(np.float32)
+        q, s, z = oracle.quantize_grouped(keys, shape.group_tokens)
+        packed = oracle.pack_int4(q)
+        npg = (n + 15) // 16
+        for p in range(npg):
+            rows = min(16, n - 16 * p)
+            k_pool[bt[b, p], :, :rows] = packed[16 * p:16 * p + rows].transpose(1, 0, 2)
+            v_pool[bt[b, p], :, :rows] = vals[16 * p:16 * p + rows].transpose(1, 0, 2)
+        for g in range(s.shape[0]):
+            sz_pool[bt[b, g * gp], :, 0] = s[g]
+            sz_pool[bt[b, g * gp], :, 1] = z[g]
+    arrays = {"query": rng.standard_normal((shape.batch, h, d)).astype(np.float32),
+              "k_pool": k_pool, "v_pool": v_pool, "sz_pool": sz_pool, "block_table": bt,
+              "seq_lens": np.asarray(shape.seq_lens, np.int32)}
+    from oracle.cpu_pool import OraclePool
+    pool = OraclePool(arrays)
+    streams = [(b, hh) for b in range(shape.batch) for hh in range(h)]
+    per_stream = shape.algorithmic_bytes() / len(streams)
+    sample = pool.procs  # one stream per process per step: a bounded sample of the step
+    try:
+        cursor = 0
+        for _ in range(args.warmup):
+            pool.run(streams[cursor:cursor + sample])
+            cursor = (cursor + sample) % len(streams)
+        wall = 0.0
+        for _ in range(args.steps):
+            chunk = [streams[(cursor + i) % len(streams)] for i in range(sample)]
+            cursor = (cursor + sample) % len(streams)
+            dt, _ = pool.run(chunk)
+            wall += dt
+    finally:
+        pool.close()
+    ms = wall / args.steps * 1e3
+    value = sample * per_stream / (ms * 1e-3) / 1e9
+    cores = pool.procs
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (NumPy)", "data": "synthetic (seeded, same distributions as ours)",
+        "config": workload_config(shape, args.config, 1),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"each step = {sample} of the {len(streams)} (sequence, head) "
+                                   "streams of one config step, oracle online softmax "
+                                   f"(src/flash_decode_ref.py:30-139 restated), {cores} spawn "
+                                   "processes x 1 BLAS thread"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

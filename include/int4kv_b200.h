@@ -1,0 +1,153 @@
+/*
+ * C ABI of the B200 (sm_100a) INT4 KV-cache library: libint4kv_b200.so.
+ *
+ * Conventions (the reference's, csrc/flash_decode_int4.cu:226-286):
+ *   - plain device pointers, int sizes and a cudaStream_t; no torch types;
+ *   - every launcher returns cudaErrorInvalidValue for bad sizes / null or
+ *     misaligned pointers, otherwise the launch's cudaGetLastError();
+ *   - launchers are stateless and re-entrant (safe on concurrent streams) and
+ *     never allocate: scratch space is passed in by the caller.
+ *
+ * Numerical contract: quantizer bins, scales and zero-points are bit-identical
+ * to the reference's NumPy oracle (src/quantize_int4_ref.py:51-75: IEEE float32,
+ * round half to even). The library is built without fast-math.
+ */
+#ifndef INT4KV_B200_H_
+#define INT4KV_B200_H_
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Largest batch the paged decode accepts (its per-CTA prefix table of pages per
+ * sequence lives in shared memory). */
+#define INT4KV_MAX_PAGED_BATCH 4096
+#ifdef __cplusplus
+static constexpr int kMaxPagedBatch = INT4KV_MAX_PAGED_BATCH;
+#endif
+
+/* Status bits a kernel ORs into the optional `status` word when it had to
+ * defend itself against malformed device-resident metadata. */
+#define INT4KV_STATUS_BAD_PAGE 1u      /* block-table entry outside [0, num_pages) */
+#define INT4KV_STATUS_BAD_LENGTH 2u    /* length < 0, beyond its table row, or misaligned start */
+#define INT4KV_STATUS_WAIT_TIMEOUT 4u  /* an async-copy wait hit its time limit */
+
+/* ---------------------------------------------------------------------------
+ * Drop-in replacements for the reference's two C launchers.
+ * ------------------------------------------------------------------------- */
+
+/* Replaces cu_quantize_int4 (reference csrc/flash_decode_int4.cu:228-247).
+ * kv[num_rows, num_channels] float32 row-major; ONE group = all rows; per
+ * channel asymmetric INT4. Outputs one code per byte q_out[num_rows,
+ * num_channels], scale_out/zp_out[num_channels]. Same signature and error
+ * behaviour; rounding is half-to-even (the reference's oracle) rather than the
+ * reference kernel's half-up. */
+cudaError_t cu_quantize_int4(const float* kv, int num_rows, int num_channels, uint8_t* q_out,
+                             float* scale_out, float* zp_out, cudaStream_t stream);
+
+/* Replaces cu_flash_decode_int4 (reference csrc/flash_decode_int4.cu:249-284).
+ * Every query in query[batch, num_heads, head_dim] attends over ONE shared
+ * page stream: k_q[num_blocks, block_size, head_dim] uint8 (one code per byte),
+ * k_scale/k_zp[num_blocks, head_dim], value[num_blocks, block_size, head_dim]
+ * float32, block_lens[num_blocks] valid rows per page (clamped to
+ * [0, block_size] on the device). head_dim in [1, 256]. No softmax scale. */
+cudaError_t cu_flash_decode_int4(const float* query, const uint8_t* k_q, const float* k_scale,
+                                 const float* k_zp, const float* value, const int* block_lens,
+                                 int batch_size, int num_heads, int head_dim, int num_blocks,
+                                 int block_size, float* output, cudaStream_t stream);
+
+/* Same contract as cu_flash_decode_int4, with the page stream split across
+ * CTAs (split-KV) for parallelism: `workspace` of at least
+ * int4kv_dense_decode_workspace_size() bytes, 16-byte aligned. */
+cudaError_t int4kv_dense_decode_workspace_size(int batch_size, int num_heads, int head_dim,
+                                               int num_blocks, int block_size, size_t* bytes);
+cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const float* k_scale,
+                                const float* k_zp, const float* value, const int* block_lens,
+                                int batch_size, int num_heads, int head_dim, int num_blocks,
+                                int block_size, float* output, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Grouped quantizer: per-(group, head, channel) scale and
+ * zero-point, two codes per byte. Replaces the per-block calls of
+ * quantize_int4_ref + pack_int4 the reference makes in its vLLM shim
+ * (src/vllm_integration.py:48-56) and benchmarks
+ * (benchmarks/bench_three_backend.py:120-124).
+ *   kv[num_tokens, num_heads, head_dim] float32 (16-byte aligned, head_dim % 4 == 0)
+ *   packed_out[num_tokens, num_heads, head_dim/2]: channel 2i -> low nibble,
+ *       2i+1 -> high nibble (src/int4_pack.py:27-29)
+ *   scale_out/zp_out[ceil(num_tokens/group_tokens), num_heads, head_dim]
+ * The last group may be partial and then uses only its own rows.
+ * ------------------------------------------------------------------------- */
+cudaError_t int4kv_quantize_grouped(const float* kv, int num_tokens, int num_heads, int head_dim,
+                                    int group_tokens, uint8_t* packed_out, float* scale_out,
+                                    float* zp_out, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Paged cache layout ("prepared cache"), shared by the writer and the decode:
+ *   k_pool  uint8   [num_pages, num_kv_heads, page_tokens, head_dim/2]
+ *   v_pool  float32 [num_pages, num_kv_heads, page_tokens, head_dim]
+ *   sz_pool float32 [num_pages, num_kv_heads, 2, head_dim]   ([scale; zp] of the
+ *           group whose first token lives in that page)
+ *   block_table int32 [batch, max_pages]  logical page -> physical page
+ *   seq_lens    int32 [batch]             tokens per sequence
+ * Replaces the reference's host-side padding of page lists into a dense
+ * layout (src/ops.py:293-308) and its dict-of-pages cache
+ * (src/vllm_integration.py:42-60).
+ * ------------------------------------------------------------------------- */
+
+/* Quantize keys and scatter keys + values of `batch` sequences into the pools.
+ * Rows of sequence b are k/v[tok_offsets[b] : tok_offsets[b+1], H, D];
+ * they are written at absolute positions start_pos[b] + row (start_pos may be
+ * NULL for 0; it must be a multiple of group_tokens). `max_rows_per_seq`
+ * bounds tok_offsets[b+1]-tok_offsets[b]. v may be NULL (keys only).
+ * group_tokens <= 128 and a multiple of page_tokens; head_dim % 4 == 0. */
+cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* tok_offsets,
+                               const int32_t* start_pos, int batch, int max_rows_per_seq,
+                               int num_heads, int head_dim, int group_tokens, int page_tokens,
+                               const int32_t* block_table, int max_pages, int num_pages,
+                               uint8_t* k_pool, float* v_pool, float* sz_pool, uint32_t* status,
+                               cudaStream_t stream);
+
+/* Fused INT4 paged flash-decode (split-KV over page runs + combine).
+ * query/out [batch, num_q_heads, head_dim] float32; head_dim in {64,128,256};
+ * page_tokens == 16; group_tokens a multiple of 16; num_q_heads == num_kv_heads.
+ * Replaces the attention call of the reference's decode path
+ * (src/ops.py:176-253 -> csrc/flash_decode_int4.cu:104-221) for distinct
+ * per-(sequence, head) KV streams. `status` (nullable) collects
+ * INT4KV_STATUS_* bits. */
+cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
+                                               int head_dim, size_t* bytes);
+cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const float* v_pool,
+                                const float* sz_pool, const int32_t* block_table,
+                                const int32_t* seq_lens, int batch, int num_q_heads,
+                                int num_kv_heads, int head_dim, int page_tokens, int group_tokens,
+                                int max_pages, int num_pages, float* out, void* workspace,
+                                size_t workspace_bytes, uint32_t* status, cudaStream_t stream);
+
+/* int4kv_paged_decode plus timing instrumentation: when non-NULL, ev_before
+ * is recorded on `stream` right before the decode kernel and ev_after right
+ * after it (before the combine kernel), so a caller can time the dominant
+ * kernel alone. The work done is identical. */
+cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_pool,
+                                         const float* v_pool, const float* sz_pool,
+                                         const int32_t* block_table, const int32_t* seq_lens,
+                                         int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                         int page_tokens, int group_tokens, int max_pages,
+                                         int num_pages, float* out, void* workspace,
+                                         size_t workspace_bytes, uint32_t* status,
+                                         cudaStream_t stream, cudaEvent_t ev_before,
+                                         cudaEvent_t ev_after);
+
+/* Library identification: returns a static string naming the build. */
+const char* int4kv_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INT4KV_B200_H_ */

@@ -1,0 +1,269 @@
+"""Torch-tensor binding over the C ABI -- the framework's ``_C`` module.
+
+Mirrors the reference's pybind extension (csrc/bindings.cpp:26-132): the same
+two entry points ``quantize_int4(kv)`` and ``flash_decode_int4(query, k_q,
+k_scale, k_zp, value, block_lens)`` with the same argument meaning, the same
+validation order and the same keywords in the ``RuntimeError`` messages
+(``float32``, ``non-empty``, ``2D``, ``k_scale``, ``value``, ``block_lens``,
+``int32``, ``head_dim`` ...). Outputs are allocated from the torch caching
+allocator on the input's device; launches go on torch's current stream.
+
+The paged entry points (``quantize_int4_grouped``, ``cache_write``,
+``paged_decode``) are new: they serve the BASELINE paged-cache configurations.
+
+Nothing here computes on the CPU: a missing library raises.
+"""
+
+import torch
+
+from . import _lib
+
+MAX_HEAD_DIM = 256
+PAGE_TOKENS = 16
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _check_input(t, name):
+    if not isinstance(t, torch.Tensor):
+        raise RuntimeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _same_device(ref, *ts):
+    for t in ts:
+        if t is not None and t.device != ref.device:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+
+
+# --------------------------------------------------------------------------
+# reference entry points
+# --------------------------------------------------------------------------
+
+def quantize_int4(kv):
+    """Per-channel INT4 over all rows of kv[rows, C] -> [q u8 [rows, C], scale [C], zp [C]]."""
+    lib = _lib.load()
+    _check_input(kv, "kv")
+    if kv.dim() != 2:
+        raise RuntimeError("kv must be 2D [num_rows, num_channels]")
+    if kv.dtype != torch.float32:
+        raise RuntimeError("kv must be float32")
+    rows, ch = kv.shape
+    if rows <= 0 or ch <= 0:
+        raise RuntimeError(f"kv must be non-empty, got [{rows}, {ch}]")
+    if rows > 2**31 - 1 or ch > 2**31 - 1:
+        raise RuntimeError("kv dimensions must fit in int32")
+    with torch.cuda.device(kv.device):
+        q = torch.empty((rows, ch), dtype=torch.uint8, device=kv.device)
+        scale = torch.empty((ch,), dtype=torch.float32, device=kv.device)
+        zp = torch.empty((ch,), dtype=torch.float32, device=kv.device)
+        _lib.check(lib.cu_quantize_int4(_p(kv), rows, ch, _p(q), _p(scale), _p(zp), _stream(kv)),
+                   "quantize_int4")
+    return [q, scale, zp]
+
+
+def flash_decode_int4(query, k_q, k_scale, k_zp, value, block_lens):
+    """Shared-stream INT4 decode (reference csrc/bindings.cpp:56-127 contract)."""
+    lib = _lib.load()
+    for t, n in ((query, "query"), (k_q, "k_q"), (k_scale, "k_scale"), (k_zp, "k_zp"),
+                 (value, "value"), (block_lens, "block_lens")):
+        _check_input(t, n)
+    if query.dim() != 3:
+        raise RuntimeError("query must be 3D [batch, heads, head_dim]")
+    if k_q.dim() != 3:
+        raise RuntimeError("k_q must be 3D [num_blocks, block_size, head_dim]")
+    if query.dtype != torch.float32:
+        raise RuntimeError("query must be float32")
+    if k_q.dtype != torch.uint8:
+        raise RuntimeError("k_q must be uint8")
+    if k_scale.dtype != torch.float32:
+        raise RuntimeError("k_scale must be float32")
+    if k_zp.dtype != torch.float32:
+        raise RuntimeError("k_zp must be float32")
+    if value.dtype != torch.float32:
+        raise RuntimeError("value must be float32")
+    if block_lens.dtype != torch.int32:
+        raise RuntimeError("block_lens must be int32")
+    hd = query.shape[2]
+    nb, bs = k_q.shape[0], k_q.shape[1]
+    if query.shape[0] <= 0 or query.shape[1] <= 0:
+        raise RuntimeError("query must have at least one batch entry and one head")
+    if not 1 <= hd <= MAX_HEAD_DIM:
+        raise RuntimeError(f"head_dim must be in [1, {MAX_HEAD_DIM}], got {hd}")
+    if k_q.shape[2] != hd:
+        raise RuntimeError("k_q last dim must equal head_dim")
+    if value.dim() != 3 or tuple(value.shape) != (nb, bs, hd):
+        raise RuntimeError("value must be [num_blocks, block_size, head_dim] matching k_q")
+    if k_scale.dim() != 2 or tuple(k_scale.shape) != (nb, hd):
+        raise RuntimeError("k_scale must be [num_blocks, head_dim]")
+    if k_zp.dim() != 2 or tuple(k_zp.shape) != (nb, hd):
+        raise RuntimeError("k_zp must be [num_blocks, head_dim]")
+    if block_lens.dim() != 1 or block_lens.shape[0] != nb:
+        raise RuntimeError("block_lens must be [num_blocks]")
+    _same_device(query, k_q, k_scale, k_zp, value, block_lens)
+    b, h = query.shape[0], query.shape[1]
+    with torch.cuda.device(query.device):
+        out = torch.empty((b, h, hd), dtype=torch.float32, device=query.device)
+        import ctypes
+        need = ctypes.c_size_t(0)
+        _lib.check(lib.int4kv_dense_decode_workspace_size(b, h, hd, nb, bs, ctypes.byref(need)),
+                   "flash_decode_int4")
+        ws = torch.empty((max(16, need.value),), dtype=torch.uint8, device=query.device)
+        _lib.check(lib.int4kv_dense_decode(_p(query), _p(k_q), _p(k_scale), _p(k_zp), _p(value),
+                                           _p(block_lens), b, h, hd, nb, bs, _p(out), _p(ws),
+                                           ws.numel(), _stream(query)),
+                   "flash_decode_int4")
+    return out
+
+
+# --------------------------------------------------------------------------
+# paged-cache entry points
+# --------------------------------------------------------------------------
+
+def quantize_int4_grouped(kv, group_tokens=128):
+    """kv[N, H, D] f32 -> (packed [N, H, D/2] u8, scale [G, H, D], zp [G, H, D])."""
+    lib = _lib.load()
+    _check_input(kv, "kv")
+    if kv.dim() != 3:
+        raise RuntimeError("kv must be 3D [num_tokens, num_heads, head_dim]")
+    if kv.dtype != torch.float32:
+        raise RuntimeError("kv must be float32")
+    n, h, d = kv.shape
+    if n <= 0 or h <= 0 or d <= 0:
+        raise RuntimeError(f"kv must be non-empty, got {list(kv.shape)}")
+    if d % 4:
+        raise RuntimeError(f"head_dim must be a multiple of 4 for the packed layout, got {d}")
+    if group_tokens <= 0:
+        raise RuntimeError(f"group_tokens must be positive, got {group_tokens}")
+    g = (n + group_tokens - 1) // group_tokens
+    with torch.cuda.device(kv.device):
+        packed = torch.empty((n, h, d // 2), dtype=torch.uint8, device=kv.device)
+        scale = torch.empty((g, h, d), dtype=torch.float32, device=kv.device)
+        zp = torch.empty((g, h, d), dtype=torch.float32, device=kv.device)
+        _lib.check(lib.int4kv_quantize_grouped(_p(kv), n, h, d, group_tokens, _p(packed), _p(scale),
+                                               _p(zp), _stream(kv)),
+                   "quantize_int4_grouped")
+    return packed, scale, zp
+
+
+def _check_pools(k_pool, v_pool, sz_pool):
+    _check_input(k_pool, "k_pool")
+    _check_input(sz_pool, "sz_pool")
+    if k_pool.dtype != torch.uint8 or k_pool.dim() != 4:
+        raise RuntimeError("k_pool must be uint8 [num_pages, kv_heads, page, head_dim/2]")
+    num_pages, hkv, page, half = k_pool.shape
+    d = 2 * half
+    if v_pool is not None:
+        _check_input(v_pool, "v_pool")
+        if v_pool.dtype != torch.float32 or tuple(v_pool.shape) != (num_pages, hkv, page, d):
+            raise RuntimeError("v_pool must be float32 [num_pages, kv_heads, page, head_dim] "
+                               "matching k_pool")
+    if sz_pool.dtype != torch.float32 or tuple(sz_pool.shape) != (num_pages, hkv, 2, d):
+        raise RuntimeError("sz_pool must be float32 [num_pages, kv_heads, 2, head_dim] matching k_pool")
+    return num_pages, hkv, page, d
+
+
+def _check_table(block_table, batch):
+    _check_input(block_table, "block_table")
+    if block_table.dtype != torch.int32:
+        raise RuntimeError("block_table must be int32")
+    if block_table.dim() != 2 or block_table.shape[0] != batch or block_table.shape[1] <= 0:
+        raise RuntimeError(f"block_table must be [batch={batch}, max_pages>0]")
+    return block_table.shape[1]
+
+
+def cache_write(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, max_rows_per_seq,
+                start_pos=None, group_tokens=128, status=None):
+    """Quantize k and scatter k/v rows of each sequence into the paged pools."""
+    lib = _lib.load()
+    num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
+    _check_input(k, "k")
+    if k.dtype != torch.float32 or k.dim() != 3 or tuple(k.shape[1:]) != (hkv, d):
+        raise RuntimeError(f"k must be float32 [tokens, {hkv}, {d}]")
+    if v is not None:
+        _check_input(v, "v")
+        if v.dtype != torch.float32 or v.shape != k.shape:
+            raise RuntimeError("v must be float32 with the shape of k")
+    _check_input(tok_offsets, "tok_offsets")
+    if tok_offsets.dtype != torch.int32 or tok_offsets.dim() != 1:
+        raise RuntimeError("tok_offsets must be int32 [batch+1]")
+    batch = tok_offsets.shape[0] - 1
+    if batch <= 0:
+        raise RuntimeError("tok_offsets must describe at least one sequence")
+    max_pages = _check_table(block_table, batch)
+    if start_pos is not None:
+        _check_input(start_pos, "start_pos")
+        if start_pos.dtype != torch.int32 or tuple(start_pos.shape) != (batch,):
+            raise RuntimeError("start_pos must be int32 [batch]")
+    if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
+        raise RuntimeError("status must be an int32 tensor")
+    _same_device(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, start_pos, status)
+    with torch.cuda.device(k.device):
+        _lib.check(lib.int4kv_cache_write(_p(k), _p(v), _p(tok_offsets), _p(start_pos), batch,
+                                          int(max_rows_per_seq), hkv, d, group_tokens, page,
+                                          _p(block_table), max_pages, num_pages, _p(k_pool),
+                                          _p(v_pool), _p(sz_pool), _p(status), _stream(k)),
+                   "cache_write")
+
+
+def paged_decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, device=None):
+    import ctypes
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        _lib.check(lib.int4kv_paged_decode_workspace_size(batch, q_heads, kv_heads, head_dim,
+                                                          ctypes.byref(need)),
+                   "paged_decode_workspace_size")
+    return need.value
+
+
+def paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, group_tokens=128,
+                 out=None, workspace=None, status=None):
+    """INT4 paged flash-decode: query[B, H, D] over per-(sequence, head) page streams."""
+    lib = _lib.load()
+    num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
+    if v_pool is None:
+        raise RuntimeError("v_pool is required")
+    _check_input(query, "query")
+    if query.dtype != torch.float32 or query.dim() != 3:
+        raise RuntimeError("query must be float32 [batch, heads, head_dim]")
+    b, hq, qd = query.shape
+    if qd != d:
+        raise RuntimeError(f"query head_dim {qd} != pool head_dim {d}")
+    if d not in (64, 128, 256):
+        raise RuntimeError(f"paged decode supports head_dim in (64, 128, 256), got {d}")
+    if page != PAGE_TOKENS:
+        raise RuntimeError(f"paged decode needs {PAGE_TOKENS}-token pages, got {page}")
+    if hq != hkv:
+        raise RuntimeError(f"query heads ({hq}) must equal kv heads ({hkv})")
+    max_pages = _check_table(block_table, b)
+    _check_input(seq_lens, "seq_lens")
+    if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,):
+        raise RuntimeError("seq_lens must be int32 [batch]")
+    _same_device(query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, workspace, status)
+    with torch.cuda.device(query.device):
+        if out is None:
+            out = torch.empty((b, hq, d), dtype=torch.float32, device=query.device)
+        elif out.dtype != torch.float32 or tuple(out.shape) != (b, hq, d) or not out.is_contiguous():
+            raise RuntimeError("out must be contiguous float32 [batch, heads, head_dim]")
+        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device)
+        if workspace is None:
+            workspace = torch.empty((need,), dtype=torch.uint8, device=query.device)
+        elif workspace.numel() * workspace.element_size() < need:
+            raise RuntimeError(f"workspace needs {need} bytes")
+        _lib.check(lib.int4kv_paged_decode(_p(query), _p(k_pool), _p(v_pool), _p(sz_pool),
+                                           _p(block_table), _p(seq_lens), b, hq, hkv, d, page,
+                                           group_tokens, max_pages, num_pages, _p(out),
+                                           _p(workspace), workspace.numel() * workspace.element_size(),
+                                           _p(status), _stream(query)),
+                   "paged_decode")
+    return out

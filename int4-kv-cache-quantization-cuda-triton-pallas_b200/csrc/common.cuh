@@ -1,0 +1,118 @@
+// Shared device helpers for the sm_100a INT4 KV kernels.
+//
+// Everything here is hand-written inline PTX for the Blackwell async-copy path
+// (mbarrier + cp.async.bulk, i.e. the bulk/TMA engine without a tensor map)
+// plus the exact-rounding float helpers the quantizer's bit-exact contract
+// needs. The library is built WITHOUT --use_fast_math: every division below
+// is IEEE round-to-nearest, as the reference's NumPy oracle computes it.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define I4KV_DEVINL __device__ __forceinline__
+
+namespace i4kv {
+
+// Status bits written into a caller-visible status word when a kernel had to
+// defend itself against malformed device-resident metadata.
+enum StatusBits : uint32_t {
+  kStatusBadPage = 1u << 0,     // block-table entry outside [0, num_pages)
+  kStatusBadLength = 1u << 1,   // sequence length < 0 or beyond its block-table row
+  kStatusWaitTimeout = 1u << 2, // an mbarrier wait hit its iteration limit
+};
+
+I4KV_DEVINL uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+I4KV_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+I4KV_DEVINL void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+I4KV_DEVINL void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+I4KV_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+I4KV_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+I4KV_DEVINL uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: polls the barrier until the phase completes or `limit_ns` of
+// wall time has passed, and then reports false. Callers record
+// kStatusWaitTimeout and stop issuing work instead of spinning forever.
+I4KV_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// Requirements (checked by callers): both addresses 16-byte aligned, size a
+// multiple of 16. No multicast: the source is always this GPU's own memory.
+I4KV_DEVINL void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Float32 value of a 4-bit code held in byte `sel` (0..3) of `w`, built without
+// an integer->float conversion: the byte is placed in the low mantissa bits of
+// 2^23, so the returned float is exactly 2^23 + code.
+I4KV_DEVINL float magic_from_byte(uint32_t w, uint32_t sel) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | sel));
+}
+
+I4KV_DEVINL uint32_t ordered_key(float f) {  // monotone float -> uint32 map
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// The reference's per-channel parameters (src/quantize_int4_ref.py:65-70):
+// range = max(max - min, 1e-8); scale = range / 15; zp = -min / scale.
+I4KV_DEVINL void channel_params(float mn, float mx, float* scale, float* zp) {
+  const float range = fmaxf(__fsub_rn(mx, mn), 1e-8f);
+  const float s = __fdiv_rn(range, 15.0f);
+  *scale = s;
+  *zp = __fdiv_rn(-mn, s);
+}
+
+// q = clip(round_half_even((x - min) / scale), 0, 15)  (src/quantize_int4_ref.py:74-75)
+I4KV_DEVINL uint32_t quant_code(float x, float mn, float scale) {
+  const float t = __fdiv_rn(__fsub_rn(x, mn), scale);
+  int q = __float2int_rn(t);
+  q = q < 0 ? 0 : (q > 15 ? 15 : q);
+  return static_cast<uint32_t>(q);
+}
+
+}  // namespace i4kv

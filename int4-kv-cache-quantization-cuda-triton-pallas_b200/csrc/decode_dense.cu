@@ -1,0 +1,290 @@
+// Generic INT4 flash-decode over ONE shared page stream (the reference's
+// cu_flash_decode_int4 contract, csrc/flash_decode_int4.cu:104-284):
+// every query of [batch, heads] attends to the same list of pages, each page
+// [block_size, head_dim] with one code per byte, its own per-channel
+// scale/zp and a valid-row count. Any head_dim in [1, 256], any page size.
+//
+// B200 mapping (CUDA cores):
+//   * A CTA serves a tile of QT queries, so every key/value byte it reads feeds
+//     QT dot products (the shared-stream case is all-queries-one-stream).
+//   * Logits: one thread per key row -- the thread dequantizes its row in
+//     float32 with the oracle's roundings and accumulates QT dot products in
+//     float64; no cross-lane reduction per token.
+//   * Softmax: per-warp online state over 32-row tiles; P.V with lanes over
+//     head_dim (coalesced value rows).
+//   * Split-KV: the page list can be cut into `splits` contiguous ranges, one
+//     CTA each, merged by a combine kernel. The drop-in entry point has no
+//     workspace argument and runs with one split.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "../../include/int4kv_b200.h"
+
+using namespace i4kv;
+
+namespace {
+
+constexpr int kQT = 4;        // queries per CTA
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxD = 256;
+constexpr int kDPL = kMaxD / 32;
+constexpr uint32_t kFull = 0xffffffffu;
+
+struct DenseArgs {
+  const float* q;
+  const uint8_t* kq;
+  const float* ks;
+  const float* kz;
+  const float* v;
+  const int* lens;
+  int nq, D, nb, bs, splits;
+  float* out;       // final output (splits == 1)
+  char* ws;         // partial records (splits > 1)
+};
+
+__host__ __device__ inline size_t dense_rec_bytes(int D) { return 16 + 4 * (size_t)D; }
+
+__global__ void __launch_bounds__(kThreads)
+dense_decode_kernel(DenseArgs a) {
+  __shared__ double s_q[kQT][kMaxD];
+  __shared__ float s_sc[kMaxD];
+  __shared__ float s_zs[kMaxD];
+  __shared__ double s_m[kWarps][kQT];
+  __shared__ float s_l[kWarps][kQT];
+  __shared__ float s_acc[kWarps][kQT][kMaxD];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q0 = blockIdx.x * kQT;
+  const int nqt = min(kQT, a.nq - q0);
+  const int D = a.D;
+  const int split = blockIdx.y;
+  const int pb = (int)((long long)split * a.nb / a.splits);
+  const int pe = (int)((long long)(split + 1) * a.nb / a.splits);
+
+  for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
+    const int qi = i / D, d = i - qi * D;
+    s_q[qi][d] = qi < nqt ? (double)a.q[(size_t)(q0 + qi) * D + d] : 0.0;
+  }
+
+  double m_w[kQT];
+  float l_lane[kQT];
+  float acc[kQT][kDPL];
+#pragma unroll
+  for (int qi = 0; qi < kQT; ++qi) {
+    m_w[qi] = -INFINITY;
+    l_lane[qi] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kDPL; ++k) acc[qi][k] = 0.f;
+  }
+
+  for (int pg = pb; pg < pe; ++pg) {
+    __syncthreads();  // previous page's scale/zp no longer in use
+    for (int d = threadIdx.x; d < D; d += kThreads) {
+      const float s = a.ks[(size_t)pg * D + d];
+      s_sc[d] = s;
+      s_zs[d] = __fmul_rn(a.kz[(size_t)pg * D + d], s);
+    }
+    __syncthreads();
+    const int blen = min(max(a.lens[pg], 0), a.bs);  // defence in depth, as the reference
+    const uint8_t* kpage = a.kq + (size_t)pg * a.bs * D;
+    const float* vpage = a.v + (size_t)pg * a.bs * D;
+    for (int r0 = warp * 32; r0 < blen; r0 += kThreads) {
+      const int r = r0 + lane;
+      const bool valid = r < blen;
+      double lg[kQT];
+#pragma unroll
+      for (int qi = 0; qi < kQT; ++qi) lg[qi] = 0.0;
+      if (valid) {
+        const uint8_t* krow = kpage + (size_t)r * D;
+        for (int d = 0; d < D; ++d) {
+          const float t = __fmul_rn((float)krow[d], s_sc[d]);
+          const double k = (double)__fsub_rn(t, s_zs[d]);
+#pragma unroll
+          for (int qi = 0; qi < kQT; ++qi) lg[qi] = fma(k, s_q[qi][d], lg[qi]);
+        }
+      }
+      const int nrow = min(32, blen - r0);
+#pragma unroll
+      for (int qi = 0; qi < kQT; ++qi) {
+        double l = valid ? lg[qi] : -INFINITY;
+        double mx = l;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(kFull, mx, o));
+        const double m_new = fmax(m_w[qi], mx);
+        const float corr = expf((float)(m_w[qi] - m_new));
+        const float p = expf((float)(l - m_new));
+        l_lane[qi] = l_lane[qi] * corr + p;
+        m_w[qi] = m_new;
+#pragma unroll
+        for (int k = 0; k < kDPL; ++k) acc[qi][k] *= corr;
+        lg[qi] = p;  // reuse as this lane's probability
+      }
+      for (int j = 0; j < nrow; ++j) {
+        const float* vrow = vpage + (size_t)(r0 + j) * D;
+        float pj[kQT];
+#pragma unroll
+        for (int qi = 0; qi < kQT; ++qi) pj[qi] = __shfl_sync(kFull, (float)lg[qi], j);
+#pragma unroll
+        for (int k = 0; k < kDPL; ++k) {
+          const int d = lane + 32 * k;
+          if (d < D) {
+            const float vv = vrow[d];
+#pragma unroll
+            for (int qi = 0; qi < kQT; ++qi) acc[qi][k] = fmaf(pj[qi], vv, acc[qi][k]);
+          }
+        }
+      }
+    }
+  }
+
+  // merge the warps' states
+#pragma unroll
+  for (int qi = 0; qi < kQT; ++qi) {
+    float l = l_lane[qi];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
+    if (lane == 0) {
+      s_m[warp][qi] = m_w[qi];
+      s_l[warp][qi] = l;
+    }
+#pragma unroll
+    for (int k = 0; k < kDPL; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) s_acc[warp][qi][d] = acc[qi][k];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nqt * D; i += kThreads) {
+    const int qi = i / D, d = i - qi * D;
+    double M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmax(M, s_m[w][qi]);
+    float L = 0.f, o = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (s_m[w][qi] == -INFINITY) continue;
+        const float e = expf((float)(s_m[w][qi] - M));
+        L = fmaf(s_l[w][qi], e, L);
+        o = fmaf(s_acc[w][qi][d], e, o);
+      }
+    }
+    if (a.splits == 1) {
+      a.out[(size_t)(q0 + qi) * D + d] = __fdiv_rn(o, fmaxf(L, 1e-10f));
+    } else {
+      char* rec = a.ws + ((size_t)(q0 + qi) * a.splits + split) * dense_rec_bytes(D);
+      if (d == 0) {
+        *reinterpret_cast<double*>(rec) = M;
+        *reinterpret_cast<float*>(rec + 8) = L;
+      }
+      reinterpret_cast<float*>(rec + 16)[d] = o;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128)
+dense_combine_kernel(const char* __restrict__ ws, int nq, int D, int splits, float* __restrict__ out) {
+  const int qi = blockIdx.x;
+  if (qi >= nq) return;
+  const size_t rb = dense_rec_bytes(D);
+  const char* base = ws + (size_t)qi * splits * rb;
+  double M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmax(M, *reinterpret_cast<const double*>(base + s * rb));
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = 0.f, o = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < splits; ++s) {
+        const char* rec = base + s * rb;
+        const double m = *reinterpret_cast<const double*>(rec);
+        if (m == -INFINITY) continue;
+        const float e = expf((float)(m - M));
+        L = fmaf(*reinterpret_cast<const float*>(rec + 8), e, L);
+        o = fmaf(reinterpret_cast<const float*>(rec + 16)[d], e, o);
+      }
+    }
+    out[(size_t)qi * D + d] = __fdiv_rn(o, fmaxf(L, 1e-10f));
+  }
+}
+
+int choose_splits(int nq, int nb) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = (nq + kQT - 1) / kQT;
+  int splits = (2 * sms + tiles - 1) / tiles;
+  if (splits > nb) splits = nb;
+  if (splits > 64) splits = 64;
+  return splits < 1 ? 1 : splits;
+}
+
+cudaError_t check(const float* query, const uint8_t* k_q, const float* k_scale, const float* k_zp,
+                  const float* value, const int* block_lens, int batch_size, int num_heads,
+                  int head_dim, int num_blocks, int block_size, const float* output) {
+  if (head_dim <= 0 || head_dim > kMaxD) return cudaErrorInvalidValue;
+  if (batch_size <= 0 || num_heads <= 0 || num_blocks < 0 || block_size < 0) return cudaErrorInvalidValue;
+  if ((long long)batch_size * num_heads >= (1LL << 31) / kMaxD) return cudaErrorInvalidValue;
+  if (!query || !output) return cudaErrorInvalidValue;
+  if (num_blocks > 0 && (!k_q || !k_scale || !k_zp || !value || !block_lens)) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t cu_flash_decode_int4(const float* query, const uint8_t* k_q, const float* k_scale,
+                                 const float* k_zp, const float* value, const int* block_lens,
+                                 int batch_size, int num_heads, int head_dim, int num_blocks,
+                                 int block_size, float* output, cudaStream_t stream) {
+  cudaError_t e = check(query, k_q, k_scale, k_zp, value, block_lens, batch_size, num_heads,
+                        head_dim, num_blocks, block_size, output);
+  if (e != cudaSuccess) return e;
+  const int nq = batch_size * num_heads;
+  DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
+              1, output, nullptr};
+  dense_decode_kernel<<<dim3((nq + kQT - 1) / kQT, 1), kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t int4kv_dense_decode_workspace_size(int batch_size, int num_heads, int head_dim,
+                                               int num_blocks, int block_size, size_t* bytes) {
+  if (!bytes || head_dim <= 0 || head_dim > kMaxD || batch_size <= 0 || num_heads <= 0 ||
+      num_blocks < 0 || block_size < 0)
+    return cudaErrorInvalidValue;
+  const int nq = batch_size * num_heads;
+  const int splits = choose_splits(nq, num_blocks);
+  *bytes = splits > 1 ? (size_t)nq * splits * dense_rec_bytes(head_dim) : 16;
+  return cudaSuccess;
+}
+
+cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const float* k_scale,
+                                const float* k_zp, const float* value, const int* block_lens,
+                                int batch_size, int num_heads, int head_dim, int num_blocks,
+                                int block_size, float* output, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+  cudaError_t e = check(query, k_q, k_scale, k_zp, value, block_lens, batch_size, num_heads,
+                        head_dim, num_blocks, block_size, output);
+  if (e != cudaSuccess) return e;
+  const int nq = batch_size * num_heads;
+  const int splits = choose_splits(nq, num_blocks);
+  if (splits > 1) {
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
+        workspace_bytes < (size_t)nq * splits * dense_rec_bytes(head_dim))
+      return cudaErrorInvalidValue;
+  }
+  DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
+              splits, output, static_cast<char*>(workspace)};
+  dense_decode_kernel<<<dim3((nq + kQT - 1) / kQT, splits), kThreads, 0, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || splits == 1) return e;
+  dense_combine_kernel<<<nq, 128, 0, stream>>>(static_cast<const char*>(workspace), nq, head_dim,
+                                               splits, output);
+  return cudaGetLastError();
+}
+
+const char* int4kv_build_info(void) {
+  return "libint4kv_b200: sm_100a, IEEE float32 (no fast-math), built " __DATE__ " " __TIME__;
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+"""Device-resident paged INT4 KV cache (the "prepared cache").
+
+Replaces two host-side structures of the reference: the dense padding of page
+lists done on every call (src/ops.py:293-308) and the dict-of-pages cache of
+the vLLM shim (src/vllm_integration.py:42-60). Everything lives in HBM:
+
+  k_pool  uint8   [num_pages, kv_heads, 16, head_dim/2]  nibble-packed keys
+  v_pool  float32 [num_pages, kv_heads, 16, head_dim]    values
+  sz_pool float32 [num_pages, kv_heads, 2, head_dim]     [scale; zp] of the
+          128-token group whose first token lives in this page
+
+Each (page, head) slab of K (1 KiB at d128) and V (8 KiB) is contiguous, so
+the decode kernel moves it with one bulk async copy. A sequence owns a list
+of physical pages (its block-table row); the group of token ``t`` takes its
+scale/zp from page ``row[(t // 128) * 8]``.
+"""
+
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _C
+
+PAGE_TOKENS = 16
+
+
+class PagedKVCache:
+    def __init__(self, num_pages: int, num_kv_heads: int, head_dim: int,
+                 group_tokens: int = 128, device="cuda", seed: Optional[int] = None,
+                 values: bool = True):
+        if head_dim % 4:
+            raise ValueError(f"head_dim must be a multiple of 4, got {head_dim}")
+        if group_tokens % PAGE_TOKENS or group_tokens <= 0 or group_tokens > 128:
+            raise ValueError("group_tokens must be a multiple of 16 in [16, 128]")
+        self.num_pages = num_pages
+        self.heads = num_kv_heads
+        self.head_dim = head_dim
+        self.group_tokens = group_tokens
+        self.device = torch.device(device)
+        self.k_pool = torch.zeros((num_pages, num_kv_heads, PAGE_TOKENS, head_dim // 2),
+                                  dtype=torch.uint8, device=self.device)
+        self.v_pool = (torch.zeros((num_pages, num_kv_heads, PAGE_TOKENS, head_dim),
+                                   dtype=torch.float32, device=self.device) if values else None)
+        self.sz_pool = torch.zeros((num_pages, num_kv_heads, 2, head_dim), dtype=torch.float32,
+                                   device=self.device)
+        order = (np.random.default_rng(seed).permutation(num_pages) if seed is not None
+                 else np.arange(num_pages))
+        self._free: List[int] = [int(p) for p in order[::-1]]
+        self.pages: Dict[int, List[int]] = {}
+        self.lens: Dict[int, int] = {}
+
+    # ---- page allocation ----
+    def _alloc(self, n: int) -> List[int]:
+        if n > len(self._free):
+            raise MemoryError(f"paged KV cache out of pages: need {n}, {len(self._free)} free")
+        return [self._free.pop() for _ in range(n)]
+
+    def free_sequence(self, seq_id: int) -> None:
+        for p in self.pages.pop(seq_id, []):
+            self._free.append(p)
+        self.lens.pop(seq_id, None)
+
+    # ---- writes ----
+    def write_sequences(self, seq_ids: Sequence[int], keys: Sequence[torch.Tensor],
+                        values: Optional[Sequence[torch.Tensor]] = None) -> None:
+        """Quantize and store whole sequences ([len, heads, head_dim] float32 each).
+
+        One kernel launch quantizes every 128-token group of every sequence and
+        scatters keys and values into freshly allocated pages.
+        """
+        if len(seq_ids) != len(keys):
+            raise ValueError("one key tensor per sequence")
+        lens = [int(k.shape[0]) for k in keys]
+        for s, n in zip(seq_ids, lens):
+            if s in self.pages:
+                self.free_sequence(s)
+            self.pages[s] = self._alloc((n + PAGE_TOKENS - 1) // PAGE_TOKENS)
+            self.lens[s] = n
+        if sum(lens) == 0:
+            return
+        k = torch.cat([t.to(self.device, torch.float32) for t in keys]).contiguous()
+        v = None
+        if values is not None and self.v_pool is not None:
+            v = torch.cat([t.to(self.device, torch.float32) for t in values]).contiguous()
+        offs = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32,
+                            device=self.device)
+        bt, _ = self.block_table(seq_ids)
+        _C.cache_write(k, v, offs, bt, self.k_pool, self.v_pool, self.sz_pool,
+                       max_rows_per_seq=max(lens), group_tokens=self.group_tokens)
+
+    # ---- reads ----
+    def block_table(self, seq_ids: Sequence[int]):
+        """(block_table int32 [B, max_pages], seq_lens int32 [B]) on the cache's device."""
+        maxp = max(1, max(len(self.pages[s]) for s in seq_ids))
+        bt = np.zeros((len(seq_ids), maxp), np.int32)
+        for i, s in enumerate(seq_ids):
+            bt[i, :len(self.pages[s])] = self.pages[s]
+        lens = np.array([self.lens[s] for s in seq_ids], np.int32)
+        return (torch.from_numpy(bt).to(self.device), torch.from_numpy(lens).to(self.device))
+
+    def decode(self, query: torch.Tensor, seq_ids: Sequence[int]) -> torch.Tensor:
+        """query [B, heads, head_dim] -> attention output [B, heads, head_dim] (device)."""
+        bt, sl = self.block_table(seq_ids)
+        return _C.paged_decode(query.to(self.device, torch.float32).contiguous(), self.k_pool,
+                               self.v_pool, self.sz_pool, bt, sl, self.group_tokens)
+
+    def memory_stats(self) -> dict:
+        used = sum(len(p) for p in self.pages.values())
+        per_page = (self.k_pool[0].numel() + self.sz_pool[0].numel() * 4
+                    + (self.v_pool[0].numel() * 4 if self.v_pool is not None else 0))
+        return {"pages_used": used, "pages_total": self.num_pages,
+                "bytes_used": used * per_page, "tokens": sum(self.lens.values())}

@@ -1,0 +1,82 @@
+"""The C-ABI library builds, loads and exports every symbol include/*.h declares.
+
+No compute runs here (no GPU needed): only the launchers' host-side argument
+checks, which must refuse bad sizes with cudaErrorInvalidValue before any
+CUDA call.
+"""
+
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from helpers import pkg
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CUDA_ERROR_INVALID_VALUE = 1
+
+
+def header_functions():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?\w+\s*\*?\s+(\w+)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build = pkg("_build")
+    build.build()
+    return pkg("_lib").load()
+
+
+def test_header_declares_the_reference_launchers():
+    names = header_functions()
+    assert {"cu_quantize_int4", "cu_flash_decode_int4"} <= names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = header_functions()
+    assert names, "no declarations parsed"
+    for n in sorted(names):
+        assert hasattr(lib, n), f"{n} declared in include/ but not exported"
+    assert set(pkg("_lib").EXPORTED) == names
+
+
+def test_build_info(lib):
+    assert "sm_100a" in pkg("_lib").build_info()
+
+
+def test_reference_launchers_reject_bad_sizes(lib):
+    n = None
+    assert lib.cu_quantize_int4(n, 0, 4, n, n, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.cu_quantize_int4(n, 4, -1, n, n, n, n) == CUDA_ERROR_INVALID_VALUE
+    # head_dim beyond the kernel limit and non-positive sizes (reference :267-269)
+    assert lib.cu_flash_decode_int4(n, n, n, n, n, n, 1, 1, 257, 1, 1, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.cu_flash_decode_int4(n, n, n, n, n, n, 1, 1, 0, 1, 1, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.cu_flash_decode_int4(n, n, n, n, n, n, 0, 1, 64, 1, 1, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.cu_flash_decode_int4(n, n, n, n, n, n, 1, 1, 64, -1, 1, n, n) == CUDA_ERROR_INVALID_VALUE
+
+
+def test_paged_launchers_reject_bad_sizes(lib):
+    n = None
+    # head_dim not a multiple of 4
+    assert lib.int4kv_quantize_grouped(n, 8, 2, 6, 128, n, n, n, n) == CUDA_ERROR_INVALID_VALUE
+    # group longer than 128 rows is not a paged-write group
+    assert lib.int4kv_cache_write(n, n, n, n, 1, 16, 2, 64, 256, 16, n, 4, 4, n, n, n, n, n) \
+        == CUDA_ERROR_INVALID_VALUE
+    # page size other than 16, GQA ratio other than 1
+    assert lib.int4kv_paged_decode(n, n, n, n, n, n, 1, 2, 2, 128, 32, 128, 4, 4, n, n, 0, n, n) \
+        == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_paged_decode(n, n, n, n, n, n, 1, 4, 2, 128, 16, 128, 4, 4, n, n, 0, n, n) \
+        == CUDA_ERROR_INVALID_VALUE
+    size = ctypes.c_size_t(0)
+    assert lib.int4kv_paged_decode_workspace_size(1, 2, 2, 96, ctypes.byref(size)) \
+        == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_dense_decode_workspace_size(1, 1, 300, 1, 1, ctypes.byref(size)) \
+        == CUDA_ERROR_INVALID_VALUE
