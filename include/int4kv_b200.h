@@ -113,7 +113,10 @@ cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* to
                                uint8_t* k_pool, float* v_pool, float* sz_pool, uint32_t* status,
                                cudaStream_t stream);
 
-/* Fused INT4 paged flash-decode (split-KV over page runs + combine).
+/* Fused INT4 paged flash-decode (split-KV over page runs, combine fused in
+ * the same kernel). The workspace must be zero-filled before its first use;
+ * every launch that completes leaves it zero-filled again (a launch that set
+ * INT4KV_STATUS_WAIT_TIMEOUT does not: zero it again before reuse).
  * query/out [batch, num_q_heads, head_dim] float32; head_dim in {64,128,256};
  * page_tokens == 16; group_tokens a multiple of 16; num_q_heads == num_kv_heads.
  * Replaces the attention call of the reference's decode path

@@ -257,7 +257,8 @@ def paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, group_to
             raise RuntimeError("out must be contiguous float32 [batch, heads, head_dim]")
         need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device)
         if workspace is None:
-            workspace = torch.empty((need,), dtype=torch.uint8, device=query.device)
+            # zero-filled once; every completed launch leaves it zero-filled again
+            workspace = torch.zeros((need,), dtype=torch.uint8, device=query.device)
         elif workspace.numel() * workspace.element_size() < need:
             raise RuntimeError(f"workspace needs {need} bytes")
         _lib.check(lib.int4kv_paged_decode(_p(query), _p(k_pool), _p(v_pool), _p(sz_pool),

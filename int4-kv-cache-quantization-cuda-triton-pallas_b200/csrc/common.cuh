@@ -63,14 +63,28 @@ I4KV_DEVINL uint64_t global_ns() {
   return t;
 }
 
-// Bounded wait: polls the barrier until the phase completes or `limit_ns` of
-// wall time has passed, and then reports false. Callers record
-// kStatusWaitTimeout and stop issuing work instead of spinning forever.
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (woken promptly) or `hint_ns` elapses, instead of spinning.
+I4KV_DEVINL bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: sleeps on the barrier until the phase completes or `limit_ns`
+// of wall time has passed, and then reports false. Callers record
+// kStatusWaitTimeout and stop issuing work instead of waiting forever.
 I4KV_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
     if (global_ns() - t0 > limit_ns) return false;
   }
 }

@@ -7,9 +7,9 @@
 // B200 mapping (CUDA cores):
 //   * A CTA serves a tile of QT queries, so every key/value byte it reads feeds
 //     QT dot products (the shared-stream case is all-queries-one-stream).
-//   * Logits: one thread per key row -- the thread dequantizes its row in
-//     float32 with the oracle's roundings and accumulates QT dot products in
-//     float64; no cross-lane reduction per token.
+//   * Logits: one thread per key row, QT dot products in float64 as
+//     sum_d (q_d*s_d)*c_d - sum_d q_d*zp_d*s_d (exact dequantization, the
+//     reference's float64 arbiter); no cross-lane reduction per token.
 //   * Softmax: per-warp online state over 32-row tiles; P.V with lanes over
 //     head_dim (coalesced value rows).
 //   * Split-KV: the page list can be cut into `splits` contiguous ranges, one
@@ -44,13 +44,15 @@ struct DenseArgs {
   char* ws;         // partial records (splits > 1)
 };
 
-__host__ __device__ inline size_t dense_rec_bytes(int D) { return 16 + 4 * (size_t)D; }
+// Partial record: [m f64][l f32][pad][acc D f32], padded to a multiple of 16
+// bytes so every record (and its double) stays aligned for any head_dim.
+__host__ __device__ inline size_t dense_rec_bytes(int D) { return 16 + 16 * (((size_t)D + 3) / 4); }
 
 __global__ void __launch_bounds__(kThreads)
 dense_decode_kernel(DenseArgs a) {
-  __shared__ double s_q[kQT][kMaxD];
-  __shared__ float s_sc[kMaxD];
-  __shared__ float s_zs[kMaxD];
+  __shared__ float s_q[kQT][kMaxD];
+  __shared__ double s_qs[kQT][kMaxD];   // q_d * s_d of the current page (exact)
+  __shared__ double s_bias[kQT];        // sum_d q_d * zp_d * s_d of the current page
   __shared__ double s_m[kWarps][kQT];
   __shared__ float s_l[kWarps][kQT];
   __shared__ float s_acc[kWarps][kQT][kMaxD];
@@ -65,7 +67,7 @@ dense_decode_kernel(DenseArgs a) {
 
   for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
     const int qi = i / D, d = i - qi * D;
-    s_q[qi][d] = qi < nqt ? (double)a.q[(size_t)(q0 + qi) * D + d] : 0.0;
+    s_q[qi][d] = qi < nqt ? a.q[(size_t)(q0 + qi) * D + d] : 0.f;
   }
 
   double m_w[kQT];
@@ -80,11 +82,19 @@ dense_decode_kernel(DenseArgs a) {
   }
 
   for (int pg = pb; pg < pe; ++pg) {
-    __syncthreads();  // previous page's scale/zp no longer in use
-    for (int d = threadIdx.x; d < D; d += kThreads) {
-      const float s = a.ks[(size_t)pg * D + d];
-      s_sc[d] = s;
-      s_zs[d] = __fmul_rn(a.kz[(size_t)pg * D + d], s);
+    __syncthreads();  // previous page's folded constants no longer in use
+    for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
+      const int qi = i / D, d = i - qi * D;
+      s_qs[qi][d] = (double)s_q[qi][d] * (double)a.ks[(size_t)pg * D + d];
+    }
+    if (warp < kQT) {  // warp qi reduces sum_d q_d * zp_d * s_d for query qi
+      double b = 0.0;
+      for (int d = lane; d < D; d += 32)
+        b = fma((double)s_q[warp][d],
+                (double)a.kz[(size_t)pg * D + d] * (double)a.ks[(size_t)pg * D + d], b);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) b += __shfl_xor_sync(kFull, b, o);
+      if (lane == 0) s_bias[warp] = b;
     }
     __syncthreads();
     const int blen = min(max(a.lens[pg], 0), a.bs);  // defence in depth, as the reference
@@ -99,11 +109,12 @@ dense_decode_kernel(DenseArgs a) {
       if (valid) {
         const uint8_t* krow = kpage + (size_t)r * D;
         for (int d = 0; d < D; ++d) {
-          const float t = __fmul_rn((float)krow[d], s_sc[d]);
-          const double k = (double)__fsub_rn(t, s_zs[d]);
+          const double code = (double)krow[d];
 #pragma unroll
-          for (int qi = 0; qi < kQT; ++qi) lg[qi] = fma(k, s_q[qi][d], lg[qi]);
+          for (int qi = 0; qi < kQT; ++qi) lg[qi] = fma(s_qs[qi][d], code, lg[qi]);
         }
+#pragma unroll
+        for (int qi = 0; qi < kQT; ++qi) lg[qi] -= s_bias[qi];
       }
       const int nrow = min(32, blen - r0);
 #pragma unroll

@@ -3,28 +3,34 @@
 //
 // Semantics: the reference's online softmax (src/flash_decode_ref.py:30-139),
 // run once per (sequence b, kv head h) stream: raw logits q.k (no 1/sqrt(d)),
-// keys dequantized as fl(fl(code*scale) - fl(zp*scale)) with the scale/zp of
-// the key's 128-token group, output o / max(l, 1e-10).
+// keys dequantized as code*scale - zp*scale with the scale/zp of the key's
+// 128-token group, output o / max(l, 1e-10); empty streams give exact zeros.
 //
 // Work decomposition (stream-K over pages): the page-heads of all streams are
 // laid end to end in (b, h, page) order -- T of them -- and the grid's NW warps
 // each take one contiguous run of ~T/NW pages, so every warp moves the same
 // number of bytes whatever the length distribution. A warp keeps its own
-// online-softmax state and writes one (m, l, acc[D]) partial per stream
-// segment it touched; a small combine kernel merges the partials of a stream.
+// online-softmax state per stream segment. A stream covered by one warp is
+// finished by that warp; otherwise each contributing warp writes an
+// (m, l, acc[D]) partial, bumps the stream's counter, and the warp that
+// arrives last merges the partials and writes the output (counters reset to
+// zero on the way out, so the workspace stays zero-filled between launches).
 //
 // Data movement: each warp owns a ring of STAGES shared-memory slots and lane 0
 // streams its pages into them with 1-D bulk async copies (cp.async.bulk, the
-// TMA engine without a tensor map) completing on per-slot mbarriers: the 16
-// valid-token rows of V (fp32) and of packed K, plus the group's scale/zp and
-// the stream's query when they change. No multicast; the sources are this
-// GPU's own pools.
+// TMA engine without a tensor map) completing on per-slot mbarriers: the valid
+// rows of V (fp32) and of packed K, plus the group's scale/zp and the stream's
+// query when they change. No multicast; the sources are this GPU's own pools.
 //
-// Numerics: keys are dequantized in float32 with exactly the oracle's
-// roundings, then dotted with the query in float64, so logits are exact up to
-// the reference's own key rounding; exponentials and the value accumulation
-// are float32 with per-page rescaling. The result is at least as close to a
-// float64 evaluation as the float32 reference is.
+// Numerics: with qs_d = q_d*s_d and c_d the 4-bit code, the logit is
+//   sum_d qs_d*(16 + c_d) - sum_d (16*qs_d + q_d*zp_d*s_d)
+// evaluated in float64 -- the products q*s and zp*s of float32 operands are
+// exact in float64 and the float64 value 16 + c is assembled from the code's
+// bits with one byte permute (no integer/float conversion on the hot loop).
+// The logits are therefore those of the reference's float64 arbiter
+// (exact dequantization); softmax weights are float32 exponentials, values are
+// summed per page in float32 and across pages in float32 with Kahan
+// compensation; partials are merged in float64.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -43,7 +49,7 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of w
 
 template <int D, int WARPS, int STAGES>
 struct Cfg {
-  static constexpr int LPT = D / 8;          // lanes per token in the logit phase (8 dims each)
+  static constexpr int LPT = D / 16;         // lanes per token in the logit phase (16 dims each)
   static constexpr int TPP = 32 / LPT;       // tokens per pass
   static constexpr int NJ = kPage / TPP;     // passes per page
   static constexpr int DPL = D / 32;         // value dims per lane in the P.V phase
@@ -52,19 +58,22 @@ struct Cfg {
   static constexpr int SZ_OFF = K_OFF + kPage * D / 2;
   static constexpr int Q_OFF = SZ_OFF + 2 * D * 4;
   static constexpr int STAGE_BYTES = Q_OFF + D * 4;
-  static constexpr int WARP_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int REC_BYTES = 16 + 4 * D;
+  static constexpr int P_BYTES = kPage * 4;  // per-warp softmax weights of the current page
+  static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + P_BYTES;
+  static constexpr int REC_BYTES = 16 + 4 * D;  // [m f64][l f64][acc D f32]
   static_assert(LPT * TPP == 32 && NJ * TPP == kPage, "lane mapping");
   static_assert(LPT == 2 * NJ, "reduce-scatter mapping needs LPT == 2*NJ");
-  static_assert(STAGE_BYTES % 16 == 0, "stage alignment");
+  static_assert(STAGE_BYTES % 16 == 0 && WARP_BYTES % 16 == 0, "stage alignment");
 };
 
-// Workspace layout shared by the decode and combine kernels.
-//   [0, 16)              reserved
-//   [16, 16 + pfx)       prefix[B+1]: exclusive prefix of pages-per-head over sequences
-//   [rec_off, ...)       partial records, slot (warp + stream), REC_BYTES each
+// Workspace layout (zero-filled before first use; every completed launch
+// leaves the counters at zero again):
+//   [0, cnt_bytes)            per-stream arrival counters, int32 [batch*heads]
+//   [cnt_bytes, ...)          partial records, slot (warp + stream), REC_BYTES each
+__host__ __device__ inline size_t cnt_bytes(long long streams) {
+  return ((size_t)streams * 4 + 127) / 128 * 128;
+}
 __host__ __device__ inline size_t pfx_bytes(int batch) { return ((size_t)(batch + 1) * 4 + 127) / 128 * 128; }
-__host__ __device__ inline size_t rec_offset(int batch) { return 16 + pfx_bytes(batch) + 112; }
 
 struct DecodeArgs {
   const float* q;
@@ -73,6 +82,7 @@ struct DecodeArgs {
   const float* sz_pool;
   const int32_t* block_table;
   const int32_t* seq_lens;
+  float* out;
   int batch, heads, max_pages, num_pages, group_pages;
   char* ws;
   uint32_t* status;
@@ -81,6 +91,8 @@ struct DecodeArgs {
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
 }
+
+__device__ __forceinline__ int clamp_len(int len, int cap) { return len < 0 ? 0 : (len > cap ? cap : len); }
 
 // Exclusive prefix over sequences of pages-per-head, into s_pfx[0..B]; returns total.
 __device__ int block_page_prefix(const DecodeArgs& a, int* s_pfx, int* s_tmp) {
@@ -91,12 +103,9 @@ __device__ int block_page_prefix(const DecodeArgs& a, int* s_pfx, int* s_tmp) {
   const int cap = a.max_pages * kPage;
   int local = 0;
   for (int b = lo; b < hi; ++b) {
-    int len = a.seq_lens[b];
-    if (len < 0 || len > cap) {
-      set_status(a.status, kStatusBadLength);
-      len = len < 0 ? 0 : cap;
-    }
-    local += (len + kPage - 1) / kPage;
+    const int len = a.seq_lens[b];
+    if ((len < 0 || len > cap) && blockIdx.x == 0) set_status(a.status, kStatusBadLength);
+    local += (clamp_len(len, cap) + kPage - 1) / kPage;
   }
   const int lane = t & 31, warp = t >> 5;
   int incl = local;
@@ -112,9 +121,7 @@ __device__ int block_page_prefix(const DecodeArgs& a, int* s_pfx, int* s_tmp) {
   int run = warp_base + incl - local;
   for (int b = lo; b < hi; ++b) {
     s_pfx[b] = run;
-    int len = a.seq_lens[b];
-    len = len < 0 ? 0 : (len > cap ? cap : len);
-    run += (len + kPage - 1) / kPage;
+    run += (clamp_len(a.seq_lens[b], cap) + kPage - 1) / kPage;
   }
   if (t == nthreads - 1) s_pfx[a.batch] = run;
   __syncthreads();
@@ -125,15 +132,15 @@ __device__ int block_page_prefix(const DecodeArgs& a, int* s_pfx, int* s_tmp) {
 struct Desc {
   int phys;   // physical page (valid when ntok > 0)
   int gphys;  // physical page holding the group's scale/zp (valid when has_sz)
-  int meta;   // ntok | has_q << 8 | has_sz << 9
+  int meta;   // ntok | has_q << 8 | has_sz << 9 | h << 16
   int stream; // b * heads + h
 };
 
-__device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx, long long g,
-                                          long long g0, long long g1) {
+__device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx, int g, int g0,
+                                          int g1) {
   Desc d{0, 0, 0, -1};
   if (g >= g1) return d;
-  const long long gq = g / a.heads;
+  const int gq = g / a.heads;
   int lo = 0, hi = a.batch - 1;  // last b with pfx[b] <= gq
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -141,12 +148,10 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   }
   const int b = lo;
   const int np = s_pfx[b + 1] - s_pfx[b];
-  const long long rem = g - (long long)a.heads * s_pfx[b];
-  const int h = (int)(rem / np);
-  const int p = (int)(rem - (long long)h * np);
-  int len = a.seq_lens[b];
-  const int cap = a.max_pages * kPage;
-  len = len < 0 ? 0 : (len > cap ? cap : len);
+  const int rem = g - a.heads * s_pfx[b];
+  const int h = rem / np;
+  const int p = rem - h * np;
+  const int len = clamp_len(a.seq_lens[b], a.max_pages * kPage);
   const int ntok = min(kPage, len - p * kPage);
   const int32_t* row = a.block_table + (size_t)b * a.max_pages;
   const int phys = row[p];
@@ -158,7 +163,8 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   if (!gok || !pok) set_status(a.status, kStatusBadPage);
   d.phys = phys;
   d.gphys = gphys;
-  d.meta = ((gok && pok) ? ntok : 0) | (first ? (1 << 8) : 0) | ((grp && gok) ? (1 << 9) : 0);
+  d.meta = ((gok && pok) ? ntok : 0) | (first ? (1 << 8) : 0) | ((grp && gok) ? (1 << 9) : 0) |
+           (h << 16);
   d.stream = b * a.heads + h;
   return d;
 }
@@ -178,7 +184,7 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   using C = Cfg<D, WARPS, STAGES>;
   const int ntok = d.meta & 0xff;
   const bool has_q = (d.meta >> 8) & 1, has_sz = (d.meta >> 9) & 1;
-  const int h = d.stream % a.heads;
+  const int h = d.meta >> 16;
   uint32_t bytes = 0;
   if (ntok) bytes += (uint32_t)ntok * (D * 4 + D / 2);
   if (has_sz) bytes += 2 * D * 4;
@@ -196,10 +202,88 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   if (has_q) bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * D, D * 4, bar);
 }
 
+// float64 value 16 + code of the low nibble held in byte `sel` of `w`, where
+// `w` holds (code | 0x30) in each byte: the byte becomes bits 16..23 of the
+// high word 0x40300000 + (code << 16), low word zero.
+__device__ __forceinline__ double code_plus16(uint32_t w, uint32_t sel) {
+  return __hiloint2double((int)__byte_perm(w, 0x40000000u, 0x7044u | (sel << 8)), 0);
+}
+
+// Store o[DPL] (this lane's dims of a D-vector) at dst with the P.V lane layout.
+template <int D>
+__device__ __forceinline__ void store_lane_vec(float* dst, const float* o, int lane) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    *reinterpret_cast<float2*>(dst + 2 * lane) = make_float2(o[0], o[1]);
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4)
+      *reinterpret_cast<float4*>(dst + v4 * 128 + 4 * lane) =
+          make_float4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void load_lane_vec_cg(const float* src, float* o, int lane) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(src + 2 * lane));
+    o[0] = v.x; o[1] = v.y;
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + v4 * 128 + 4 * lane));
+      o[4 * v4] = v.x; o[4 * v4 + 1] = v.y; o[4 * v4 + 2] = v.z; o[4 * v4 + 3] = v.w;
+    }
+  }
+}
+
+// sum = sum*r + x with a running compensation term c (Kahan): the rescale
+// applies to both, the addition captures its own rounding error in c.
+__device__ __forceinline__ void kahan_rescale_add(float& sum, float& c, float r, float x) {
+  sum *= r;
+  c *= r;
+  const float y = __fsub_rn(x, c);
+  const float t = __fadd_rn(sum, y);
+  c = __fsub_rn(__fsub_rn(t, sum), y);
+  sum = t;
+}
+
+// ps += p[t] * V[t, lane's dims] (lane layout of store_lane_vec).
+template <int D>
+__device__ __forceinline__ void pv_row(const float* vs, float pt, int t, int lane, float* ps) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(vs + t * D + 2 * lane);
+    ps[0] = fmaf(pt, v.x, ps[0]);
+    ps[1] = fmaf(pt, v.y, ps[1]);
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4) {
+      const float4 v = *reinterpret_cast<const float4*>(vs + t * D + v4 * 128 + 4 * lane);
+      ps[4 * v4 + 0] = fmaf(pt, v.x, ps[4 * v4 + 0]);
+      ps[4 * v4 + 1] = fmaf(pt, v.y, ps[4 * v4 + 1]);
+      ps[4 * v4 + 2] = fmaf(pt, v.z, ps[4 * v4 + 2]);
+      ps[4 * v4 + 3] = fmaf(pt, v.w, ps[4 * v4 + 3]);
+    }
+  }
+}
+
+// e^x for x <= 0 given in float64: 2^(x*log2(e)) with the hardware base-2
+// exponential (relative error ~2^-22, far inside the kernel's 1e-6 budget);
+// x = -inf gives exactly 0.
+__device__ __forceinline__ float exp_neg(double x) {
+  const float y = (float)(x * 1.4426950408889634);
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
+  return r;
+}
+
 template <int D, int WARPS, int STAGES>
 __global__ void __launch_bounds__(WARPS * 32)
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES>;
+  constexpr int DPL = C::DPL;
   extern __shared__ __align__(128) char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // WARPS*STAGES
   int* s_tmp = reinterpret_cast<int*>(smem + 8 * WARPS * STAGES);      // WARPS ints
@@ -209,19 +293,28 @@ paged_decode_kernel(DecodeArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = lane % C::LPT, tsub = lane / C::LPT;
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
-  if (blockIdx.x == 0) {
-    int* g_pfx = reinterpret_cast<int*>(a.ws + 16);
-    for (int i = threadIdx.x; i <= a.batch; i += blockDim.x) g_pfx[i] = s_pfx[i];
+  const long long streams = (long long)a.batch * a.heads;
+
+  // Empty streams get exact zeros (the reference returns 0 / max(0, 1e-10)).
+  for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < streams;
+       s += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(s / a.heads);
+    if (s_pfx[b + 1] == s_pfx[b]) {
+      float* dst = a.out + (size_t)s * D;
+      for (int k = 0; k < D; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
-  const long long T = (long long)a.heads * total_pages;
+
+  const long long T = (long long)a.heads * total_pages;  // < 2^31 (checked on the host)
   const long long NW = (long long)gridDim.x * WARPS;
   const long long gw = (long long)blockIdx.x * WARPS + warp;
-  const long long g0 = gw * T / NW, g1 = (gw + 1) * T / NW;
-  const int n = (int)(g1 - g0);
+  const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
+  const int n = g1 - g0;
   if (n <= 0) return;
 
   uint64_t* bar = bars + warp * STAGES;
   char* ring = stages + (size_t)warp * C::WARP_BYTES;
+  float* p_tab = reinterpret_cast<float*>(ring + STAGES * C::STAGE_BYTES);
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) mbar_init(&bar[s], 1);
@@ -231,45 +324,96 @@ paged_decode_kernel(DecodeArgs a) {
 
   Desc cur = make_desc(a, s_pfx, g0 + lane, g0, g1);
   Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
-  // Prologue: the first STAGES pages (all inside chunk 0 since STAGES <= 32).
 #pragma unroll
-  for (int i = 0; i < STAGES; ++i) {
+  for (int i = 0; i < STAGES; ++i) {  // prologue: the first STAGES pages (all in chunk 0)
     const Desc d = shfl_desc(cur, i);
     if (lane == 0 && i < n) issue_page<D, WARPS, STAGES>(a, d, ring + i * C::STAGE_BYTES, &bar[i]);
   }
 
-  double q64[8];
-  float sc[8], ns[8], zs[8];
-  float acc[C::DPL];
+  float q16[16];     // this lane's 16 query dims [16c, 16c+16)
+  double qs[16];     // q*s of those dims for the current group (exact products)
+  double bias = 0.0; // sum over all dims of 16*q*s + q*zp*s for the current group
+  // Value and denominator sums: float32 with a Kahan compensation term, so
+  // long page runs accumulate without float64 conversions on the hot path.
+  float acc[DPL], acc_c[DPL];
+  float l_lane = 0.f, l_c = 0.f;
   double m_run = -INFINITY;
-  float l_lane = 0.f;
   int seg_stream = -1;
   bool aborted = false;
   int abort_at = 0;
 #pragma unroll
-  for (int i = 0; i < C::DPL; ++i) acc[i] = 0.f;
+  for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) { q64[i] = 0.0; sc[i] = 0.f; ns[i] = 0.f; zs[i] = 0.f; }
+  for (int k = 0; k < 16; ++k) { q16[k] = 0.f; qs[k] = 0.0; }
 
-  char* recs = a.ws + rec_offset(a.batch);
-  auto flush = [&](int stream) {
-    float lsum = l_lane;
+  int* counters = reinterpret_cast<int*>(a.ws);
+  char* recs = a.ws + cnt_bytes(streams);
+
+  // Finish the segment of `stream` this warp has accumulated.
+  auto finish = [&](int stream) {
+    double lsum = (double)l_lane - (double)l_c;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
+    const int b = stream / a.heads, h = stream - b * a.heads;
+    const int np = s_pfx[b + 1] - s_pfx[b];
+    const long long gs = (long long)a.heads * s_pfx[b] + (long long)h * np, ge = gs + np;
+    const long long w_lo = ((gs + 1) * NW - 1) / T, w_hi = (ge * NW - 1) / T;
+    const int contributors = (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
+    float* dst = a.out + (size_t)stream * D;
+    float o[DPL];
+    if (contributors == 1) {
+      const double den = fmax(lsum, 1e-10);
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[k] - (double)acc_c[k]) / den);
+      store_lane_vec<D>(dst, o, lane);
+      return;
+    }
     char* rec = recs + (size_t)(gw + stream) * C::REC_BYTES;
     if (lane == 0) {
       *reinterpret_cast<double*>(rec) = m_run;
-      *reinterpret_cast<float*>(rec + 8) = lsum;
+      *reinterpret_cast<double*>(rec + 8) = lsum;
     }
-    float* racc = reinterpret_cast<float*>(rec + 16);
-    if constexpr (C::DPL == 2) {
-      *reinterpret_cast<float2*>(racc + 2 * lane) = make_float2(acc[0], acc[1]);
-    } else {
 #pragma unroll
-      for (int v4 = 0; v4 < C::DPL / 4; ++v4)
-        *reinterpret_cast<float4*>(racc + v4 * 128 + 4 * lane) =
-            make_float4(acc[4 * v4], acc[4 * v4 + 1], acc[4 * v4 + 2], acc[4 * v4 + 3]);
+    for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
+    store_lane_vec<D>(reinterpret_cast<float*>(rec + 16), o, lane);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      const int prev = atomicAdd(&counters[stream], 1);
+      last = (prev == contributors - 1);
+      if (last) counters[stream] = 0;  // leave the workspace zero-filled
     }
+    last = __shfl_sync(kFull, last, 0);
+    if (!last) return;
+    __threadfence();
+    // Merge every contributing warp's record (warps with empty runs wrote none).
+    double M = -INFINITY;
+    for (long long w = w_lo; w <= w_hi; ++w) {
+      if ((w * T) / NW == ((w + 1) * T) / NW) continue;
+      M = fmax(M, __ldcg(reinterpret_cast<const double*>(recs + (size_t)(w + stream) * C::REC_BYTES)));
+    }
+    double L = 0.0, O[DPL];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) O[k] = 0.0;
+    if (M != -INFINITY) {
+      for (long long w = w_lo; w <= w_hi; ++w) {
+        if ((w * T) / NW == ((w + 1) * T) / NW) continue;
+        const char* r = recs + (size_t)(w + stream) * C::REC_BYTES;
+        const double m = __ldcg(reinterpret_cast<const double*>(r));
+        if (m == -INFINITY) continue;
+        const double e = (double)exp_neg(m - M);
+        L = fma(__ldcg(reinterpret_cast<const double*>(r + 8)), e, L);
+        float v[DPL];
+        load_lane_vec_cg<D>(reinterpret_cast<const float*>(r + 16), v, lane);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
+      }
+    }
+    const double den = fmax(L, 1e-10);
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
+    store_lane_vec<D>(dst, o, lane);
   };
 
   for (int i = 0; i < n; ++i) {
@@ -291,49 +435,62 @@ paged_decode_kernel(DecodeArgs a) {
     }
 
     if (has_q) {
-      if (seg_stream >= 0) flush(seg_stream);
+      if (seg_stream >= 0) finish(seg_stream);
       seg_stream = d.stream;
       m_run = -INFINITY;
       l_lane = 0.f;
+      l_c = 0.f;
 #pragma unroll
-      for (int k = 0; k < C::DPL; ++k) acc[k] = 0.f;
-      const float4* qs = reinterpret_cast<const float4*>(slot + C::Q_OFF) + 2 * c;
-      const float4 qa = qs[0], qb = qs[1];
-      q64[0] = qa.x; q64[1] = qa.y; q64[2] = qa.z; q64[3] = qa.w;
-      q64[4] = qb.x; q64[5] = qb.y; q64[6] = qb.z; q64[7] = qb.w;
+      for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
+      const float4* qv = reinterpret_cast<const float4*>(slot + C::Q_OFF) + 4 * c;
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const float4 x = qv[k4];
+        q16[4 * k4] = x.x; q16[4 * k4 + 1] = x.y; q16[4 * k4 + 2] = x.z; q16[4 * k4 + 3] = x.w;
+      }
     }
     if (has_sz) {
-      const float4* ss = reinterpret_cast<const float4*>(slot + C::SZ_OFF) + 2 * c;
-      const float4* zz = reinterpret_cast<const float4*>(slot + C::SZ_OFF + D * 4) + 2 * c;
-      const float4 sa = ss[0], sb = ss[1], za = zz[0], zb = zz[1];
-      const float s8[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-      const float z8[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
+      const float4* sv = reinterpret_cast<const float4*>(slot + C::SZ_OFF) + 4 * c;
+      const float4* zv = reinterpret_cast<const float4*>(slot + C::SZ_OFF + D * 4) + 4 * c;
+      double bsum = 0.0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        sc[k] = s8[k];
-        ns[k] = __fmul_rn(s8[k], -8388608.0f);  // exact: power-of-two scaling
-        zs[k] = __fmul_rn(z8[k], s8[k]);        // the oracle's zp*scale
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const float4 sx = sv[k4], zx = zv[k4];
+        const float s4[4] = {sx.x, sx.y, sx.z, sx.w};
+        const float z4[4] = {zx.x, zx.y, zx.z, zx.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const double qd = (double)q16[4 * k4 + k], sd = (double)s4[k];
+          qs[4 * k4 + k] = qd * sd;  // exact product
+          bsum = fma(16.0, qs[4 * k4 + k], bsum);
+          bsum = fma(qd, (double)z4[k] * sd, bsum);
+        }
       }
+#pragma unroll
+      for (int o = 1; o < C::LPT; o <<= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
+      bias = bsum;
     }
 
     if (ntok > 0) {
-      // ---- logits: lane (c, tsub) dots dims [8c, 8c+8) of tokens j*TPP + tsub ----
-      const uint32_t* kw = reinterpret_cast<const uint32_t*>(slot + C::K_OFF);
+      // ---- logits: lane (c, tsub) dots dims [16c, 16c+16) of tokens j*TPP + tsub ----
+      const uint2* kw = reinterpret_cast<const uint2*>(slot + C::K_OFF);
       double part[C::NJ];
 #pragma unroll
       for (int j = 0; j < C::NJ; ++j) {
-        const uint32_t w = kw[j * 32 + lane];
-        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-        double s = 0.0;
+        const uint2 w = kw[j * 32 + lane];
+        const uint32_t lo0 = (w.x & 0x0F0F0F0Fu) | 0x30303030u;
+        const uint32_t hi0 = ((w.x >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
+        const uint32_t lo1 = (w.y & 0x0F0F0F0Fu) | 0x30303030u;
+        const uint32_t hi1 = ((w.y >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
+        double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const float k0 = __fsub_rn(__fmaf_rn(magic_from_byte(lo, b), sc[2 * b], ns[2 * b]), zs[2 * b]);
-          const float k1 =
-              __fsub_rn(__fmaf_rn(magic_from_byte(hi, b), sc[2 * b + 1], ns[2 * b + 1]), zs[2 * b + 1]);
-          s = fma((double)k0, q64[2 * b], s);
-          s = fma((double)k1, q64[2 * b + 1], s);
+          s0 = fma(qs[2 * b], code_plus16(lo0, b), s0);
+          s1 = fma(qs[2 * b + 1], code_plus16(hi0, b), s1);
+          s2 = fma(qs[8 + 2 * b], code_plus16(lo1, b), s2);
+          s3 = fma(qs[8 + 2 * b + 1], code_plus16(hi1, b), s3);
         }
-        part[j] = s;
+        part[j] = (s0 + s1) + (s2 + s3);
       }
       // reduce-scatter over the LPT lanes of a token group: lane c ends with token j = c >> 1
 #pragma unroll
@@ -348,44 +505,51 @@ paged_decode_kernel(DecodeArgs a) {
           part[k] = keep + __shfl_xor_sync(kFull, send, mask);
         }
       }
-      double logit = part[0] + __shfl_xor_sync(kFull, part[0], 1);
+      double logit = part[0] + __shfl_xor_sync(kFull, part[0], 1) - bias;
       const int tok = (c >> 1) * C::TPP + tsub;
       if (tok >= ntok) logit = -INFINITY;
 
-      // ---- online softmax update for the page ----
-      double pmax = logit;
+      // ---- online softmax: rescale only when the running max moves ----
+      if (__any_sync(kFull, logit > m_run)) {
+        double pmax = logit;
 #pragma unroll
-      for (int o = 16; o > 1; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
-      const double m_new = fmax(m_run, pmax);
-      const float corr = expf((float)(m_run - m_new));
-      const float p = expf((float)(logit - m_new));
-      l_lane = l_lane * corr + (((c & 1) == 0) ? p : 0.f);
-      m_run = m_new;
+        for (int o = 16; o > 1; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
+        const double m_new = fmax(m_run, pmax);
+        const float corr = exp_neg(m_run - m_new);
+        l_lane *= corr;
+        l_c *= corr;
 #pragma unroll
-      for (int k = 0; k < C::DPL; ++k) acc[k] *= corr;
-
-      // ---- P.V over the page's valid rows ----
-      const float* vs = reinterpret_cast<const float*>(slot + C::V_OFF);
-#pragma unroll
-      for (int t = 0; t < kPage; ++t) {
-        if (t < ntok) {
-          const float pt = __shfl_sync(kFull, p, (t % C::TPP) * C::LPT + 2 * (t / C::TPP));
-          if constexpr (C::DPL == 2) {
-            const float2 v = *reinterpret_cast<const float2*>(vs + t * D + 2 * lane);
-            acc[0] = fmaf(pt, v.x, acc[0]);
-            acc[1] = fmaf(pt, v.y, acc[1]);
-          } else {
-#pragma unroll
-            for (int v4 = 0; v4 < C::DPL / 4; ++v4) {
-              const float4 v = *reinterpret_cast<const float4*>(vs + t * D + v4 * 128 + 4 * lane);
-              acc[4 * v4 + 0] = fmaf(pt, v.x, acc[4 * v4 + 0]);
-              acc[4 * v4 + 1] = fmaf(pt, v.y, acc[4 * v4 + 1]);
-              acc[4 * v4 + 2] = fmaf(pt, v.z, acc[4 * v4 + 2]);
-              acc[4 * v4 + 3] = fmaf(pt, v.w, acc[4 * v4 + 3]);
-            }
-          }
-        }
+        for (int k = 0; k < DPL; ++k) { acc[k] *= corr; acc_c[k] *= corr; }
+        m_run = m_new;
       }
+      const float p = exp_neg(logit - m_run);
+      if ((c & 1) == 0) {
+        kahan_rescale_add(l_lane, l_c, 1.f, p);
+        p_tab[tok] = p;  // tok < 16; lanes c and c^1 hold the same token
+      }
+      __syncwarp();
+
+      // ---- P.V over the page's valid rows (float32 page sum, Kahan into the run) ----
+      const float* vs = reinterpret_cast<const float*>(slot + C::V_OFF);
+      float ps[DPL];
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) ps[k] = 0.f;
+      if (ntok == kPage) {
+#pragma unroll
+        for (int t4 = 0; t4 < kPage / 4; ++t4) {
+          const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
+          pv_row<D>(vs, pt.x, 4 * t4 + 0, lane, ps);
+          pv_row<D>(vs, pt.y, 4 * t4 + 1, lane, ps);
+          pv_row<D>(vs, pt.z, 4 * t4 + 2, lane, ps);
+          pv_row<D>(vs, pt.w, 4 * t4 + 3, lane, ps);
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < kPage; ++t)
+          if (t < ntok) pv_row<D>(vs, p_tab[t], t, lane, ps);
+      }
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[k], acc_c[k], 1.f, ps[k]);
     }
 
     __syncwarp();
@@ -404,78 +568,18 @@ paged_decode_kernel(DecodeArgs a) {
       (void)mbar_wait_bounded(&bar[k % STAGES], (uint32_t)((k / STAGES) & 1), kWaitNs);
     return;
   }
-  if (seg_stream >= 0) flush(seg_stream);
-}
-
-// One warp per stream: merge the partial records written by the warps whose
-// page runs overlap the stream; empty streams get exact zeros.
-template <int D>
-__global__ void __launch_bounds__(128)
-combine_kernel(const char* __restrict__ ws, int batch, int heads, long long nw, float* __restrict__ out) {
-  constexpr int REC = 16 + 4 * D;
-  constexpr int DPL = D / 32;
-  const int lane = threadIdx.x & 31;
-  const long long s = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (s >= (long long)batch * heads) return;
-  const int b = (int)(s / heads), h = (int)(s % heads);
-  const int* pfx = reinterpret_cast<const int*>(ws + 16);
-  const long long total = (long long)heads * pfx[batch];
-  const int np = pfx[b + 1] - pfx[b];
-  float o[DPL];
-#pragma unroll
-  for (int k = 0; k < DPL; ++k) o[k] = 0.f;
-  float* dst = out + (size_t)s * D;
-  if (np > 0 && total > 0) {
-    const long long gs = (long long)heads * pfx[b] + (long long)h * np, ge = gs + np;
-    const long long w_lo = ((gs + 1) * nw - 1) / total, w_hi = (ge * nw - 1) / total;
-    const char* recs = ws + rec_offset(batch);
-    double M = -INFINITY;
-    for (long long w = w_lo + lane; w <= w_hi; w += 32)
-      M = fmax(M, *reinterpret_cast<const double*>(recs + (size_t)(w + s) * REC));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmax(M, __shfl_xor_sync(kFull, M, off));
-    float L = 0.f;
-    if (M != -INFINITY) {
-      for (long long w = w_lo; w <= w_hi; ++w) {
-        const char* rec = recs + (size_t)(w + s) * REC;
-        const double m = *reinterpret_cast<const double*>(rec);
-        if (m == -INFINITY) continue;
-        const float e = expf((float)(m - M));
-        L = fmaf(*reinterpret_cast<const float*>(rec + 8), e, L);
-        const float* ra = reinterpret_cast<const float*>(rec + 16);
-        if constexpr (DPL == 2) {
-          const float2 v = *reinterpret_cast<const float2*>(ra + 2 * lane);
-          o[0] = fmaf(v.x, e, o[0]);
-          o[1] = fmaf(v.y, e, o[1]);
-        } else {
-#pragma unroll
-          for (int v4 = 0; v4 < DPL / 4; ++v4) {
-            const float4 v = *reinterpret_cast<const float4*>(ra + v4 * 128 + 4 * lane);
-            o[4 * v4 + 0] = fmaf(v.x, e, o[4 * v4 + 0]);
-            o[4 * v4 + 1] = fmaf(v.y, e, o[4 * v4 + 1]);
-            o[4 * v4 + 2] = fmaf(v.z, e, o[4 * v4 + 2]);
-            o[4 * v4 + 3] = fmaf(v.w, e, o[4 * v4 + 3]);
-          }
-        }
-      }
-      const float den = fmaxf(L, 1e-10f);
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = __fdiv_rn(o[k], den);
-    }
-  }
-  if constexpr (DPL == 2) {
-    *reinterpret_cast<float2*>(dst + 2 * lane) = make_float2(o[0], o[1]);
-  } else {
-#pragma unroll
-    for (int v4 = 0; v4 < DPL / 4; ++v4)
-      *reinterpret_cast<float4*>(dst + v4 * 128 + 4 * lane) =
-          make_float4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
-  }
+  if (seg_stream >= 0) finish(seg_stream);
 }
 
 // ---- host side ----
-constexpr int kWarps = 4;
-constexpr int kStages = 2;
+#ifndef I4KV_DECODE_WARPS
+#define I4KV_DECODE_WARPS 4
+#endif
+#ifndef I4KV_DECODE_STAGES
+#define I4KV_DECODE_STAGES 2
+#endif
+constexpr int kWarps = I4KV_DECODE_WARPS;    // warps per CTA
+constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 
 template <int D>
 size_t dyn_smem(int batch) {
@@ -532,13 +636,14 @@ cudaError_t ws_size(int batch, int heads, size_t* out) {
   int grid = 0;
   cudaError_t e = decode_grid<D>(batch, &grid);
   if (e != cudaSuccess) return e;
-  const size_t nrec = (size_t)grid * kWarps + (size_t)batch * heads;
-  *out = rec_offset(batch) + nrec * Cfg<D, kWarps, kStages>::REC_BYTES;
+  const long long streams = (long long)batch * heads;
+  const size_t nrec = (size_t)grid * kWarps + (size_t)streams;
+  *out = cnt_bytes(streams) + nrec * Cfg<D, kWarps, kStages>::REC_BYTES;
   return cudaSuccess;
 }
 
 template <int D>
-cudaError_t launch(const DecodeArgs& a, float* out, size_t ws_bytes, cudaStream_t stream,
+cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
                    cudaEvent_t ev_before, cudaEvent_t ev_after) {
   int grid = 0;
   cudaError_t e = decode_grid<D>(a.batch, &grid);
@@ -552,10 +657,7 @@ cudaError_t launch(const DecodeArgs& a, float* out, size_t ws_bytes, cudaStream_
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;
-  const long long streams = (long long)a.batch * a.heads;
-  combine_kernel<D><<<(unsigned)((streams + 3) / 4), 128, 0, stream>>>(a.ws, a.batch, a.heads,
-                                                                      (long long)grid * kWarps, out);
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -589,17 +691,17 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
     return cudaErrorInvalidValue;
   if (page_tokens != kPage || group_tokens <= 0 || group_tokens % kPage != 0) return cudaErrorInvalidValue;
   if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
-  if ((long long)batch * num_kv_heads * max_pages >= (1LL << 31)) return cudaErrorInvalidValue;
+  if ((long long)batch * num_kv_heads * max_pages >= (1LL << 31) - 1024) return cudaErrorInvalidValue;
   if (!query || !k_pool || !v_pool || !sz_pool || !block_table || !seq_lens || !out || !workspace)
     return cudaErrorInvalidValue;
   if (!al16(query) || !al16(k_pool) || !al16(v_pool) || !al16(sz_pool) || !al16(out) || !al16(workspace))
     return cudaErrorInvalidValue;
-  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch, num_kv_heads,
+  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_kv_heads,
                max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status};
   switch (head_dim) {
-    case 64: return launch<64>(a, out, workspace_bytes, stream, ev_before, ev_after);
-    case 128: return launch<128>(a, out, workspace_bytes, stream, ev_before, ev_after);
-    case 256: return launch<256>(a, out, workspace_bytes, stream, ev_before, ev_after);
+    case 64: return launch<64>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 128: return launch<128>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 256: return launch<256>(a, workspace_bytes, stream, ev_before, ev_after);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -216,7 +216,7 @@ def prepare_flash_decode_paged(query, k_pool, v_pool, sz_pool, block_table, seq_
     bt = dev(block_table, torch.int32)
     sl = dev(seq_lens, torch.int32)
     out = torch.empty_like(q)
-    ws = torch.empty((_C.paged_decode_workspace_bytes(q.shape[0], q.shape[1], kp.shape[1],
+    ws = torch.zeros((_C.paged_decode_workspace_bytes(q.shape[0], q.shape[1], kp.shape[1],
                                                       q.shape[2], q.device),),
                      dtype=torch.uint8, device=q.device)
     return PreparedCall(

@@ -108,7 +108,8 @@ def test_grouped_baseline_sizes(n_tokens):
     G = n_tokens // group
     blk = kv.view(G, group, h, d)
     lo, hi = blk.amin(dim=1), blk.amax(dim=1)
-    exp_scale = torch.clamp(hi - lo, min=1e-8) / 15.0
+    # tensor / tensor is IEEE division (tensor / python-scalar multiplies by a reciprocal)
+    exp_scale = torch.clamp(hi - lo, min=1e-8) / torch.full_like(lo, 15.0)
     assert torch.equal(scale.view(torch.int32), exp_scale.view(torch.int32))
     assert torch.equal(zp.view(torch.int32), (-lo / exp_scale).view(torch.int32))
     # round trip: |k - dequant(k)| <= scale/2 (+1 ulp slack of the float32 dequant)
