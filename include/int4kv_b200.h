@@ -146,6 +146,35 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
                                          cudaStream_t stream, cudaEvent_t ev_before,
                                          cudaEvent_t ev_after);
 
+/* Scratch capacity of int4kv_paged_decode_static_scratch, per device: a
+ * file-scope device array in the library (8 MiB; enough for 8192 streams at
+ * head_dim 128). */
+#define INT4KV_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* int4kv_paged_decode without a workspace argument, for callers that cannot
+ * allocate device memory on the decode path (a host runtime bound through
+ * this C ABI with no device allocator of its own; a serving step whose device
+ * memory is reserved up front, where cudaMalloc would fail or synchronize the
+ * device). No counterpart in the reference: its launcher allocated nothing
+ * because it had no split-KV scratch. Scratch is a fixed device array of
+ * INT4KV_STATIC_SCRATCH_BYTES per device; a launch that would need more is
+ * rejected with cudaErrorInvalidValue, and *scratch_needed (nullable) receives
+ * the bytes it would need. Each call zeroes the scratch's counter region on
+ * `stream` itself; nothing has to be zeroed by the caller. All calls on one
+ * device share the scratch: calls that overlap in time race, so serialize
+ * them. The first call on a device (and the first per head_dim and batch
+ * size class) performs set-up -- it resolves the array's device address and
+ * sets the kernel's shared-memory attribute -- and should precede any stream
+ * capture. Other arguments, checks and results as int4kv_paged_decode. */
+cudaError_t int4kv_paged_decode_static_scratch(const float* query, const uint8_t* k_pool,
+                                               const float* v_pool, const float* sz_pool,
+                                               const int32_t* block_table,
+                                               const int32_t* seq_lens, int batch,
+                                               int num_q_heads, int num_kv_heads, int head_dim,
+                                               int page_tokens, int group_tokens, int max_pages,
+                                               int num_pages, float* out, uint32_t* status,
+                                               size_t* scratch_needed, cudaStream_t stream);
+
 /* Library identification: returns a static string naming the build. */
 const char* int4kv_build_info(void);
 

@@ -31,6 +31,8 @@ _PROTOS = {
                                                              _c_void_p, _c_void_p],
     "int4kv_paged_decode_profiled": [_c_void_p] * 6 + [_c_int] * 8
                                     + [_c_void_p, _c_void_p, _c_size_t] + [_c_void_p] * 4,
+    "int4kv_paged_decode_static_scratch": [_c_void_p] * 6 + [_c_int] * 8
+                                          + [_c_void_p, _c_void_p, _c_size_p, _c_void_p],
 }
 
 #: Every symbol include/int4kv_b200.h declares (checked by the CPU test suite).

@@ -719,3 +719,78 @@ cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the same decode kernel, with its scratch (per-stream
+// arrival counters + partial records) taken from a fixed device array instead
+// of a caller-provided workspace. It serves callers that cannot allocate
+// device memory on the decode path: a host runtime bound through the C ABI
+// (a cgo / JNI / ctypes stub) that has no device allocator of its own, and a
+// serving step whose device memory is fully reserved up front, where a
+// cudaMalloc would fail or implicitly synchronize the device and stall the
+// other streams.
+//
+// Contract:
+//   * scratch is the file-scope array below, INT4KV_STATIC_SCRATCH_BYTES per
+//     device; a call whose launch would need more is rejected with
+//     cudaErrorInvalidValue and the bytes it would need in *scratch_needed;
+//   * what must start at zero: the counter region [0, cnt_bytes(streams)) --
+//     every call zeroes it on `stream` (cudaMemsetAsync, no allocation) before
+//     the kernel; the partial records need no initial value;
+//   * one scratch per device: calls that overlap in time on the same device
+//     (concurrent streams, host threads) race on it -- serialize them;
+//   * set-up: the first call on a device resolves the array's device address
+//     (cudaGetSymbolAddress, with that device current) and the first call per
+//     (head_dim, batch size class) sets the kernel's shared-memory attribute;
+//     make those first calls before any stream capture begins.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_static_scratch[INT4KV_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices] = {};
+
+// Device address of g_static_scratch on the current device (set up once per device).
+cudaError_t static_scratch_ptr(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    if (!p || (reinterpret_cast<uintptr_t>(p) & 255u)) return cudaErrorInvalidDevicePointer;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" cudaError_t int4kv_paged_decode_static_scratch(
+    const float* query, const uint8_t* k_pool, const float* v_pool, const float* sz_pool,
+    const int32_t* block_table, const int32_t* seq_lens, int batch, int num_q_heads,
+    int num_kv_heads, int head_dim, int page_tokens, int group_tokens, int max_pages,
+    int num_pages, float* out, uint32_t* status, size_t* scratch_needed, cudaStream_t stream) {
+  size_t need = 0;
+  cudaError_t e = int4kv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
+                                                     &need);
+  if (e != cudaSuccess) return e;
+  if (scratch_needed) *scratch_needed = need;
+  if (need > (size_t)INT4KV_STATIC_SCRATCH_BYTES) return cudaErrorInvalidValue;
+  void* scratch = nullptr;
+  e = static_scratch_ptr(&scratch);
+  if (e != cudaSuccess) return e;
+  const size_t zero_bytes = cnt_bytes((long long)batch * num_kv_heads);
+  e = cudaMemsetAsync(scratch, 0, zero_bytes, stream);
+  if (e != cudaSuccess) return e;
+  return int4kv_paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch,
+                             num_q_heads, num_kv_heads, head_dim, page_tokens, group_tokens,
+                             max_pages, num_pages, out, scratch, INT4KV_STATIC_SCRATCH_BYTES,
+                             status, stream);
+}

@@ -78,5 +78,11 @@ def test_paged_launchers_reject_bad_sizes(lib):
     size = ctypes.c_size_t(0)
     assert lib.int4kv_paged_decode_workspace_size(1, 2, 2, 96, ctypes.byref(size)) \
         == CUDA_ERROR_INVALID_VALUE
+    # the allocation-free variant checks the same sizes before touching its scratch
+    need = ctypes.c_size_t(12345)
+    assert lib.int4kv_paged_decode_static_scratch(n, n, n, n, n, n, 1, 4, 2, 128, 16, 128, 4, 4,
+                                                  n, n, ctypes.byref(need), n) \
+        == CUDA_ERROR_INVALID_VALUE
+    assert need.value == 12345
     assert lib.int4kv_dense_decode_workspace_size(1, 1, 300, 1, 1, ctypes.byref(size)) \
         == CUDA_ERROR_INVALID_VALUE
