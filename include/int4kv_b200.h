@@ -134,7 +134,7 @@ cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const
 
 /* int4kv_paged_decode plus timing instrumentation: when non-NULL, ev_before
  * is recorded on `stream` right before the decode kernel and ev_after right
- * after it (before the combine kernel), so a caller can time the dominant
+ * after it (the combine is fused into that kernel), so a caller can time the
  * kernel alone. The work done is identical. */
 cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_pool,
                                          const float* v_pool, const float* sz_pool,
@@ -145,6 +145,38 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream, cudaEvent_t ev_before,
                                          cudaEvent_t ev_after);
+
+/* ---------------------------------------------------------------------------
+ * Sequence split across GPUs (one long sequence, tokens partitioned into
+ * 128-token-group-aligned ranges, one range per GPU). Each GPU decodes its
+ * range into per-stream partial records, the records of all GPUs are gathered
+ * (one collective, e.g. ncclAllGather), and int4kv_merge_partials combines
+ * them. Record of one (sequence, head) stream, INT4KV_PARTIAL_RECORD_BYTES:
+ *   [m float64][l float64][acc float32 x head_dim]
+ * m = running max logit, l = sum of e^(logit - m), acc = sum of e^(logit - m) v
+ * (unnormalized); an empty stream is m = -inf, l = 0, acc = 0. No counterpart
+ * in the reference, whose kernel merges the same triple across the warps of
+ * one CTA (csrc/flash_decode_int4.cu:199-220).
+ * ------------------------------------------------------------------------- */
+#define INT4KV_PARTIAL_RECORD_BYTES(head_dim) (16 + 4 * (head_dim))
+
+/* int4kv_paged_decode, but writing partials [batch * num_kv_heads] records
+ * (16-byte aligned) instead of normalized outputs. */
+cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_pool,
+                                         const float* v_pool, const float* sz_pool,
+                                         const int32_t* block_table, const int32_t* seq_lens,
+                                         int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                         int page_tokens, int group_tokens, int max_pages,
+                                         int num_pages, void* partials, void* workspace,
+                                         size_t workspace_bytes, uint32_t* status,
+                                         cudaStream_t stream);
+
+/* Combine partials [num_parts][streams] records into out [streams, head_dim]
+ * float32: out = sum_p acc_p e^(m_p - M) / max(sum_p l_p e^(m_p - M), 1e-10)
+ * with M = max_p m_p, parts with m = -inf skipped (the reference's warp merge,
+ * csrc/flash_decode_int4.cu:199-220), evaluated in float64. */
+cudaError_t int4kv_merge_partials(const void* partials, int num_parts, int streams, int head_dim,
+                                  float* out, cudaStream_t stream);
 
 /* Scratch capacity of int4kv_paged_decode_static_scratch, per device: a
  * file-scope device array in the library (8 MiB; enough for 8192 streams at

@@ -268,3 +268,63 @@ def paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, group_to
                                            _p(status), _stream(query)),
                    "paged_decode")
     return out
+
+
+def paged_decode_partials(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
+                          group_tokens=128, out=None, workspace=None, status=None):
+    """paged_decode writing per-stream partial records instead of outputs.
+
+    Returns ``out``: uint8 [batch * heads * (16 + 4 * head_dim)], one record
+    ``[m f64][l f64][acc f32 x head_dim]`` per (sequence, head) stream
+    (``INT4KV_PARTIAL_RECORD_BYTES``), for a later ``merge_partials``.
+    """
+    lib = _lib.load()
+    num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
+    if v_pool is None:
+        raise RuntimeError("v_pool is required")
+    _check_input(query, "query")
+    if query.dtype != torch.float32 or query.dim() != 3:
+        raise RuntimeError("query must be float32 [batch, heads, head_dim]")
+    b, hq, qd = query.shape
+    if qd != d or hq != hkv:
+        raise RuntimeError("query must be [batch, kv_heads, pool head_dim]")
+    max_pages = _check_table(block_table, b)
+    _check_input(seq_lens, "seq_lens")
+    if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,):
+        raise RuntimeError("seq_lens must be int32 [batch]")
+    _same_device(query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, workspace, status)
+    nbytes = b * hq * (16 + 4 * d)
+    with torch.cuda.device(query.device):
+        if out is None:
+            out = torch.empty((nbytes,), dtype=torch.uint8, device=query.device)
+        elif out.dtype != torch.uint8 or out.numel() != nbytes or not out.is_contiguous():
+            raise RuntimeError(f"partials must be contiguous uint8 [{nbytes}]")
+        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device)
+        if workspace is None:
+            workspace = torch.zeros((need,), dtype=torch.uint8, device=query.device)
+        elif workspace.numel() * workspace.element_size() < need:
+            raise RuntimeError(f"workspace needs {need} bytes")
+        _lib.check(lib.int4kv_paged_decode_partials(
+            _p(query), _p(k_pool), _p(v_pool), _p(sz_pool), _p(block_table), _p(seq_lens), b, hq,
+            hkv, d, page, group_tokens, max_pages, num_pages, _p(out), _p(workspace),
+            workspace.numel() * workspace.element_size(), _p(status), _stream(query)),
+            "paged_decode_partials")
+    return out
+
+
+def merge_partials(partials, streams, head_dim, out=None):
+    """Combine partial records [parts, streams * record] into float32 [streams, head_dim]."""
+    lib = _lib.load()
+    _check_input(partials, "partials")
+    rec = 16 + 4 * head_dim
+    if partials.dtype != torch.uint8 or partials.numel() % (streams * rec):
+        raise RuntimeError(f"partials must be uint8 [parts, {streams} x {rec}]")
+    parts = partials.numel() // (streams * rec)
+    with torch.cuda.device(partials.device):
+        if out is None:
+            out = torch.empty((streams, head_dim), dtype=torch.float32, device=partials.device)
+        elif out.dtype != torch.float32 or out.numel() != streams * head_dim or not out.is_contiguous():
+            raise RuntimeError("out must be contiguous float32 [streams, head_dim]")
+        _lib.check(lib.int4kv_merge_partials(_p(partials), parts, streams, head_dim, _p(out),
+                                             _stream(partials)), "merge_partials")
+    return out

@@ -91,7 +91,7 @@ I4KV_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limi
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // Requirements (checked by callers): both addresses 16-byte aligned, size a
-// multiple of 16. No multicast: the source is always this GPU's own memory.
+// multiple of 16. One destination CTA; the source is always this GPU's own memory.
 I4KV_DEVINL void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

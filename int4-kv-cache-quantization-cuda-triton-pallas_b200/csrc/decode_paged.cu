@@ -20,7 +20,8 @@
 // streams its pages into them with 1-D bulk async copies (cp.async.bulk, the
 // TMA engine without a tensor map) completing on per-slot mbarriers: the valid
 // rows of V (fp32) and of packed K, plus the group's scale/zp and the stream's
-// query when they change. No multicast; the sources are this GPU's own pools.
+// query when they change. Each copy has one destination CTA; the sources are
+// this GPU's own pools.
 //
 // Numerics: with qs_d = q_d*s_d and c_d the 4-bit code, the logit is
 //   sum_d qs_d*(16 + c_d) - sum_d (16*qs_d + q_d*zp_d*s_d)
@@ -86,6 +87,7 @@ struct DecodeArgs {
   int batch, heads, max_pages, num_pages, group_pages;
   char* ws;
   uint32_t* status;
+  char* part_out;  // nullable: write per-stream partial records instead of outputs
 };
 
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
@@ -295,12 +297,19 @@ paged_decode_kernel(DecodeArgs a) {
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
   const long long streams = (long long)a.batch * a.heads;
 
-  // Empty streams get exact zeros (the reference returns 0 / max(0, 1e-10)).
+  // Empty streams get exact zeros (the reference returns 0 / max(0, 1e-10)),
+  // or, in partial mode, the empty record (m = -inf, l = 0, acc = 0).
   for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < streams;
        s += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(s / a.heads);
     if (s_pfx[b + 1] == s_pfx[b]) {
       float* dst = a.out + (size_t)s * D;
+      if (a.part_out) {
+        char* rec = a.part_out + (size_t)s * C::REC_BYTES;
+        *reinterpret_cast<double*>(rec) = -INFINITY;
+        *reinterpret_cast<double*>(rec + 8) = 0.0;
+        dst = reinterpret_cast<float*>(rec + 16);
+      }
       for (int k = 0; k < D; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
@@ -361,6 +370,17 @@ paged_decode_kernel(DecodeArgs a) {
     const int contributors = (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
     float* dst = a.out + (size_t)stream * D;
     float o[DPL];
+    if (contributors == 1 && a.part_out) {  // partial mode: this warp's record is the stream's
+      char* pr = a.part_out + (size_t)stream * C::REC_BYTES;
+      if (lane == 0) {
+        *reinterpret_cast<double*>(pr) = m_run;
+        *reinterpret_cast<double*>(pr + 8) = lsum;
+      }
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
+      store_lane_vec<D>(reinterpret_cast<float*>(pr + 16), o, lane);
+      return;
+    }
     if (contributors == 1) {
       const double den = fmax(lsum, 1e-10);
 #pragma unroll
@@ -409,6 +429,17 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
         for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
       }
+    }
+    if (a.part_out) {  // partial mode: the merged (M, L, O) of this GPU's share of the stream
+      char* pr = a.part_out + (size_t)stream * C::REC_BYTES;
+      if (lane == 0) {
+        *reinterpret_cast<double*>(pr) = M;
+        *reinterpret_cast<double*>(pr + 8) = L;
+      }
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
+      store_lane_vec<D>(reinterpret_cast<float*>(pr + 16), o, lane);
+      return;
     }
     const double den = fmax(L, 1e-10);
 #pragma unroll
@@ -571,6 +602,46 @@ paged_decode_kernel(DecodeArgs a) {
   if (seg_stream >= 0) finish(seg_stream);
 }
 
+// Merge per-GPU partial records [parts][streams] of one decode step into
+// outputs: the log-sum-exp combine of the reference's warp merge
+// (csrc/flash_decode_int4.cu:199-220: M = max m, L = sum l*e^(m-M),
+// out = sum acc*e^(m-M) / max(L, 1e-10), parts with m = -inf skipped), in
+// float64. One warp per stream.
+template <int D>
+__global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, int num_parts,
+                                                              int streams, float* out) {
+  using C = Cfg<D, 1, 1>;
+  constexpr int DPL = C::DPL;
+  const int lane = threadIdx.x & 31;
+  const long long s = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (s >= streams) return;
+  const size_t stride = (size_t)streams * C::REC_BYTES;
+  const char* base = parts + (size_t)s * C::REC_BYTES;
+  double M = -INFINITY;
+  for (int p = 0; p < num_parts; ++p) M = fmax(M, *reinterpret_cast<const double*>(base + p * stride));
+  double L = 0.0, O[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) O[k] = 0.0;
+  if (M != -INFINITY) {
+    for (int p = 0; p < num_parts; ++p) {
+      const char* r = base + p * stride;
+      const double m = *reinterpret_cast<const double*>(r);
+      if (m == -INFINITY) continue;
+      const double e = (double)exp_neg(m - M);
+      L = fma(*reinterpret_cast<const double*>(r + 8), e, L);
+      float v[DPL];
+      load_lane_vec_cg<D>(reinterpret_cast<const float*>(r + 16), v, lane);
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
+    }
+  }
+  const double den = fmax(L, 1e-10);
+  float o[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
+  store_lane_vec<D>(out + (size_t)s * D, o, lane);
+}
+
 // ---- host side ----
 #ifndef I4KV_DECODE_WARPS
 #define I4KV_DECODE_WARPS 4
@@ -662,6 +733,37 @@ cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Argument checks shared by the decode entry points, then the launch. Exactly
+// one of `out` (normalized outputs) and `part_out` (partial records) is used.
+cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const float* v_pool,
+                        const float* sz_pool, const int32_t* block_table, const int32_t* seq_lens,
+                        int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_tokens, int group_tokens, int max_pages, int num_pages,
+                        float* out, char* part_out, void* workspace, size_t workspace_bytes,
+                        uint32_t* status, cudaStream_t stream, cudaEvent_t ev_before,
+                        cudaEvent_t ev_after) {
+  if (batch <= 0 || batch > kMaxPagedBatch || num_kv_heads <= 0 || num_q_heads != num_kv_heads)
+    return cudaErrorInvalidValue;
+  if (page_tokens != kPage || group_tokens <= 0 || group_tokens % kPage != 0) return cudaErrorInvalidValue;
+  if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
+  if ((long long)batch * num_kv_heads * max_pages >= (1LL << 31) - 1024) return cudaErrorInvalidValue;
+  if (!query || !k_pool || !v_pool || !sz_pool || !block_table || !seq_lens || !workspace)
+    return cudaErrorInvalidValue;
+  if (!out && !part_out) return cudaErrorInvalidValue;
+  if (!al16(query) || !al16(k_pool) || !al16(v_pool) || !al16(sz_pool) || !al16(workspace))
+    return cudaErrorInvalidValue;
+  if ((out && !al16(out)) || (part_out && !al16(part_out))) return cudaErrorInvalidValue;
+  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_kv_heads,
+               max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status,
+               part_out};
+  switch (head_dim) {
+    case 64: return launch<64>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 128: return launch<128>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 256: return launch<256>(a, workspace_bytes, stream, ev_before, ev_after);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -687,23 +789,40 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream, cudaEvent_t ev_before,
                                          cudaEvent_t ev_after) {
-  if (batch <= 0 || batch > kMaxPagedBatch || num_kv_heads <= 0 || num_q_heads != num_kv_heads)
-    return cudaErrorInvalidValue;
-  if (page_tokens != kPage || group_tokens <= 0 || group_tokens % kPage != 0) return cudaErrorInvalidValue;
-  if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
-  if ((long long)batch * num_kv_heads * max_pages >= (1LL << 31) - 1024) return cudaErrorInvalidValue;
-  if (!query || !k_pool || !v_pool || !sz_pool || !block_table || !seq_lens || !out || !workspace)
-    return cudaErrorInvalidValue;
-  if (!al16(query) || !al16(k_pool) || !al16(v_pool) || !al16(sz_pool) || !al16(out) || !al16(workspace))
-    return cudaErrorInvalidValue;
-  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_kv_heads,
-               max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status};
+  return paged_entry(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch, num_q_heads,
+                     num_kv_heads, head_dim, page_tokens, group_tokens, max_pages, num_pages, out,
+                     nullptr, workspace, workspace_bytes, status, stream, ev_before, ev_after);
+}
+
+cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_pool,
+                                         const float* v_pool, const float* sz_pool,
+                                         const int32_t* block_table, const int32_t* seq_lens,
+                                         int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                         int page_tokens, int group_tokens, int max_pages,
+                                         int num_pages, void* partials, void* workspace,
+                                         size_t workspace_bytes, uint32_t* status,
+                                         cudaStream_t stream) {
+  if (!partials) return cudaErrorInvalidValue;
+  return paged_entry(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch, num_q_heads,
+                     num_kv_heads, head_dim, page_tokens, group_tokens, max_pages, num_pages,
+                     nullptr, static_cast<char*>(partials), workspace, workspace_bytes, status,
+                     stream, nullptr, nullptr);
+}
+
+cudaError_t int4kv_merge_partials(const void* partials, int num_parts, int streams, int head_dim,
+                                  float* out, cudaStream_t stream) {
+  if (!partials || !out || num_parts <= 0 || streams <= 0) return cudaErrorInvalidValue;
+  if (!al16(partials) || !al16(out)) return cudaErrorInvalidValue;
+  const int warps = 8;
+  const unsigned grid = (unsigned)((streams + warps - 1) / warps);
+  const char* p = static_cast<const char*>(partials);
   switch (head_dim) {
-    case 64: return launch<64>(a, workspace_bytes, stream, ev_before, ev_after);
-    case 128: return launch<128>(a, workspace_bytes, stream, ev_before, ev_after);
-    case 256: return launch<256>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 64: merge_partials_kernel<64><<<grid, warps * 32, 0, stream>>>(p, num_parts, streams, out); break;
+    case 128: merge_partials_kernel<128><<<grid, warps * 32, 0, stream>>>(p, num_parts, streams, out); break;
+    case 256: merge_partials_kernel<256><<<grid, warps * 32, 0, stream>>>(p, num_parts, streams, out); break;
     default: return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
 }
 
 cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const float* v_pool,

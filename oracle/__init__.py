@@ -26,6 +26,9 @@ from .quantize import (  # noqa: F401
 from .pack import pack_int4, unpack_int4, packed_nbytes  # noqa: F401
 from .attention import (  # noqa: F401
     online_softmax,
+    online_softmax_state,
+    merge_partials,
+    decode_paged_state,
     attention_f64,
     attention_exact_f32_keys,
     paged_stream_pages,

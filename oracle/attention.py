@@ -35,6 +35,15 @@ _F32 = np.float32
 
 def online_softmax(query, pages, values, block_lens=None):
     """(out [B,H,D] f32, log_partition [B,H]) -- src/flash_decode_ref.py:30-139."""
+    m, l, o = online_softmax_state(query, pages, values, block_lens)
+    logz = np.log(np.maximum(l, 1e-10))
+    return o / np.maximum(l, 1e-10)[:, :, np.newaxis], logz
+
+
+def online_softmax_state(query, pages, values, block_lens=None):
+    """The running (m, l, o) of src/flash_decode_ref.py:30-134 before the final
+    normalization (:136-137): max logit, sum of e^(logit-m), unnormalized
+    e^(logit-m)-weighted value sum, all float32."""
     q = np.asarray(query)
     if q.ndim != 3:
         raise AssertionError(f"Query must be 3D (batch, heads, dim), got {q.ndim}D")
@@ -61,8 +70,26 @@ def online_softmax(query, pages, values, block_lens=None):
         l = l * rescale + np.sum(e, axis=-1)
         o = o * rescale[:, :, np.newaxis] + np.einsum('bhs,sd->bhd', e, v)
         m = m_new
-    logz = np.log(np.maximum(l, 1e-10))
-    return o / np.maximum(l, 1e-10)[:, :, np.newaxis], logz
+    return m, l, o
+
+
+def merge_partials(ms, ls, accs):
+    """Combine partial softmax states of disjoint key ranges.
+
+    Restates the cross-warp merge of the reference's CUDA kernel
+    (csrc/flash_decode_int4.cu:199-220): M = max_p m_p; parts whose m is -inf
+    are skipped; L = max(sum_p l_p e^(m_p - M), 1e-10); out = sum_p acc_p
+    e^(m_p - M) / L -- here in float64. ms, ls: [P, ...]; accs: [P, ..., D].
+    """
+    ms = np.asarray(ms, np.float64)
+    ls = np.asarray(ls, np.float64)
+    accs = np.asarray(accs, np.float64)
+    big = ms.max(axis=0)
+    live = ms != -np.inf
+    with np.errstate(invalid="ignore"):
+        e = np.where(live, np.exp(np.where(live, ms - np.where(np.isfinite(big), big, 0.0), 0.0)), 0.0)
+    den = np.maximum((ls * e).sum(axis=0), 1e-10)
+    return (accs * e[..., None]).sum(axis=0) / den[..., None]
 
 
 def _concat_live(pages, values, block_lens, key_f32):
@@ -118,6 +145,26 @@ def paged_stream_pages(k_pool, v_pool, sz_pool, block_table, seq_lens, b, h,
         pages.append((kq, sz_pool[g_phys, h, 0], sz_pool[g_phys, h, 1]))
         vals.append(v_pool[phys, h, :rows])
     return pages, vals
+
+
+def decode_paged_state(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
+                       page=16, group_pages=8):
+    """Per-stream (m [B,H], l [B,H], acc [B,H,D]) of the float32 oracle over a
+    paged cache (query heads == kv heads); empty streams are (-inf, 0, 0)."""
+    q = np.asarray(query, dtype=_F32)
+    nb_, h_, d = q.shape
+    m = np.full((nb_, h_), -np.inf, _F32)
+    l = np.zeros((nb_, h_), _F32)
+    acc = np.zeros((nb_, h_, d), _F32)
+    for b in range(nb_):
+        for h in range(h_):
+            pages, vals = paged_stream_pages(k_pool, v_pool, sz_pool, block_table, seq_lens,
+                                             b, h, d, page, group_pages)
+            if not pages:
+                continue
+            mm, ll, oo = online_softmax_state(q[b:b + 1, h:h + 1], pages, vals)
+            m[b, h], l[b, h], acc[b, h] = mm[0, 0], ll[0, 0], oo[0, 0]
+    return m, l, acc
 
 
 _METHODS = {
