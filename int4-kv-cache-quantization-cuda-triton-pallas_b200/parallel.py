@@ -201,9 +201,16 @@ class SequenceSplitDecoder:
         self.partials = torch.empty((h * self.rec,), dtype=torch.uint8, device=dev)
         self.workspace = torch.zeros((_C.paged_decode_workspace_bytes(1, h, h, d, dev),),
                                      dtype=torch.uint8, device=dev)
+        self._tables = {}
+
+    def refresh(self) -> None:
+        """Forget cached block tables (call after the cache's pages change)."""
+        self._tables.clear()
 
     def local_partials(self, query: torch.Tensor, seq_id: int = 0) -> torch.Tensor:
-        bt, sl = self.cache.block_table([seq_id])
+        if seq_id not in self._tables:
+            self._tables[seq_id] = self.cache.block_table([seq_id])
+        bt, sl = self._tables[seq_id]
         _C.paged_decode_partials(query, self.cache.k_pool, self.cache.v_pool, self.cache.sz_pool,
                                  bt, sl, self.cache.group_tokens, out=self.partials,
                                  workspace=self.workspace)
