@@ -35,6 +35,12 @@ I4KV_DEVINL void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Release/acquire fence at GPU scope (lighter than the sequentially
+// consistent __threadfence): with relaxed atomics on either side it orders
+// the record stores before the arrival count and the merger's record loads
+// after it.
+I4KV_DEVINL void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 I4KV_DEVINL void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -358,93 +358,178 @@ paged_decode_kernel(DecodeArgs a) {
   int* counters = reinterpret_cast<int*>(a.ws);
   char* recs = a.ws + cnt_bytes(streams);
 
-  // Finish the segment of `stream` this warp has accumulated.
-  auto finish = [&](int stream) {
-    double lsum = (double)l_lane - (double)l_c;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
+  // Warps [w_lo, w_hi] whose runs touch `stream`; returns how many of them
+  // hold a non-empty run (those are the stream's contributors).
+  auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
     const int b = stream / a.heads, h = stream - b * a.heads;
     const int np = s_pfx[b + 1] - s_pfx[b];
     const long long gs = (long long)a.heads * s_pfx[b] + (long long)h * np, ge = gs + np;
-    const long long w_lo = ((gs + 1) * NW - 1) / T, w_hi = (ge * NW - 1) / T;
-    const int contributors = (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
-    float* dst = a.out + (size_t)stream * D;
+    w_lo = ((gs + 1) * NW - 1) / T;
+    w_hi = (ge * NW - 1) / T;
+    return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
+  };
+
+  // Warp-wide sum of the lanes' denominators (float32 sum minus compensation).
+  auto lane_sum = [&]() -> double {
+    double lsum = (double)l_lane - (double)l_c;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
+    return lsum;
+  };
+
+  auto put_record = [&](char* rec, double m, double l, const float* o) {
+    if (lane == 0) {
+      *reinterpret_cast<double*>(rec) = m;
+      *reinterpret_cast<double*>(rec + 8) = l;
+    }
+    store_lane_vec<D>(reinterpret_cast<float*>(rec + 16), o, lane);
+  };
+
+  // A stream this warp covered alone: write its output (or, in partial mode,
+  // its record) straight from the running state.
+  auto finish_alone = [&](int stream) {
+    const double lsum = lane_sum();
     float o[DPL];
-    if (contributors == 1 && a.part_out) {  // partial mode: this warp's record is the stream's
-      char* pr = a.part_out + (size_t)stream * C::REC_BYTES;
-      if (lane == 0) {
-        *reinterpret_cast<double*>(pr) = m_run;
-        *reinterpret_cast<double*>(pr + 8) = lsum;
-      }
+    if (a.part_out) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-      store_lane_vec<D>(reinterpret_cast<float*>(pr + 16), o, lane);
+      put_record(a.part_out + (size_t)stream * C::REC_BYTES, m_run, lsum, o);
       return;
     }
-    if (contributors == 1) {
-      const double den = fmax(lsum, 1e-10);
+    const double den = fmax(lsum, 1e-10);
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[k] - (double)acc_c[k]) / den);
-      store_lane_vec<D>(dst, o, lane);
-      return;
-    }
-    char* rec = recs + (size_t)(gw + stream) * C::REC_BYTES;
-    if (lane == 0) {
-      *reinterpret_cast<double*>(rec) = m_run;
-      *reinterpret_cast<double*>(rec + 8) = lsum;
-    }
-#pragma unroll
-    for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-    store_lane_vec<D>(reinterpret_cast<float*>(rec + 16), o, lane);
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      const int prev = atomicAdd(&counters[stream], 1);
-      last = (prev == contributors - 1);
-      if (last) counters[stream] = 0;  // leave the workspace zero-filled
-    }
-    last = __shfl_sync(kFull, last, 0);
-    if (!last) return;
-    __threadfence();
-    // Merge every contributing warp's record (warps with empty runs wrote none).
-    double M = -INFINITY;
-    for (long long w = w_lo; w <= w_hi; ++w) {
-      if ((w * T) / NW == ((w + 1) * T) / NW) continue;
-      M = fmax(M, __ldcg(reinterpret_cast<const double*>(recs + (size_t)(w + stream) * C::REC_BYTES)));
-    }
-    double L = 0.0, O[DPL];
+    for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[k] - (double)acc_c[k]) / den);
+    store_lane_vec<D>(a.out + (size_t)stream * D, o, lane);
+  };
+
+  // Merge every contributor's record of `stream` (this warp arrived last) and
+  // write the output, or in partial mode the merged record. Contributors are
+  // taken in chunks: lane j loads the (m, l) of the chunk's j-th record while
+  // every lane loads its dims of all the chunk's value sums, so a chunk costs
+  // one round trip to L2 (the records were written by other SMs, often on the
+  // other die); chunks combine online in float64.
+  auto merge_stream = [&](int stream, long long w_lo, long long w_hi) {
+    constexpr int CH = 32 / DPL;   // records per chunk (registers: CH * DPL floats)
+    const bool all_run = T >= NW;  // then every warp in [w_lo, w_hi] wrote a record
+    double M = -INFINITY, L = 0.0, O[DPL];
 #pragma unroll
     for (int k = 0; k < DPL; ++k) O[k] = 0.0;
-    if (M != -INFINITY) {
-      for (long long w = w_lo; w <= w_hi; ++w) {
-        if ((w * T) / NW == ((w + 1) * T) / NW) continue;
-        const char* r = recs + (size_t)(w + stream) * C::REC_BYTES;
-        const double m = __ldcg(reinterpret_cast<const double*>(r));
-        if (m == -INFINITY) continue;
-        const double e = (double)exp_neg(m - M);
-        L = fma(__ldcg(reinterpret_cast<const double*>(r + 8)), e, L);
-        float v[DPL];
-        load_lane_vec_cg<D>(reinterpret_cast<const float*>(r + 16), v, lane);
+    for (long long base = w_lo; base <= w_hi; base += CH) {
+      const int cnt = (int)min((long long)CH, w_hi - base + 1);
+      const long long wj = base + lane;
+      const bool okj = lane < cnt && (all_run || (wj * T) / NW != ((wj + 1) * T) / NW);
+      double mj = -INFINITY, lj = 0.0;
+      if (okj) {
+        const char* r = recs + (size_t)(wj + stream) * C::REC_BYTES;
+        mj = __ldcg(reinterpret_cast<const double*>(r));
+        lj = __ldcg(reinterpret_cast<const double*>(r + 8));
+      }
+      float v[CH][DPL];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
+      for (int j = 0; j < CH; ++j) {
+        if (j < cnt) {
+          load_lane_vec_cg<D>(reinterpret_cast<const float*>(
+              recs + (size_t)(base + j + stream) * C::REC_BYTES + 16), v[j], lane);
+        }
       }
+      double cm = mj;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cm = fmax(cm, __shfl_xor_sync(kFull, cm, o));
+      const double m_new = fmax(M, cm);
+      if (m_new == -INFINITY) continue;  // nothing live yet
+      // float64 exponentials (a handful per stream, off the page loop)
+      const double c = (M == -INFINITY) ? 0.0 : exp(M - m_new);
+      const double ej = (okj && mj != -INFINITY) ? exp(mj - m_new) : 0.0;
+      double lc = lj * ej;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lc += __shfl_xor_sync(kFull, lc, o);
+      L = fma(L, c, lc);
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) O[k] *= c;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const double e = __shfl_sync(kFull, ej, j);
+        if (j < cnt && e != 0.0) {  // records of empty runs are never read into the sum
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[j][k], e, O[k]);
+        }
+      }
+      M = m_new;
     }
+    float o[DPL];
     if (a.part_out) {  // partial mode: the merged (M, L, O) of this GPU's share of the stream
-      char* pr = a.part_out + (size_t)stream * C::REC_BYTES;
-      if (lane == 0) {
-        *reinterpret_cast<double*>(pr) = M;
-        *reinterpret_cast<double*>(pr + 8) = L;
-      }
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
-      store_lane_vec<D>(reinterpret_cast<float*>(pr + 16), o, lane);
+      put_record(a.part_out + (size_t)stream * C::REC_BYTES, M, L, o);
       return;
     }
     const double den = fmax(L, 1e-10);
 #pragma unroll
     for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
-    store_lane_vec<D>(dst, o, lane);
+    store_lane_vec<D>(a.out + (size_t)stream * D, o, lane);
+  };
+
+  // The warp's first segment, when its stream is shared with earlier warps and
+  // ends inside this run: its record is held in registers and published with
+  // the last segment's at the end of the run, so the run never stalls on a
+  // fence or an atomic in the middle.
+  int held_stream = -1;
+  double held_m = 0.0, held_l = 0.0;
+  float held_o[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) held_o[k] = 0.f;
+
+  auto end_segment = [&](int stream) {
+    long long w_lo, w_hi;
+    if (contributors_of(stream, w_lo, w_hi) == 1) {
+      finish_alone(stream);
+      return;
+    }
+    held_stream = stream;  // only the run's first segment can get here mid-run
+    held_m = m_run;
+    held_l = lane_sum();
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) held_o[k] = (float)((double)acc[k] - (double)acc_c[k]);
+  };
+
+  // End of the run: publish the held record and the last segment's record
+  // (if shared), one fence, both arrivals counted in parallel, then merge
+  // every stream this warp arrived last at.
+  auto end_run = [&]() {
+    long long lo_c = 0, hi_c = -1, lo_h = 0, hi_h = -1;
+    int n_cur = 0, n_held = 0;
+    if (seg_stream >= 0) {
+      n_cur = contributors_of(seg_stream, lo_c, hi_c);
+      if (n_cur == 1) finish_alone(seg_stream);
+    }
+    if (held_stream >= 0) n_held = contributors_of(held_stream, lo_h, hi_h);
+    const bool pub_cur = n_cur > 1, pub_held = held_stream >= 0;
+    if (!pub_cur && !pub_held) return;
+    if (pub_cur) {
+      float o[DPL];
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
+      const double lsum = lane_sum();
+      put_record(recs + (size_t)(gw + seg_stream) * C::REC_BYTES, m_run, lsum, o);
+    }
+    if (pub_held) put_record(recs + (size_t)(gw + held_stream) * C::REC_BYTES, held_m, held_l, held_o);
+    fence_acq_rel_gpu();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0 && pub_held) {
+      last = atomicAdd(&counters[held_stream], 1) == n_held - 1;
+      if (last) counters[held_stream] = 0;  // leave the workspace zero-filled
+    }
+    if (lane == 1 && pub_cur) {
+      last = atomicAdd(&counters[seg_stream], 1) == n_cur - 1;
+      if (last) counters[seg_stream] = 0;
+    }
+    const bool last_held = __shfl_sync(kFull, last, 0) != 0;
+    const bool last_cur = __shfl_sync(kFull, last, 1) != 0;
+    if (!last_held && !last_cur) return;
+    fence_acq_rel_gpu();
+    if (last_held) merge_stream(held_stream, lo_h, hi_h);
+    if (last_cur) merge_stream(seg_stream, lo_c, hi_c);
   };
 
   for (int i = 0; i < n; ++i) {
@@ -466,7 +551,7 @@ paged_decode_kernel(DecodeArgs a) {
     }
 
     if (has_q) {
-      if (seg_stream >= 0) finish(seg_stream);
+      if (seg_stream >= 0) end_segment(seg_stream);
       seg_stream = d.stream;
       m_run = -INFINITY;
       l_lane = 0.f;
@@ -599,7 +684,7 @@ paged_decode_kernel(DecodeArgs a) {
       (void)mbar_wait_bounded(&bar[k % STAGES], (uint32_t)((k / STAGES) & 1), kWaitNs);
     return;
   }
-  if (seg_stream >= 0) finish(seg_stream);
+  end_run();
 }
 
 // Merge per-GPU partial records [parts][streams] of one decode step into
@@ -627,7 +712,7 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, 
       const char* r = base + p * stride;
       const double m = *reinterpret_cast<const double*>(r);
       if (m == -INFINITY) continue;
-      const double e = (double)exp_neg(m - M);
+      const double e = exp(m - M);
       L = fma(*reinterpret_cast<const double*>(r + 8), e, L);
       float v[DPL];
       load_lane_vec_cg<D>(reinterpret_cast<const float*>(r + 16), v, lane);
