@@ -106,6 +106,17 @@ I4KV_DEVINL void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* 
       : "memory");
 }
 
+// 2-D tiled TMA load of the box at element coordinates (x = inner, y = outer)
+// through a tensor map held in kernel-parameter space; completion counted on
+// `bar`. x * element size must be a multiple of 16 bytes (callers pass
+// multiples of the box width). One destination CTA.
+I4KV_DEVINL void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // Float32 value of a 4-bit code held in byte `sel` (0..3) of `w`, built without
 // an integer->float conversion: the byte is placed in the low mantissa bits of
 // 2^23, so the returned float is exactly 2^23 + code.
@@ -125,6 +136,26 @@ I4KV_DEVINL void channel_params(float mn, float mx, float* scale, float* zp) {
   const float s = __fdiv_rn(range, 15.0f);
   *scale = s;
   *zp = __fdiv_rn(-mn, s);
+}
+
+// The same code without a division per element, bit-identical: y = (x - mn)
+// * RN(1/scale) is within 3 ulp of the IEEE quotient fl((x - mn) / scale); the
+// two round to the same integer unless y lies within 2^-17 (> 3 ulp for
+// y < 16) of a half-integer, and only there the IEEE quotient is computed.
+// Round-half-even to an integer is one add of 1.5 * 2^23 (exact for
+// |y| < 2^22; here 0 <= y <= 15 * (1 + 2^-22)), read back from the bits.
+I4KV_DEVINL uint32_t quant_code_rcp(float x, float mn, float scale, float rcp) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
+  const float a = __fsub_rn(x, mn);
+  float y = __fmul_rn(a, rcp);
+  float t = __fadd_rn(y, kMagic);  // 1.5 * 2^23 + rint(y), ties to even
+  // y - rint(y) is exact (Sterbenz); |.| >= 0.5 - 2^-17 means "near a half"
+  if (fabsf(__fsub_rn(y, __fsub_rn(t, kMagic))) >= 0.49999237060546875f) {
+    y = __fdiv_rn(a, scale);
+    t = __fadd_rn(y, kMagic);
+  }
+  const int q = __float_as_int(t) - 0x4B400000;
+  return static_cast<uint32_t>(min(max(q, 0), 15));
 }
 
 // q = clip(round_half_even((x - min) / scale), 0, 15)  (src/quantize_int4_ref.py:74-75)

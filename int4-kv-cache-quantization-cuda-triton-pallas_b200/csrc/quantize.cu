@@ -22,8 +22,12 @@
 //                            splits the rows; partial min/max meet in distributed
 //                            shared memory, so no global scratch is needed.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "../../include/int4kv_b200.h"
@@ -65,20 +69,22 @@ __device__ __forceinline__ void minmax4(const float4& v, float4& mn, float4& mx)
   mx.x = fmaxf(mx.x, v.x); mx.y = fmaxf(mx.y, v.y); mx.z = fmaxf(mx.z, v.z); mx.w = fmaxf(mx.w, v.w);
 }
 
-__device__ __forceinline__ uint16_t pack4(const float4& v, const float4& mn, const float4& sc) {
-  const uint32_t a = quant_code(v.x, mn.x, sc.x);
-  const uint32_t b = quant_code(v.y, mn.y, sc.y);
-  const uint32_t c = quant_code(v.z, mn.z, sc.z);
-  const uint32_t d = quant_code(v.w, mn.w, sc.w);
+__device__ __forceinline__ uint16_t pack4(const float4& v, const float4& mn, const float4& sc,
+                                           const float4& rc) {
+  const uint32_t a = quant_code_rcp(v.x, mn.x, sc.x, rc.x);
+  const uint32_t b = quant_code_rcp(v.y, mn.y, sc.y, rc.y);
+  const uint32_t c = quant_code_rcp(v.z, mn.z, sc.z, rc.z);
+  const uint32_t d = quant_code_rcp(v.w, mn.w, sc.w, rc.w);
   return static_cast<uint16_t>(a | (b << 4) | (c << 8) | (d << 12));
 }
 
 // Cross-warp reduction of per-lane [4-channel] min/max into per-channel
-// (min, scale) in shared memory; also emits scale/zp through `emit(ch, s, z)`.
+// (min, scale, 1/scale) in shared memory; also emits scale/zp through
+// `emit(ch, s, z)`.
 template <class Emit>
 __device__ __forceinline__ void reduce_params(float4 mn, float4 mx, float* s_min, float* s_max,
-                                              float* s_lo, float* s_sc, int slab_c0, int C,
-                                              Emit emit) {
+                                              float* s_lo, float* s_sc, float* s_rc, int slab_c0,
+                                              int C, Emit emit) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   reinterpret_cast<float4*>(s_min)[warp * 32 + lane] = mn;
   reinterpret_cast<float4*>(s_max)[warp * 32 + lane] = mx;
@@ -95,6 +101,7 @@ __device__ __forceinline__ void reduce_params(float4 mn, float4 mx, float* s_min
     channel_params(lo, hi, &s, &z);
     s_lo[ch] = lo;
     s_sc[ch] = s;
+    s_rc[ch] = __frcp_rn(s);
     if (slab_c0 + ch < C) emit(slab_c0 + ch, s, z);
   }
   __syncthreads();
@@ -107,6 +114,7 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
   __shared__ __align__(16) float s_max[kQuantWarps * kSlab];
   __shared__ __align__(16) float s_lo[kSlab];
   __shared__ __align__(16) float s_sc[kSlab];
+  __shared__ __align__(16) float s_rc[kSlab];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slab_c0 = blockIdx.x * kSlab;
@@ -145,7 +153,7 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
   }
 
   if constexpr (!kPaged) {
-    reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, slab_c0, C, [&](int ch, float s, float z) {
+    reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, s_rc, slab_c0, C, [&](int ch, float s, float z) {
       oc.scale[(size_t)g * C + ch] = s;
       oc.zp[(size_t)g * C + ch] = z;
     });
@@ -154,7 +162,7 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
     const int gpage = gpos / op.page;
     int slot = (gpage < op.max_pages) ? op.block_table[(size_t)seq * op.max_pages + gpage] : -1;
     if (slot < 0 || slot >= op.num_pages) slot = -1;
-    reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, slab_c0, C, [&](int ch, float s, float z) {
+    reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, s_rc, slab_c0, C, [&](int ch, float s, float z) {
       if (slot < 0) return;
       const int h = ch / op.head_dim, d = ch - h * op.head_dim;
       float* dst = op.sz_pool + ((size_t)slot * op.heads + h) * 2 * op.head_dim;
@@ -167,11 +175,12 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
 
   const float4 lo = reinterpret_cast<const float4*>(s_lo)[lane];
   const float4 sc = reinterpret_cast<const float4*>(s_sc)[lane];
+  const float4 rc = reinterpret_cast<const float4*>(s_rc)[lane];
 #pragma unroll
   for (int i = 0; i < kMaxRowsPerWarp; ++i) {
     const int r = warp + i * kQuantWarps;
     if (r < rows) {
-      const uint16_t code = pack4(vals[i], lo, sc);
+      const uint16_t code = pack4(vals[i], lo, sc, rc);
       if constexpr (!kPaged) {
         *reinterpret_cast<uint16_t*>(oc.packed + ((size_t)(r0 + r) * C + c0) / 2) = code;
       } else {
@@ -195,6 +204,178 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
   }
 }
 
+// Persistent, TMA-pipelined form of grouped_quant_kernel for the contiguous
+// output (groups of R <= 128 rows, C % 32 == 0). Two CTAs per SM walk tiles
+// (group g, 64-channel slab) t = blockIdx.x, + gridDim.x, ...; the TMA engine
+// moves each tile (R rows x 256 B, one 2-D tensor copy) into a ring of
+// kTmaStages shared-memory stages, so later tiles stream in while the current
+// one is reduced and quantized, and the other CTA's serial phases overlap
+// this one's. Thread (row group q = tid / 16, channel quad c = tid % 16) owns
+// channels [4c, 4c+4) of rows q, q+32, q+64, q+96, held in registers between
+// the min/max pass and the quantize pass; codes are staged in shared memory
+// and leave as 16-byte stores. Thread 0 alone waits on a stage's barrier
+// (bounded) and the CTA learns the outcome through shared memory, so every
+// thread takes the same path; after a timeout the CTA drains its copies
+// (bounded), writes NaN into the scale/zp of every tile it did not finish,
+// and exits.
+constexpr int kTmaStages = 3;
+constexpr int kTmaThreads = 512;
+constexpr int kTmaSlab = 64;                                // channels per tile
+constexpr int kTmaQuads = kTmaSlab / 4;                     // 16 threads per row
+constexpr int kTmaRowGroups = kTmaThreads / kTmaQuads;      // 32
+constexpr int kTmaRowsPerThread = kRegGroupMax / kTmaRowGroups;  // 4
+constexpr int kTileRows = kRegGroupMax;                     // 128 rows x 64 channels = 32 KB
+constexpr int kOutRowBytes = kTmaSlab / 2;                  // 32 B of codes per row
+constexpr int kTmaWarps = kTmaThreads / 32;
+constexpr uint64_t kQuantWaitNs = 2000000000ull;            // 2 s
+
+struct TmaSmem {
+  float stage[kTmaStages][kTileRows * kTmaSlab];
+  float4 s_min[kTmaWarps * kTmaQuads];   // per warp: 2 row groups folded, 16 quads
+  float4 s_max[kTmaWarps * kTmaQuads];
+  float s_lo[kTmaSlab];
+  float s_sc[kTmaSlab];
+  float s_rc[kTmaSlab];
+  uint8_t s_out[kTileRows * kOutRowBytes];
+  uint64_t bar[kTmaStages];
+  int ok;
+};
+
+// Load tile `tile` into `dst`: one 2-D tensor copy for a full group; the
+// short last group (rows < R) instead takes one 1-D bulk copy per row, so no
+// box ever reaches past the tensor and the byte count is exact.
+__device__ __forceinline__ void tma_issue_tile(const CUtensorMap* tmap, const float* kv, int N,
+                                               int C, int R, int S, long long tile, float* dst,
+                                               uint64_t* bar) {
+  const int g = (int)(tile / S), slab = (int)(tile - (long long)g * S);
+  const int r0 = g * R, rows = min(R, N - r0);
+  fence_proxy_async_smem();
+  mbar_arrive_expect_tx(bar, (uint32_t)(rows * kTmaSlab * 4));
+  if (rows == R) {
+    tma_load_2d(dst, tmap, slab * kTmaSlab, r0, bar);
+  } else {
+    for (int r = 0; r < rows; ++r)
+      bulk_g2s(dst + r * kTmaSlab, kv + (size_t)(r0 + r) * C + slab * kTmaSlab, kTmaSlab * 4, bar);
+  }
+}
+
+__global__ void __launch_bounds__(kTmaThreads, 2)
+grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ kv,
+                         int N, int C, int R, OutContig oc) {
+  extern __shared__ __align__(128) char smem_raw[];
+  TmaSmem& sm = *reinterpret_cast<TmaSmem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cq = tid % kTmaQuads, rg = tid / kTmaQuads;
+  const int S = C / kTmaSlab;  // C % 64 == 0 (launcher)
+  const long long total = (long long)((N + R - 1) / R) * S;
+  const long long first = blockIdx.x, step = gridDim.x;
+  if (first >= total) return;
+  if (tid == 0) {
+    for (int i = 0; i < kTmaStages; ++i) mbar_init(&sm.bar[i], 1);
+    fence_barrier_init();
+    for (int i = 0; i < kTmaStages; ++i) {
+      const long long t = first + i * step;
+      if (t < total) tma_issue_tile(&tmap, kv, N, C, R, S, t, sm.stage[i], &sm.bar[i]);
+    }
+  }
+  __syncthreads();
+  long long i = 0;
+  for (long long t = first; t < total; t += step, ++i) {
+    const int st = (int)(i % kTmaStages);
+    const uint32_t parity = (uint32_t)((i / kTmaStages) & 1);
+    if (tid == 0) sm.ok = mbar_wait_bounded(&sm.bar[st], parity, kQuantWaitNs) ? 1 : 0;
+    __syncthreads();
+    if (!sm.ok) {
+      // drain the copies still in flight (bounded), poison what was not done
+      if (tid == 0) {
+        for (long long k = 0; k < kTmaStages && t + k * step < total; ++k)
+          (void)mbar_wait_bounded(&sm.bar[(i + k) % kTmaStages],
+                                  (uint32_t)(((i + k) / kTmaStages) & 1), kQuantWaitNs);
+      }
+      for (long long u = t; u < total; u += step) {
+        const int g = (int)(u / S), c0 = (int)(u - (long long)g * S) * kTmaSlab;
+        for (int c = tid; c < kTmaSlab; c += blockDim.x) {
+          oc.scale[(size_t)g * C + c0 + c] = __int_as_float(0x7fc00000);
+          oc.zp[(size_t)g * C + c0 + c] = __int_as_float(0x7fc00000);
+        }
+      }
+      return;
+    }
+    (void)mbar_try_wait(&sm.bar[st], parity);  // completed: acquire for this thread too
+    const int g = (int)(t / S), slab = (int)(t - (long long)g * S);
+    const int r0 = g * R, rows = min(R, N - r0);
+    const int slab_c0 = slab * kTmaSlab;
+    const float* tile = sm.stage[st];
+
+    float4 vals[kTmaRowsPerThread];
+    float4 mn = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+    float4 mx = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+    for (int k = 0; k < kTmaRowsPerThread; ++k) {
+      const int r = rg + k * kTmaRowGroups;
+      if (r < rows) {
+        vals[k] = reinterpret_cast<const float4*>(tile + r * kTmaSlab)[cq];
+        minmax4(vals[k], mn, mx);
+      }
+    }
+    // fold the warp's two row groups (lanes l and l ^ 16 hold the same quad)
+    {
+      float4 o;
+      o.x = __shfl_xor_sync(0xffffffffu, mn.x, 16); o.y = __shfl_xor_sync(0xffffffffu, mn.y, 16);
+      o.z = __shfl_xor_sync(0xffffffffu, mn.z, 16); o.w = __shfl_xor_sync(0xffffffffu, mn.w, 16);
+      float4 p;
+      p.x = __shfl_xor_sync(0xffffffffu, mx.x, 16); p.y = __shfl_xor_sync(0xffffffffu, mx.y, 16);
+      p.z = __shfl_xor_sync(0xffffffffu, mx.z, 16); p.w = __shfl_xor_sync(0xffffffffu, mx.w, 16);
+      mn.x = fminf(mn.x, o.x); mn.y = fminf(mn.y, o.y); mn.z = fminf(mn.z, o.z); mn.w = fminf(mn.w, o.w);
+      mx.x = fmaxf(mx.x, p.x); mx.y = fmaxf(mx.y, p.y); mx.z = fmaxf(mx.z, p.z); mx.w = fmaxf(mx.w, p.w);
+    }
+    if (lane < kTmaQuads) {
+      sm.s_min[warp * kTmaQuads + lane] = mn;
+      sm.s_max[warp * kTmaQuads + lane] = mx;
+    }
+    __syncthreads();  // stage st fully read: refill it; partial min/max visible
+    if (tid == 0 && t + kTmaStages * step < total)
+      tma_issue_tile(&tmap, kv, N, C, R, S, t + kTmaStages * step, sm.stage[st], &sm.bar[st]);
+    if (tid < kTmaSlab) {
+      const int ch = tid, q = ch >> 2, e = ch & 3;
+      const float* pmin = reinterpret_cast<const float*>(sm.s_min);
+      const float* pmax = reinterpret_cast<const float*>(sm.s_max);
+      float lo = pmin[q * 4 + e], hi = pmax[q * 4 + e];
+#pragma unroll
+      for (int w = 1; w < kTmaWarps; ++w) {
+        lo = fminf(lo, pmin[(w * kTmaQuads + q) * 4 + e]);
+        hi = fmaxf(hi, pmax[(w * kTmaQuads + q) * 4 + e]);
+      }
+      float sc, zp;
+      channel_params(lo, hi, &sc, &zp);
+      sm.s_lo[ch] = lo;
+      sm.s_sc[ch] = sc;
+      sm.s_rc[ch] = __frcp_rn(sc);
+      oc.scale[(size_t)g * C + slab_c0 + ch] = sc;
+      oc.zp[(size_t)g * C + slab_c0 + ch] = zp;
+    }
+    __syncthreads();
+    {
+      const float4 lo = reinterpret_cast<const float4*>(sm.s_lo)[cq];
+      const float4 sc = reinterpret_cast<const float4*>(sm.s_sc)[cq];
+      const float4 rc = reinterpret_cast<const float4*>(sm.s_rc)[cq];
+#pragma unroll
+      for (int k = 0; k < kTmaRowsPerThread; ++k) {
+        const int r = rg + k * kTmaRowGroups;
+        if (r < rows)
+          *reinterpret_cast<uint16_t*>(sm.s_out + r * kOutRowBytes + cq * 2) = pack4(vals[k], lo, sc, rc);
+      }
+    }
+    __syncthreads();
+    // codes out: two 16-byte stores per row; C % 64 == 0 keeps them aligned
+    for (int idx = tid; idx < rows * (kOutRowBytes / 16); idx += blockDim.x) {
+      const int r = idx >> 1, part = idx & 1;
+      *reinterpret_cast<uint4*>(oc.packed + ((size_t)(r0 + r) * C + slab_c0) / 2 + part * 16) =
+          *reinterpret_cast<const uint4*>(sm.s_out + r * kOutRowBytes + part * 16);
+    }
+  }
+}
+
 // Groups longer than 128 rows: pass 1 min/max, pass 2 quantize (re-read, L2-resident).
 __global__ void __launch_bounds__(kQuantThreads)
 grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, OutContig oc) {
@@ -202,6 +383,7 @@ grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, Out
   __shared__ __align__(16) float s_max[kQuantWarps * kSlab];
   __shared__ __align__(16) float s_lo[kSlab];
   __shared__ __align__(16) float s_sc[kSlab];
+  __shared__ __align__(16) float s_rc[kSlab];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slab_c0 = blockIdx.x * kSlab;
   const int c0 = slab_c0 + lane * 4;
@@ -217,16 +399,17 @@ grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, Out
       minmax4(__ldg(reinterpret_cast<const float4*>(kv + (size_t)(r0 + r) * C + c0)), mn, mx);
     }
   }
-  reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, slab_c0, C, [&](int ch, float s, float z) {
+  reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, s_rc, slab_c0, C, [&](int ch, float s, float z) {
     oc.scale[(size_t)g * C + ch] = s;
     oc.zp[(size_t)g * C + ch] = z;
   });
   if (!lane_ok) return;
   const float4 lo = reinterpret_cast<const float4*>(s_lo)[lane];
   const float4 sc = reinterpret_cast<const float4*>(s_sc)[lane];
+  const float4 rc = reinterpret_cast<const float4*>(s_rc)[lane];
   for (int r = warp; r < rows; r += kQuantWarps) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(kv + (size_t)(r0 + r) * C + c0));
-    *reinterpret_cast<uint16_t*>(oc.packed + ((size_t)(r0 + r) * C + c0) / 2) = pack4(v, lo, sc);
+    *reinterpret_cast<uint16_t*>(oc.packed + ((size_t)(r0 + r) * C + c0) / 2) = pack4(v, lo, sc, rc);
   }
 }
 
@@ -244,6 +427,7 @@ legacy_quant_kernel(const float* __restrict__ kv, int rows, int C, uint8_t* __re
   __shared__ float s_pmax[32];
   __shared__ float s_lo[32];
   __shared__ float s_sc[32];
+  __shared__ float s_rc[32];
   cg::cluster_group cluster = cg::this_cluster();
   const int cl = static_cast<int>(cluster.num_blocks());
   const int rank = static_cast<int>(cluster.block_rank());
@@ -295,6 +479,7 @@ legacy_quant_kernel(const float* __restrict__ kv, int rows, int C, uint8_t* __re
     channel_params(glo, ghi, &s, &z);
     s_lo[lane] = glo;
     s_sc[lane] = s;
+    s_rc[lane] = __frcp_rn(s);
     if (rank == 0 && ok) {
       scale_out[c] = s;
       zp_out[c] = z;
@@ -302,13 +487,65 @@ legacy_quant_kernel(const float* __restrict__ kv, int rows, int C, uint8_t* __re
   }
   cluster.sync();  // peers are done reading this CTA's partials; s_lo/s_sc visible
   if (!ok) return;
-  const float mn = s_lo[lane], sc = s_sc[lane];
+  const float mn = s_lo[lane], sc = s_sc[lane], rc = s_rc[lane];
   for (int r = rb + warp; r < re; r += kLegacyWarps) {
-    q_out[(size_t)r * C + c] = static_cast<uint8_t>(quant_code(__ldg(kv + (size_t)r * C + c), mn, sc));
+    q_out[(size_t)r * C + c] =
+        static_cast<uint8_t>(quant_code_rcp(__ldg(kv + (size_t)r * C + c), mn, sc, rc));
   }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// SM count and the persistent kernel's shared-memory opt-in, once per device.
+cudaError_t tma_quant_setup(int* sms_out) {
+  static std::mutex mu;
+  static int sms[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!sms[dev]) {
+    e = cudaFuncSetAttribute(grouped_quant_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(TmaSmem));
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sms[dev] = n;
+  }
+  *sms_out = sms[dev];
+  return cudaSuccess;
+}
+
+// 2-D tensor map over a row-major float32 matrix [rows, cols]: boxes of
+// box_rows x box_cols (the driver's encoder, reached through the runtime so
+// the library does not link libcuda itself).
+cudaError_t encode_rows_map(CUtensorMap* map, const float* base, int rows, int cols, int box_cols,
+                            int box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!encode) {
+      cudaDriverEntryPointQueryResult qr;
+      void* fn = nullptr;
+      const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr);
+      if (e != cudaSuccess) return e;
+      if (qr != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
 
 }  // namespace
 
@@ -350,7 +587,20 @@ cudaError_t int4kv_quantize_grouped(const float* kv, int num_tokens, int num_hea
   if (groups > 65535) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((C + kSlab - 1) / kSlab), groups, 1);
   OutContig oc{packed_out, scale_out, zp_out};
-  if (group_tokens <= kRegGroupMax) {
+  cudaError_t e = cudaSuccess;
+  int sms = 0;
+  CUtensorMap tmap;
+  if (group_tokens <= kRegGroupMax && C % kTmaSlab == 0 && aligned16(packed_out) &&
+      (e = tma_quant_setup(&sms)) == cudaSuccess &&
+      (e = encode_rows_map(&tmap, kv, num_tokens, (int)C, kTmaSlab, group_tokens)) == cudaSuccess) {
+    const long long tiles = (long long)groups * (C / kTmaSlab);
+    const long long slots = 2LL * sms;  // two CTAs per SM
+    const unsigned pgrid = (unsigned)(tiles < slots ? tiles : slots);
+    grouped_quant_tma_kernel<<<pgrid, kTmaThreads, sizeof(TmaSmem), stream>>>(
+        tmap, kv, num_tokens, (int)C, group_tokens, oc);
+  } else if (e != cudaSuccess) {
+    return e;
+  } else if (group_tokens <= kRegGroupMax) {
     grouped_quant_kernel<false><<<grid, kQuantThreads, 0, stream>>>(kv, num_tokens, (int)C,
                                                                      group_tokens, oc, OutPaged{});
   } else {
