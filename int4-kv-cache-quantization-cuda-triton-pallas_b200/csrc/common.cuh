@@ -154,8 +154,54 @@ I4KV_DEVINL uint32_t quant_code_rcp(float x, float mn, float scale, float rcp) {
     y = __fdiv_rn(a, scale);
     t = __fadd_rn(y, kMagic);
   }
-  const int q = __float_as_int(t) - 0x4B400000;
-  return static_cast<uint32_t>(min(max(q, 0), 15));
+  // 0 <= y <= 15 * (1 + 3 * 2^-24) for x in [mn, max], so rint(y) is already
+  // in [0, 15]: the mask only keeps the nibble (and maps a NaN input to 0).
+  return static_cast<uint32_t>(__float_as_int(t) - 0x4B400000) & 15u;
+}
+
+// Paired IEEE float32 arithmetic (sm_100 f32x2 instructions, round to
+// nearest even, subnormals kept): two lanes of work per instruction.
+#define I4KV_F32X2_OP(name, op)                                                               \
+  I4KV_DEVINL void name(float& d0, float& d1, float a0, float a1, float b0, float b1) {       \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" op \
+        " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                      \
+        : "=f"(d0), "=f"(d1)                                                                \
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));                                              \
+  }
+I4KV_F32X2_OP(add2_rn, "add.rn.f32x2")
+I4KV_F32X2_OP(sub2_rn, "sub.rn.f32x2")
+I4KV_F32X2_OP(mul2_rn, "mul.rn.f32x2")
+#undef I4KV_F32X2_OP
+
+// Four codes of one row's channel quad (quant_code_rcp for each, in paired
+// arithmetic), nibble-packed as c0 | c1 << 4 | c2 << 8 | c3 << 12. The low
+// byte of the bits of 1.5 * 2^23 + rint(y) is rint(y) itself, so the codes
+// are gathered with byte permutes.
+I4KV_DEVINL uint32_t pack4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
+  constexpr float kMagic = 12582912.0f;
+  constexpr float kNearHalf = 0.49999237060546875f;  // 0.5 - 2^-17
+  float a0, a1, a2, a3, y0, y1, y2, y3, t0, t1, t2, t3, r0, r1, r2, r3, d0, d1, d2, d3;
+  sub2_rn(a0, a1, v.x, v.y, mn.x, mn.y);
+  sub2_rn(a2, a3, v.z, v.w, mn.z, mn.w);
+  mul2_rn(y0, y1, a0, a1, rc.x, rc.y);
+  mul2_rn(y2, y3, a2, a3, rc.z, rc.w);
+  add2_rn(t0, t1, y0, y1, kMagic, kMagic);
+  add2_rn(t2, t3, y2, y3, kMagic, kMagic);
+  sub2_rn(r0, r1, t0, t1, kMagic, kMagic);
+  sub2_rn(r2, r3, t2, t3, kMagic, kMagic);
+  sub2_rn(d0, d1, y0, y1, r0, r1);
+  sub2_rn(d2, d3, y2, y3, r2, r3);
+  if (fmaxf(fmaxf(fabsf(d0), fabsf(d1)), fmaxf(fabsf(d2), fabsf(d3))) >= kNearHalf) {
+    if (fabsf(d0) >= kNearHalf) t0 = __fadd_rn(__fdiv_rn(a0, sc.x), kMagic);
+    if (fabsf(d1) >= kNearHalf) t1 = __fadd_rn(__fdiv_rn(a1, sc.y), kMagic);
+    if (fabsf(d2) >= kNearHalf) t2 = __fadd_rn(__fdiv_rn(a2, sc.z), kMagic);
+    if (fabsf(d3) >= kNearHalf) t3 = __fadd_rn(__fdiv_rn(a3, sc.w), kMagic);
+  }
+  const uint32_t x = __byte_perm(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040),
+                                 __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040),
+                                 0x5410);                       // bytes c0, c1, c2, c3
+  const uint32_t y = (x | (x >> 4)) & 0x00FF00FFu;              // c0|c1<<4, ., c2|c3<<4, .
+  return __byte_perm(y, 0u, 0x4420);                            // [c0|c1<<4][c2|c3<<4]
 }
 
 // q = clip(round_half_even((x - min) / scale), 0, 15)  (src/quantize_int4_ref.py:74-75)

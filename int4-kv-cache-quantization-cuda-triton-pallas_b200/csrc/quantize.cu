@@ -71,11 +71,7 @@ __device__ __forceinline__ void minmax4(const float4& v, float4& mn, float4& mx)
 
 __device__ __forceinline__ uint16_t pack4(const float4& v, const float4& mn, const float4& sc,
                                            const float4& rc) {
-  const uint32_t a = quant_code_rcp(v.x, mn.x, sc.x, rc.x);
-  const uint32_t b = quant_code_rcp(v.y, mn.y, sc.y, rc.y);
-  const uint32_t c = quant_code_rcp(v.z, mn.z, sc.z, rc.z);
-  const uint32_t d = quant_code_rcp(v.w, mn.w, sc.w, rc.w);
-  return static_cast<uint16_t>(a | (b << 4) | (c << 8) | (d << 12));
+  return static_cast<uint16_t>(pack4_rcp(v, mn, sc, rc));
 }
 
 // Cross-warp reduction of per-lane [4-channel] min/max into per-channel
@@ -212,8 +208,8 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
 // one is reduced and quantized, and the other CTA's serial phases overlap
 // this one's. Thread (row group q = tid / 16, channel quad c = tid % 16) owns
 // channels [4c, 4c+4) of rows q, q+32, q+64, q+96, held in registers between
-// the min/max pass and the quantize pass; codes are staged in shared memory
-// and leave as 16-byte stores. Thread 0 alone waits on a stage's barrier
+// the min/max pass and the quantize pass; the 16 threads of a row store its
+// 32 code bytes together (one full sector). Thread 0 alone waits on a stage's barrier
 // (bounded) and the CTA learns the outcome through shared memory, so every
 // thread takes the same path; after a timeout the CTA drains its copies
 // (bounded), writes NaN into the scale/zp of every tile it did not finish,
@@ -225,18 +221,16 @@ constexpr int kTmaQuads = kTmaSlab / 4;                     // 16 threads per ro
 constexpr int kTmaRowGroups = kTmaThreads / kTmaQuads;      // 32
 constexpr int kTmaRowsPerThread = kRegGroupMax / kTmaRowGroups;  // 4
 constexpr int kTileRows = kRegGroupMax;                     // 128 rows x 64 channels = 32 KB
-constexpr int kOutRowBytes = kTmaSlab / 2;                  // 32 B of codes per row
 constexpr int kTmaWarps = kTmaThreads / 32;
 constexpr uint64_t kQuantWaitNs = 2000000000ull;            // 2 s
 
 struct TmaSmem {
   float stage[kTmaStages][kTileRows * kTmaSlab];
-  float4 s_min[kTmaWarps * kTmaQuads];   // per warp: 2 row groups folded, 16 quads
+  float4 s_min[kTmaWarps * kTmaQuads];   // [warp][channel] partials (2 row groups folded)
   float4 s_max[kTmaWarps * kTmaQuads];
   float s_lo[kTmaSlab];
   float s_sc[kTmaSlab];
   float s_rc[kTmaSlab];
-  uint8_t s_out[kTileRows * kOutRowBytes];
   uint64_t bar[kTmaStages];
   int ok;
 };
@@ -337,14 +331,15 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     if (tid == 0 && t + kTmaStages * step < total)
       tma_issue_tile(&tmap, kv, N, C, R, S, t + kTmaStages * step, sm.stage[st], &sm.bar[st]);
     if (tid < kTmaSlab) {
-      const int ch = tid, q = ch >> 2, e = ch & 3;
+      // consecutive threads read consecutive channels of each warp's partials
       const float* pmin = reinterpret_cast<const float*>(sm.s_min);
       const float* pmax = reinterpret_cast<const float*>(sm.s_max);
-      float lo = pmin[q * 4 + e], hi = pmax[q * 4 + e];
+      const int ch = tid;
+      float lo = pmin[ch], hi = pmax[ch];
 #pragma unroll
       for (int w = 1; w < kTmaWarps; ++w) {
-        lo = fminf(lo, pmin[(w * kTmaQuads + q) * 4 + e]);
-        hi = fmaxf(hi, pmax[(w * kTmaQuads + q) * 4 + e]);
+        lo = fminf(lo, pmin[w * kTmaSlab + ch]);
+        hi = fmaxf(hi, pmax[w * kTmaSlab + ch]);
       }
       float sc, zp;
       channel_params(lo, hi, &sc, &zp);
@@ -359,19 +354,14 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
       const float4 lo = reinterpret_cast<const float4*>(sm.s_lo)[cq];
       const float4 sc = reinterpret_cast<const float4*>(sm.s_sc)[cq];
       const float4 rc = reinterpret_cast<const float4*>(sm.s_rc)[cq];
+      // the 16 threads of a row write its 32 code bytes: one full sector
 #pragma unroll
       for (int k = 0; k < kTmaRowsPerThread; ++k) {
         const int r = rg + k * kTmaRowGroups;
         if (r < rows)
-          *reinterpret_cast<uint16_t*>(sm.s_out + r * kOutRowBytes + cq * 2) = pack4(vals[k], lo, sc, rc);
+          *reinterpret_cast<uint16_t*>(oc.packed + ((size_t)(r0 + r) * C + slab_c0) / 2 + cq * 2) =
+              pack4(vals[k], lo, sc, rc);
       }
-    }
-    __syncthreads();
-    // codes out: two 16-byte stores per row; C % 64 == 0 keeps them aligned
-    for (int idx = tid; idx < rows * (kOutRowBytes / 16); idx += blockDim.x) {
-      const int r = idx >> 1, part = idx & 1;
-      *reinterpret_cast<uint4*>(oc.packed + ((size_t)(r0 + r) * C + slab_c0) / 2 + part * 16) =
-          *reinterpret_cast<const uint4*>(sm.s_out + r * kOutRowBytes + part * 16);
     }
   }
 }
