@@ -159,6 +159,18 @@ I4KV_DEVINL uint32_t quant_code_rcp(float x, float mn, float scale, float rcp) {
   return static_cast<uint32_t>(__float_as_int(t) - 0x4B400000) & 15u;
 }
 
+// Three-input float32 min / max (sm_100), with fminf / fmaxf semantics.
+I4KV_DEVINL float fmin3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+I4KV_DEVINL float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Paired IEEE float32 arithmetic (sm_100 f32x2 instructions, round to
 // nearest even, subnormals kept): two lanes of work per instruction.
 #define I4KV_F32X2_OP(name, op)                                                               \
@@ -200,7 +212,7 @@ I4KV_DEVINL uint32_t pack4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
   const uint32_t x = __byte_perm(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040),
                                  __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040),
                                  0x5410);                       // bytes c0, c1, c2, c3
-  const uint32_t y = (x | (x >> 4)) & 0x00FF00FFu;              // c0|c1<<4, ., c2|c3<<4, .
+  const uint32_t y = x | (x >> 4);                              // c0|c1<<4, ., c2|c3<<4, .
   return __byte_perm(y, 0u, 0x4420);                            // [c0|c1<<4][c2|c3<<4]
 }
 

@@ -273,10 +273,13 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     }
   }
   __syncthreads();
+  // tile t = g * S + slab, walked incrementally (no division per tile)
+  const int step_g = (int)(step / S), step_s = (int)(step - (long long)step_g * S);
+  int g = (int)(first / S), slab = (int)(first - (long long)g * S);
+  int st = 0;
+  uint32_t parity = 0;
   long long i = 0;
   for (long long t = first; t < total; t += step, ++i) {
-    const int st = (int)(i % kTmaStages);
-    const uint32_t parity = (uint32_t)((i / kTmaStages) & 1);
     if (tid == 0) sm.ok = mbar_wait_bounded(&sm.bar[st], parity, kQuantWaitNs) ? 1 : 0;
     __syncthreads();
     if (!sm.ok) {
@@ -296,20 +299,35 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
       return;
     }
     (void)mbar_try_wait(&sm.bar[st], parity);  // completed: acquire for this thread too
-    const int g = (int)(t / S), slab = (int)(t - (long long)g * S);
     const int r0 = g * R, rows = min(R, N - r0);
     const int slab_c0 = slab * kTmaSlab;
     const float* tile = sm.stage[st];
 
     float4 vals[kTmaRowsPerThread];
-    float4 mn = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
-    float4 mx = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    float4 mn, mx;
+    if (rows == kTileRows) {  // full tile: three-input min / max over the 4 rows
+      static_assert(kTmaRowsPerThread == 4, "min3/max3 pairing");
 #pragma unroll
-    for (int k = 0; k < kTmaRowsPerThread; ++k) {
-      const int r = rg + k * kTmaRowGroups;
-      if (r < rows) {
-        vals[k] = reinterpret_cast<const float4*>(tile + r * kTmaSlab)[cq];
-        minmax4(vals[k], mn, mx);
+      for (int k = 0; k < kTmaRowsPerThread; ++k)
+        vals[k] = reinterpret_cast<const float4*>(tile + (rg + k * kTmaRowGroups) * kTmaSlab)[cq];
+      mn.x = fmin3f(fmin3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, INFINITY);
+      mn.y = fmin3f(fmin3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, INFINITY);
+      mn.z = fmin3f(fmin3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, INFINITY);
+      mn.w = fmin3f(fmin3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, INFINITY);
+      mx.x = fmax3f(fmax3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, -INFINITY);
+      mx.y = fmax3f(fmax3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, -INFINITY);
+      mx.z = fmax3f(fmax3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, -INFINITY);
+      mx.w = fmax3f(fmax3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, -INFINITY);
+    } else {
+      mn = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+      mx = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+      for (int k = 0; k < kTmaRowsPerThread; ++k) {
+        const int r = rg + k * kTmaRowGroups;
+        if (r < rows) {
+          vals[k] = reinterpret_cast<const float4*>(tile + r * kTmaSlab)[cq];
+          minmax4(vals[k], mn, mx);
+        }
       }
     }
     // fold the warp's two row groups (lanes l and l ^ 16 hold the same quad)
@@ -363,6 +381,10 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
               pack4(vals[k], lo, sc, rc);
       }
     }
+    g += step_g;
+    slab += step_s;
+    if (slab >= S) { slab -= S; ++g; }
+    if (++st == kTmaStages) { st = 0; parity ^= 1u; }
   }
 }
 
