@@ -88,11 +88,18 @@ def profile_traffic():
 
 
 def workload_config(shape, name, world):
+    lens = shape.seq_lens
+    if min(lens) == max(lens):
+        tokens = f"{lens[0]} tokens"
+        seq_len = lens[0]
+    else:
+        tokens = f"{min(lens)}..{max(lens)} tokens (mean {sum(lens) / len(lens):.0f}, ragged)"
+        seq_len = {"min": min(lens), "max": max(lens), "mean": round(sum(lens) / len(lens), 1)}
     return {"workload": f"{name}: decode step, batch {shape.batch} x {shape.heads} heads x "
-                        f"d{shape.head_dim} x {shape.seq_lens[0]} tokens per GPU, 16-token pages "
+                        f"d{shape.head_dim} x {tokens} per GPU, 16-token pages "
                         "(seeded random block table), INT4 keys / 128-token groups, fp32 q and values",
             "batch_per_gpu": shape.batch, "global_batch": shape.batch * world,
-            "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": shape.seq_lens[0],
+            "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": seq_len,
             "page_tokens": 16, "group_tokens": shape.group_tokens,
             "l2": "flushed (256 MiB write + 256 MiB read, untimed) before every timed step; inputs "
                   f"{shape.algorithmic_bytes() / 1e6:.1f} MB/GPU > 126 MB L2",
@@ -368,7 +375,7 @@ def run_ours(args):
     total_bytes = bytes_step * world
     value = total_bytes / (mean_step * 1e-3) / 1e9
     achieved = bytes_step / (mean_kern * 1e-3) / 1e9
-    traffic = profile_traffic()
+    traffic = profile_traffic() if args.config == "cfg0" else None
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": K, "warmup": Wm, "ms_per_step": round(mean_step, 5), "higher_is_better": True,
@@ -379,7 +386,8 @@ def run_ours(args):
         "hbm_frac_of_peak": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "paged_decode_kernel<128,4,2> (decode + fused combine)", "kernel_us": round(mean_kern * 1e3, 2),
+                     "kernel": f"paged_decode_kernel<{d},4,2> (decode + fused combine)",
+                     "kernel_us": round(mean_kern * 1e3, 2),
                      "algorithmic_bytes_per_launch": bytes_step,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
                      "measured" else "fallback 6.65 TB/s"},
