@@ -216,11 +216,48 @@ class SequenceSplitDecoder:
                                  workspace=self.workspace)
         return self.partials
 
-    def decode(self, query: torch.Tensor, seq_id: int = 0) -> torch.Tensor:
-        """query [1, H, D] float32 on this rank's GPU -> [1, H, D] on every rank."""
+    def _step(self, query: torch.Tensor, seq_id: int) -> torch.Tensor:
         parts = self.local_partials(query, seq_id)
-        if self.monitor is not None:
-            self.monitor.check()
         gathered = exchange_partials(parts, self.world, self.group)
         return _C.merge_partials(gathered, self.cache.heads, self.cache.head_dim).view(
             1, self.cache.heads, self.cache.head_dim)
+
+    def decode(self, query: torch.Tensor, seq_id: int = 0) -> torch.Tensor:
+        """query [1, H, D] float32 on this rank's GPU -> [1, H, D] on every rank."""
+        if self.monitor is not None:
+            self.monitor.check()
+        return self._step(query, seq_id)
+
+    # ---- CUDA graph of the whole step ----
+    graph = None
+
+    def capture(self, query: torch.Tensor, seq_id: int = 0, warmup: int = 2) -> torch.Tensor:
+        """Record one step (partial decode -> all-gather -> merge) as a CUDA graph.
+
+        ``query`` becomes the graph's input buffer: copy each new query into it
+        and call ``replay()``, which returns the (static) output tensor. Every
+        rank must capture, and release the graph (``release()``) before the
+        process group is destroyed.
+        """
+        side = torch.cuda.Stream(device=query.device)
+        side.wait_stream(torch.cuda.current_stream(query.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._step(query, seq_id)
+        torch.cuda.current_stream(query.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.graph_out = self._step(query, seq_id)
+        return self.graph_out
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        if self.monitor is not None:
+            self.monitor.check()
+        self.graph.replay()
+        return self.graph_out
+
+    def release(self) -> None:
+        self.graph = None
+        self.graph_out = None

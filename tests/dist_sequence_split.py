@@ -51,10 +51,18 @@ def main():
     full.write_sequences([0], [k], [v])
     want = full.decode(q, [0])
     err = float((out - want).abs().max())
-    ok = torch.tensor([1.0 if err <= 2e-6 and bool(torch.isfinite(out).all()) else 0.0],
+    # the same step as a CUDA graph, replayed on a new query written into its input buffer
+    dec.capture(q)
+    q.copy_(torch.randn((1, heads, d), generator=g, device="cuda"))
+    got = dec.replay().clone()
+    gerr = float((got - full.decode(q, [0])).abs().max())
+    dec.release()
+    torch.cuda.synchronize()
+    ok = torch.tensor([1.0 if max(err, gerr) <= 2e-6 and bool(torch.isfinite(out).all()) else 0.0],
                       device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    print(f"rank {rank}: range [{t0}, {t1}) max|split - whole| = {err:.3e}", flush=True)
+    print(f"rank {rank}: range [{t0}, {t1}) max|split - whole| = {err:.3e}, graph replay {gerr:.3e}",
+          flush=True)
     good = bool(ok.item() == 1.0)
     dist.destroy_process_group()
     sys.exit(0 if good else 1)
