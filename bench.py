@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: fused INT4 paged flash-decode attention on B200 (+ quantizer GB/s).
 
-One step = one decode-attention pass of BASELINE config 0 per GPU
+One step = one decode-attention pass of benchmark config 0 per GPU
 (8 sequences x 32 heads x d128 x 2048 tokens, 16-token pages in a seeded
 random block table, INT4 keys with per-(128-token group, head, channel)
 scale/zp, fp32 values), inputs resident in HBM. With N GPUs every rank owns
@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-quantizer", action="store_true")
+    ap.add_argument("--values", default="f32", choices=["f32", "f16", "bf16"],
+                    help="value-pool storage type (keys are INT4 either way)")
     return ap.parse_args()
 
 
@@ -97,7 +99,8 @@ def workload_config(shape, name, world):
         seq_len = {"min": min(lens), "max": max(lens), "mean": round(sum(lens) / len(lens), 1)}
     return {"workload": f"{name}: decode step, batch {shape.batch} x {shape.heads} heads x "
                         f"d{shape.head_dim} x {tokens} per GPU, 16-token pages "
-                        "(seeded random block table), INT4 keys / 128-token groups, fp32 q and values",
+                        "(seeded random block table), INT4 keys / 128-token groups, fp32 q, "
+                        f"{'fp32' if shape.value_bytes == 4 else '16-bit'} values",
             "batch_per_gpu": shape.batch, "global_batch": shape.batch * world,
             "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": seq_len,
             "page_tokens": 16, "group_tokens": shape.group_tokens,
@@ -228,21 +231,25 @@ def run_ours(args):
     lib = importlib.import_module(PKG + "._lib").load()
 
     shape = W.config_shape(args.config)
-    prob = W.torch_build_cache(shape, seed=7 + 1000 * rank)
+    vdtype = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.values]
+    shape.value_bytes = 4 if args.values == "f32" else 2
+    prob = W.torch_build_cache(shape, seed=7 + 1000 * rank, value_dtype=vdtype)
     cache, query = prob["cache"], prob["query"]
     ids = list(range(shape.batch))
     bt, sl = cache.block_table(ids)
     d, h = shape.head_dim, shape.heads
     out = torch.empty_like(query)
-    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, h, h, d)
+    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, h, h, d, value_dtype=vdtype)
+    vk = C.VALUE_KINDS[vdtype]
     ws = torch.zeros((ws_bytes,), dtype=torch.uint8, device="cuda")  # zero-filled once
     stream = torch.cuda.current_stream()
     maxp, npages = bt.shape[1], cache.num_pages
 
     def call_args(q_ptr, out_ptr, ev0=None, ev1=None):
-        return (q_ptr, cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), cache.sz_pool.data_ptr(),
-                bt.data_ptr(), sl.data_ptr(), shape.batch, h, h, d, 16, shape.group_tokens, maxp,
-                npages, out_ptr, ws.data_ptr(), ws_bytes, None, stream.cuda_stream, ev0, ev1)
+        return (q_ptr, cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), vk,
+                cache.sz_pool.data_ptr(), bt.data_ptr(), sl.data_ptr(), shape.batch, h, h, d, 16,
+                shape.group_tokens, maxp, npages, out_ptr, ws.data_ptr(), ws_bytes, None,
+                stream.cuda_stream, ev0, ev1)
 
     # correctness gate before timing: a sample of streams against the float64 arbiter
     C.paged_decode(query, cache.k_pool, cache.v_pool, cache.sz_pool, bt, sl, shape.group_tokens,
@@ -250,7 +257,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     import oracle
     host = {"query": query.cpu().numpy(), "k_pool": cache.k_pool.cpu().numpy(),
-            "v_pool": cache.v_pool.cpu().numpy(), "sz_pool": cache.sz_pool.cpu().numpy(),
+            "v_pool": cache.v_pool.float().cpu().numpy(), "sz_pool": cache.sz_pool.cpu().numpy(),
             "block_table": bt.cpu().numpy(), "seq_lens": sl.cpu().numpy()}
     rng = np.random.default_rng(rank)
     gate_streams = [(int(b), int(hh)) for b, hh in zip(rng.integers(0, shape.batch, 4),
@@ -271,7 +278,7 @@ def run_ours(args):
         for x in e:
             x.record()
     torch.cuda.synchronize()
-    fn = lib.int4kv_paged_decode_profiled
+    fn = lib.int4kv_paged_decode_ex
     for i in range(Wm):
         flush(i)
         rc = fn(*call_args(query.data_ptr(), out.data_ptr()))
@@ -317,7 +324,7 @@ def run_ours(args):
 
     def e2e_args():
         a = list(call_args(q_dev.data_ptr(), out.data_ptr()))
-        a[4], a[5] = bt_dev.data_ptr(), sl_dev.data_ptr()
+        a[5], a[6] = bt_dev.data_ptr(), sl_dev.data_ptr()
         return a
 
     ea = e2e_args()
@@ -340,7 +347,7 @@ def run_ours(args):
     if not torch.equal(out_host, out.cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident output")
 
-    # ---- quantizer GB/s, rank-local ----
+    # ---- quantizer GB/s (benchmark config 1), rank-local ----
     quant = None
     if not args.no_quantizer:
         quant = {}
@@ -379,7 +386,8 @@ def run_ours(args):
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": K, "warmup": Wm, "ms_per_step": round(mean_step, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (fp64 logits), int4 keys",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": f"fp32 (fp64 logits), int4 keys, {args.values} values",
         "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
         "config": workload_config(shape, args.config, world),
         "decode_us": round(mean_step * 1e3, 2),

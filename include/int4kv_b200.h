@@ -30,6 +30,13 @@ extern "C" {
 static constexpr int kMaxPagedBatch = INT4KV_MAX_PAGED_BATCH;
 #endif
 
+/* Storage type of the value pool (v_pool) of the *_ex entry points. The
+ * reference's vLLM shim stores values as float16 (src/vllm_integration.py:55);
+ * the decode widens 16-bit values to float32 exactly on load. */
+#define INT4KV_VALUES_F32 0
+#define INT4KV_VALUES_F16 1
+#define INT4KV_VALUES_BF16 2
+
 /* Status bits a kernel ORs into the optional `status` word when it had to
  * defend itself against malformed device-resident metadata. */
 #define INT4KV_STATUS_BAD_PAGE 1u      /* block-table entry outside [0, num_pages) */
@@ -72,7 +79,7 @@ cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const fl
                                 size_t workspace_bytes, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
- * Grouped quantizer: per-(group, head, channel) scale and
+ * Grouped quantizer (benchmark config 1): per-(group, head, channel) scale and
  * zero-point, two codes per byte. Replaces the per-block calls of
  * quantize_int4_ref + pack_int4 the reference makes in its vLLM shim
  * (src/vllm_integration.py:48-56) and benchmarks
@@ -145,6 +152,31 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream, cudaEvent_t ev_before,
                                          cudaEvent_t ev_after);
+
+/* int4kv_paged_decode_workspace_size / int4kv_paged_decode_profiled with the
+ * value pool stored as `value_dtype` (INT4KV_VALUES_*): v_pool is then
+ * [num_pages, num_kv_heads, page_tokens, head_dim] of that type. Halving the
+ * value bytes halves most of the decode's HBM traffic. No counterpart in the
+ * reference's kernels (float32 values only); its vLLM shim keeps float16. */
+cudaError_t int4kv_paged_decode_workspace_size_ex(int batch, int num_q_heads, int num_kv_heads,
+                                                  int head_dim, int value_dtype, size_t* bytes);
+cudaError_t int4kv_paged_decode_ex(const float* query, const uint8_t* k_pool, const void* v_pool,
+                                   int value_dtype, const float* sz_pool,
+                                   const int32_t* block_table, const int32_t* seq_lens, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim,
+                                   int page_tokens, int group_tokens, int max_pages, int num_pages,
+                                   float* out, void* workspace, size_t workspace_bytes,
+                                   uint32_t* status, cudaStream_t stream, cudaEvent_t ev_before,
+                                   cudaEvent_t ev_after);
+
+/* int4kv_cache_write with the values converted (round to nearest even) to
+ * `value_dtype` as they are stored; v_pool as in int4kv_paged_decode_ex. */
+cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t* tok_offsets,
+                                  const int32_t* start_pos, int batch, int max_rows_per_seq,
+                                  int num_heads, int head_dim, int group_tokens, int page_tokens,
+                                  const int32_t* block_table, int max_pages, int num_pages,
+                                  uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
+                                  uint32_t* status, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Sequence split across GPUs (one long sequence, tokens partitioned into

@@ -9,7 +9,7 @@ validation order and the same keywords in the ``RuntimeError`` messages
 allocator on the input's device; launches go on torch's current stream.
 
 The paged entry points (``quantize_int4_grouped``, ``cache_write``,
-``paged_decode``) are new: they serve the BASELINE paged-cache configurations.
+``paged_decode``) are new: they serve the benchmark paged-cache configurations.
 
 Nothing here computes on the CPU: a missing library raises.
 """
@@ -20,6 +20,9 @@ from . import _lib
 
 MAX_HEAD_DIM = 256
 PAGE_TOKENS = 16
+
+#: value-pool dtypes of the paged path -> INT4KV_VALUES_* (include/int4kv_b200.h)
+VALUE_KINDS = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 
 def _stream(t):
@@ -164,9 +167,9 @@ def _check_pools(k_pool, v_pool, sz_pool):
     d = 2 * half
     if v_pool is not None:
         _check_input(v_pool, "v_pool")
-        if v_pool.dtype != torch.float32 or tuple(v_pool.shape) != (num_pages, hkv, page, d):
-            raise RuntimeError("v_pool must be float32 [num_pages, kv_heads, page, head_dim] "
-                               "matching k_pool")
+        if v_pool.dtype not in VALUE_KINDS or tuple(v_pool.shape) != (num_pages, hkv, page, d):
+            raise RuntimeError("v_pool must be float32, float16 or bfloat16 "
+                               "[num_pages, kv_heads, page, head_dim] matching k_pool")
     if sz_pool.dtype != torch.float32 or tuple(sz_pool.shape) != (num_pages, hkv, 2, d):
         raise RuntimeError("sz_pool must be float32 [num_pages, kv_heads, 2, head_dim] matching k_pool")
     return num_pages, hkv, page, d
@@ -207,21 +210,24 @@ def cache_write(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, max_row
     if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
         raise RuntimeError("status must be an int32 tensor")
     _same_device(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, start_pos, status)
+    vk = VALUE_KINDS[v_pool.dtype] if v_pool is not None else 0
     with torch.cuda.device(k.device):
-        _lib.check(lib.int4kv_cache_write(_p(k), _p(v), _p(tok_offsets), _p(start_pos), batch,
-                                          int(max_rows_per_seq), hkv, d, group_tokens, page,
-                                          _p(block_table), max_pages, num_pages, _p(k_pool),
-                                          _p(v_pool), _p(sz_pool), _p(status), _stream(k)),
+        _lib.check(lib.int4kv_cache_write_ex(_p(k), _p(v), _p(tok_offsets), _p(start_pos), batch,
+                                             int(max_rows_per_seq), hkv, d, group_tokens, page,
+                                             _p(block_table), max_pages, num_pages, _p(k_pool),
+                                             _p(v_pool), vk, _p(sz_pool), _p(status), _stream(k)),
                    "cache_write")
 
 
-def paged_decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, device=None):
+def paged_decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, device=None,
+                                 value_dtype=torch.float32):
     import ctypes
     lib = _lib.load()
     need = ctypes.c_size_t(0)
     with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
-        _lib.check(lib.int4kv_paged_decode_workspace_size(batch, q_heads, kv_heads, head_dim,
-                                                          ctypes.byref(need)),
+        _lib.check(lib.int4kv_paged_decode_workspace_size_ex(batch, q_heads, kv_heads, head_dim,
+                                                             VALUE_KINDS[value_dtype],
+                                                             ctypes.byref(need)),
                    "paged_decode_workspace_size")
     return need.value
 
@@ -255,17 +261,19 @@ def paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, group_to
             out = torch.empty((b, hq, d), dtype=torch.float32, device=query.device)
         elif out.dtype != torch.float32 or tuple(out.shape) != (b, hq, d) or not out.is_contiguous():
             raise RuntimeError("out must be contiguous float32 [batch, heads, head_dim]")
-        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device)
+        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device, v_pool.dtype)
         if workspace is None:
             # zero-filled once; every completed launch leaves it zero-filled again
             workspace = torch.zeros((need,), dtype=torch.uint8, device=query.device)
         elif workspace.numel() * workspace.element_size() < need:
             raise RuntimeError(f"workspace needs {need} bytes")
-        _lib.check(lib.int4kv_paged_decode(_p(query), _p(k_pool), _p(v_pool), _p(sz_pool),
-                                           _p(block_table), _p(seq_lens), b, hq, hkv, d, page,
-                                           group_tokens, max_pages, num_pages, _p(out),
-                                           _p(workspace), workspace.numel() * workspace.element_size(),
-                                           _p(status), _stream(query)),
+        _lib.check(lib.int4kv_paged_decode_ex(_p(query), _p(k_pool), _p(v_pool),
+                                              VALUE_KINDS[v_pool.dtype], _p(sz_pool),
+                                              _p(block_table), _p(seq_lens), b, hq, hkv, d, page,
+                                              group_tokens, max_pages, num_pages, _p(out),
+                                              _p(workspace),
+                                              workspace.numel() * workspace.element_size(),
+                                              _p(status), _stream(query), None, None),
                    "paged_decode")
     return out
 
@@ -280,8 +288,8 @@ def paged_decode_partials(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
     """
     lib = _lib.load()
     num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
-    if v_pool is None:
-        raise RuntimeError("v_pool is required")
+    if v_pool is None or v_pool.dtype != torch.float32:
+        raise RuntimeError("paged_decode_partials needs a float32 v_pool")
     _check_input(query, "query")
     if query.dtype != torch.float32 or query.dim() != 3:
         raise RuntimeError("query must be float32 [batch, heads, head_dim]")

@@ -11,7 +11,7 @@ Modules:
   vllm_integration  -- the reference's INT4PagedKVCache shim, device-resident
   int4_pack         -- host view of the nibble-packed storage format
   parallel          -- multi-GPU sharding and the sequence-split merge
-  workloads         -- seeded synthetic inputs of the BASELINE configurations
+  workloads         -- seeded synthetic inputs of the benchmark configurations
 
 The package directory name is not a Python identifier; import it with
 ``importlib.import_module("int4-kv-cache-quantization-cuda-triton-pallas_b200")``.

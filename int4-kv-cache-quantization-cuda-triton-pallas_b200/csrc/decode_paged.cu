@@ -32,6 +32,8 @@
 // (exact dequantization); softmax weights are float32 exponentials, values are
 // summed per page in float32 and across pages in float32 with Kahan
 // compensation; partials are merged in float64.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -48,14 +50,21 @@ constexpr int kPage = 16;
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of wall time
 
-template <int D, int WARPS, int STAGES>
+// Value storage kinds (INT4KV_VALUES_*): 0 float32, 1 float16, 2 bfloat16.
+template <int VK>
+struct ValueKind {
+  static constexpr int BYTES = VK == 0 ? 4 : 2;
+};
+
+template <int D, int WARPS, int STAGES, int VK = 0>
 struct Cfg {
+  static constexpr int VB = ValueKind<VK>::BYTES;  // bytes per stored value
   static constexpr int LPT = D / 16;         // lanes per token in the logit phase (16 dims each)
   static constexpr int TPP = 32 / LPT;       // tokens per pass
   static constexpr int NJ = kPage / TPP;     // passes per page
   static constexpr int DPL = D / 32;         // value dims per lane in the P.V phase
   static constexpr int V_OFF = 0;
-  static constexpr int K_OFF = kPage * D * 4;
+  static constexpr int K_OFF = kPage * D * VB;
   static constexpr int SZ_OFF = K_OFF + kPage * D / 2;
   static constexpr int Q_OFF = SZ_OFF + 2 * D * 4;
   static constexpr int STAGE_BYTES = Q_OFF + D * 4;
@@ -79,7 +88,7 @@ __host__ __device__ inline size_t pfx_bytes(int batch) { return ((size_t)(batch 
 struct DecodeArgs {
   const float* q;
   const uint8_t* k_pool;
-  const float* v_pool;
+  const void* v_pool;  // float32 / float16 / bfloat16 [pages, heads, 16, D]
   const float* sz_pool;
   const int32_t* block_table;
   const int32_t* seq_lens;
@@ -180,22 +189,23 @@ __device__ __forceinline__ Desc shfl_desc(const Desc& d, int src) {
   return o;
 }
 
-template <int D, int WARPS, int STAGES>
+template <int D, int WARPS, int STAGES, int VK>
 __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, char* slot,
                                            uint64_t* bar) {
-  using C = Cfg<D, WARPS, STAGES>;
+  using C = Cfg<D, WARPS, STAGES, VK>;
   const int ntok = d.meta & 0xff;
   const bool has_q = (d.meta >> 8) & 1, has_sz = (d.meta >> 9) & 1;
   const int h = d.meta >> 16;
   uint32_t bytes = 0;
-  if (ntok) bytes += (uint32_t)ntok * (D * 4 + D / 2);
+  if (ntok) bytes += (uint32_t)ntok * (D * C::VB + D / 2);
   if (has_sz) bytes += 2 * D * 4;
   if (has_q) bytes += D * 4;
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (ntok) {
     const size_t ph = (size_t)d.phys * a.heads + h;
-    bulk_g2s(slot + C::V_OFF, a.v_pool + ph * kPage * D, (uint32_t)ntok * D * 4, bar);
+    bulk_g2s(slot + C::V_OFF, static_cast<const char*>(a.v_pool) + ph * kPage * D * C::VB,
+             (uint32_t)ntok * D * C::VB, bar);
     bulk_g2s(slot + C::K_OFF, a.k_pool + ph * kPage * (D / 2), (uint32_t)ntok * (D / 2), bar);
   }
   if (has_sz) {
@@ -251,22 +261,54 @@ __device__ __forceinline__ void kahan_rescale_add(float& sum, float& c, float r,
   sum = t;
 }
 
-// ps += p[t] * V[t, lane's dims] (lane layout of store_lane_vec).
-template <int D>
-__device__ __forceinline__ void pv_row(const float* vs, float pt, int t, int lane, float* ps) {
+// Two 16-bit stored values (one 32-bit word, low half first) widened to
+// float32 exactly.
+template <int VK>
+__device__ __forceinline__ float2 widen2(uint32_t w) {
+  if constexpr (VK == 1) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  } else {  // bfloat16: the float32 with the same top 16 bits
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  }
+}
+
+// ps += p[t] * V[t, lane's dims] (lane layout of store_lane_vec); V rows are
+// stored as float32 (VK 0) or as 16-bit floats widened on load (VK 1, 2).
+template <int D, int VK>
+__device__ __forceinline__ void pv_row(const char* vs, float pt, int t, int lane, float* ps) {
   constexpr int DPL = D / 32;
-  if constexpr (DPL == 2) {
-    const float2 v = *reinterpret_cast<const float2*>(vs + t * D + 2 * lane);
-    ps[0] = fmaf(pt, v.x, ps[0]);
-    ps[1] = fmaf(pt, v.y, ps[1]);
-  } else {
+  if constexpr (VK == 0) {
+    const float* row = reinterpret_cast<const float*>(vs) + t * D;
+    if constexpr (DPL == 2) {
+      const float2 v = *reinterpret_cast<const float2*>(row + 2 * lane);
+      ps[0] = fmaf(pt, v.x, ps[0]);
+      ps[1] = fmaf(pt, v.y, ps[1]);
+    } else {
 #pragma unroll
-    for (int v4 = 0; v4 < DPL / 4; ++v4) {
-      const float4 v = *reinterpret_cast<const float4*>(vs + t * D + v4 * 128 + 4 * lane);
-      ps[4 * v4 + 0] = fmaf(pt, v.x, ps[4 * v4 + 0]);
-      ps[4 * v4 + 1] = fmaf(pt, v.y, ps[4 * v4 + 1]);
-      ps[4 * v4 + 2] = fmaf(pt, v.z, ps[4 * v4 + 2]);
-      ps[4 * v4 + 3] = fmaf(pt, v.w, ps[4 * v4 + 3]);
+      for (int v4 = 0; v4 < DPL / 4; ++v4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + v4 * 128 + 4 * lane);
+        ps[4 * v4 + 0] = fmaf(pt, v.x, ps[4 * v4 + 0]);
+        ps[4 * v4 + 1] = fmaf(pt, v.y, ps[4 * v4 + 1]);
+        ps[4 * v4 + 2] = fmaf(pt, v.z, ps[4 * v4 + 2]);
+        ps[4 * v4 + 3] = fmaf(pt, v.w, ps[4 * v4 + 3]);
+      }
+    }
+  } else {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(vs) + t * D;
+    if constexpr (DPL == 2) {
+      const float2 v = widen2<VK>(*reinterpret_cast<const uint32_t*>(row + 2 * lane));
+      ps[0] = fmaf(pt, v.x, ps[0]);
+      ps[1] = fmaf(pt, v.y, ps[1]);
+    } else {
+#pragma unroll
+      for (int v4 = 0; v4 < DPL / 4; ++v4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(row + v4 * 128 + 4 * lane);
+        const float2 lo = widen2<VK>(w.x), hi = widen2<VK>(w.y);
+        ps[4 * v4 + 0] = fmaf(pt, lo.x, ps[4 * v4 + 0]);
+        ps[4 * v4 + 1] = fmaf(pt, lo.y, ps[4 * v4 + 1]);
+        ps[4 * v4 + 2] = fmaf(pt, hi.x, ps[4 * v4 + 2]);
+        ps[4 * v4 + 3] = fmaf(pt, hi.y, ps[4 * v4 + 3]);
+      }
     }
   }
 }
@@ -281,10 +323,10 @@ __device__ __forceinline__ float exp_neg(double x) {
   return r;
 }
 
-template <int D, int WARPS, int STAGES>
+template <int D, int WARPS, int STAGES, int VK>
 __global__ void __launch_bounds__(WARPS * 32)
 paged_decode_kernel(DecodeArgs a) {
-  using C = Cfg<D, WARPS, STAGES>;
+  using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
   extern __shared__ __align__(128) char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // WARPS*STAGES
@@ -336,7 +378,7 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
   for (int i = 0; i < STAGES; ++i) {  // prologue: the first STAGES pages (all in chunk 0)
     const Desc d = shfl_desc(cur, i);
-    if (lane == 0 && i < n) issue_page<D, WARPS, STAGES>(a, d, ring + i * C::STAGE_BYTES, &bar[i]);
+    if (lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * C::STAGE_BYTES, &bar[i]);
   }
 
   float q16[16];     // this lane's 16 query dims [16c, 16c+16)
@@ -646,7 +688,7 @@ paged_decode_kernel(DecodeArgs a) {
       __syncwarp();
 
       // ---- P.V over the page's valid rows (float32 page sum, Kahan into the run) ----
-      const float* vs = reinterpret_cast<const float*>(slot + C::V_OFF);
+      const char* vs = slot + C::V_OFF;
       float ps[DPL];
 #pragma unroll
       for (int k = 0; k < DPL; ++k) ps[k] = 0.f;
@@ -654,15 +696,15 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
         for (int t4 = 0; t4 < kPage / 4; ++t4) {
           const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
-          pv_row<D>(vs, pt.x, 4 * t4 + 0, lane, ps);
-          pv_row<D>(vs, pt.y, 4 * t4 + 1, lane, ps);
-          pv_row<D>(vs, pt.z, 4 * t4 + 2, lane, ps);
-          pv_row<D>(vs, pt.w, 4 * t4 + 3, lane, ps);
+          pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps);
+          pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, ps);
+          pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps);
+          pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps);
         }
       } else {
 #pragma unroll
         for (int t = 0; t < kPage; ++t)
-          if (t < ntok) pv_row<D>(vs, p_tab[t], t, lane, ps);
+          if (t < ntok) pv_row<D, VK>(vs, p_tab[t], t, lane, ps);
       }
 #pragma unroll
       for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[k], acc_c[k], 1.f, ps[k]);
@@ -673,7 +715,7 @@ paged_decode_kernel(DecodeArgs a) {
     if (nx < n) {
       const int src = nx & 31;
       const Desc dn = (nx >> 5) == (i >> 5) ? shfl_desc(cur, src) : shfl_desc(nxt, src);
-      if (lane == 0) issue_page<D, WARPS, STAGES>(a, dn, slot, &bar[st]);
+      if (lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
     }
   }
 
@@ -737,36 +779,37 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, 
 constexpr int kWarps = I4KV_DECODE_WARPS;    // warps per CTA
 constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 
-template <int D>
+template <int D, int VK>
 size_t dyn_smem(int batch) {
-  return 256 + pfx_bytes(batch) + (size_t)kWarps * Cfg<D, kWarps, kStages>::WARP_BYTES;
+  return 256 + pfx_bytes(batch) + (size_t)kWarps * Cfg<D, kWarps, kStages, VK>::WARP_BYTES;
 }
 
 struct OccCache {
   std::mutex mu;
-  int dev[16] = {};
-  int d[16] = {};
-  size_t smem[16] = {};
-  int grid[16] = {};
+  int dev[32] = {};
+  int key[32] = {};  // D * 4 + value kind
+  size_t smem[32] = {};
+  int grid[32] = {};
   int n = 0;
 };
 OccCache g_occ;
 
-template <int D>
+template <int D, int VK>
 cudaError_t decode_grid(int batch, int* grid_out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const size_t smem = dyn_smem<D>(batch);
+  const size_t smem = dyn_smem<D, VK>(batch);
+  const int key = D * 4 + VK;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
     for (int i = 0; i < g_occ.n; ++i)
-      if (g_occ.dev[i] == dev && g_occ.d[i] == D && g_occ.smem[i] == smem) {
+      if (g_occ.dev[i] == dev && g_occ.key[i] == key && g_occ.smem[i] == smem) {
         *grid_out = g_occ.grid[i];
         return cudaSuccess;
       }
   }
-  auto kern = paged_decode_kernel<D, kWarps, kStages>;
+  auto kern = paged_decode_kernel<D, kWarps, kStages, VK>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0, sms = 0;
@@ -778,8 +821,8 @@ cudaError_t decode_grid(int batch, int* grid_out) {
   const int grid = per_sm * sms;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
-    if (g_occ.n < 16) {
-      g_occ.dev[g_occ.n] = dev; g_occ.d[g_occ.n] = D; g_occ.smem[g_occ.n] = smem;
+    if (g_occ.n < 32) {
+      g_occ.dev[g_occ.n] = dev; g_occ.key[g_occ.n] = key; g_occ.smem[g_occ.n] = smem;
       g_occ.grid[g_occ.n] = grid; ++g_occ.n;
     }
   }
@@ -787,40 +830,62 @@ cudaError_t decode_grid(int batch, int* grid_out) {
   return cudaSuccess;
 }
 
-template <int D>
+template <int D, int VK>
 cudaError_t ws_size(int batch, int heads, size_t* out) {
   int grid = 0;
-  cudaError_t e = decode_grid<D>(batch, &grid);
+  cudaError_t e = decode_grid<D, VK>(batch, &grid);
   if (e != cudaSuccess) return e;
   const long long streams = (long long)batch * heads;
   const size_t nrec = (size_t)grid * kWarps + (size_t)streams;
-  *out = cnt_bytes(streams) + nrec * Cfg<D, kWarps, kStages>::REC_BYTES;
+  *out = cnt_bytes(streams) + nrec * Cfg<D, kWarps, kStages, VK>::REC_BYTES;
   return cudaSuccess;
 }
 
-template <int D>
+template <int D, int VK>
 cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
                    cudaEvent_t ev_before, cudaEvent_t ev_after) {
   int grid = 0;
-  cudaError_t e = decode_grid<D>(a.batch, &grid);
+  cudaError_t e = decode_grid<D, VK>(a.batch, &grid);
   if (e != cudaSuccess) return e;
   size_t need = 0;
-  e = ws_size<D>(a.batch, a.heads, &need);
+  e = ws_size<D, VK>(a.batch, a.heads, &need);
   if (e != cudaSuccess) return e;
   if (ws_bytes < need) return cudaErrorInvalidValue;
   if (ev_before && (e = cudaEventRecord(ev_before, stream)) != cudaSuccess) return e;
-  paged_decode_kernel<D, kWarps, kStages><<<grid, kWarps * 32, dyn_smem<D>(a.batch), stream>>>(a);
+  paged_decode_kernel<D, kWarps, kStages, VK>
+      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch), stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 
+template <int D>
+cudaError_t launch_kind(int vk, const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
+                        cudaEvent_t ev_before, cudaEvent_t ev_after) {
+  switch (vk) {
+    case INT4KV_VALUES_F32: return launch<D, 0>(a, ws_bytes, stream, ev_before, ev_after);
+    case INT4KV_VALUES_F16: return launch<D, 1>(a, ws_bytes, stream, ev_before, ev_after);
+    case INT4KV_VALUES_BF16: return launch<D, 2>(a, ws_bytes, stream, ev_before, ev_after);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int D>
+cudaError_t ws_size_kind(int vk, int batch, int heads, size_t* out) {
+  switch (vk) {
+    case INT4KV_VALUES_F32: return ws_size<D, 0>(batch, heads, out);
+    case INT4KV_VALUES_F16: return ws_size<D, 1>(batch, heads, out);
+    case INT4KV_VALUES_BF16: return ws_size<D, 2>(batch, heads, out);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Argument checks shared by the decode entry points, then the launch. Exactly
 // one of `out` (normalized outputs) and `part_out` (partial records) is used.
-cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const float* v_pool,
+cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v_pool, int vk,
                         const float* sz_pool, const int32_t* block_table, const int32_t* seq_lens,
                         int batch, int num_q_heads, int num_kv_heads, int head_dim,
                         int page_tokens, int group_tokens, int max_pages, int num_pages,
@@ -842,9 +907,9 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const float* 
                max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status,
                part_out};
   switch (head_dim) {
-    case 64: return launch<64>(a, workspace_bytes, stream, ev_before, ev_after);
-    case 128: return launch<128>(a, workspace_bytes, stream, ev_before, ev_after);
-    case 256: return launch<256>(a, workspace_bytes, stream, ev_before, ev_after);
+    case 64: return launch_kind<64>(vk, a, workspace_bytes, stream, ev_before, ev_after);
+    case 128: return launch_kind<128>(vk, a, workspace_bytes, stream, ev_before, ev_after);
+    case 256: return launch_kind<256>(vk, a, workspace_bytes, stream, ev_before, ev_after);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -858,11 +923,37 @@ cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int n
   if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads) return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size<64>(batch, num_kv_heads, bytes);
-    case 128: return ws_size<128>(batch, num_kv_heads, bytes);
-    case 256: return ws_size<256>(batch, num_kv_heads, bytes);
+    case 64: return ws_size<64, 0>(batch, num_kv_heads, bytes);
+    case 128: return ws_size<128, 0>(batch, num_kv_heads, bytes);
+    case 256: return ws_size<256, 0>(batch, num_kv_heads, bytes);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t int4kv_paged_decode_workspace_size_ex(int batch, int num_q_heads, int num_kv_heads,
+                                                  int head_dim, int value_dtype, size_t* bytes) {
+  if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads) return cudaErrorInvalidValue;
+  if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
+  switch (head_dim) {
+    case 64: return ws_size_kind<64>(value_dtype, batch, num_kv_heads, bytes);
+    case 128: return ws_size_kind<128>(value_dtype, batch, num_kv_heads, bytes);
+    case 256: return ws_size_kind<256>(value_dtype, batch, num_kv_heads, bytes);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t int4kv_paged_decode_ex(const float* query, const uint8_t* k_pool, const void* v_pool,
+                                   int value_dtype, const float* sz_pool,
+                                   const int32_t* block_table, const int32_t* seq_lens, int batch,
+                                   int num_q_heads, int num_kv_heads, int head_dim,
+                                   int page_tokens, int group_tokens, int max_pages, int num_pages,
+                                   float* out, void* workspace, size_t workspace_bytes,
+                                   uint32_t* status, cudaStream_t stream, cudaEvent_t ev_before,
+                                   cudaEvent_t ev_after) {
+  return paged_entry(query, k_pool, v_pool, value_dtype, sz_pool, block_table, seq_lens, batch,
+                     num_q_heads, num_kv_heads, head_dim, page_tokens, group_tokens, max_pages,
+                     num_pages, out, nullptr, workspace, workspace_bytes, status, stream,
+                     ev_before, ev_after);
 }
 
 cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_pool,
@@ -874,7 +965,8 @@ cudaError_t int4kv_paged_decode_profiled(const float* query, const uint8_t* k_po
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream, cudaEvent_t ev_before,
                                          cudaEvent_t ev_after) {
-  return paged_entry(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch, num_q_heads,
+  return paged_entry(query, k_pool, v_pool, INT4KV_VALUES_F32, sz_pool, block_table, seq_lens,
+                     batch, num_q_heads,
                      num_kv_heads, head_dim, page_tokens, group_tokens, max_pages, num_pages, out,
                      nullptr, workspace, workspace_bytes, status, stream, ev_before, ev_after);
 }
@@ -888,7 +980,8 @@ cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_po
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream) {
   if (!partials) return cudaErrorInvalidValue;
-  return paged_entry(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch, num_q_heads,
+  return paged_entry(query, k_pool, v_pool, INT4KV_VALUES_F32, sz_pool, block_table, seq_lens,
+                     batch, num_q_heads,
                      num_kv_heads, head_dim, page_tokens, group_tokens, max_pages, num_pages,
                      nullptr, static_cast<char*>(partials), workspace, workspace_bytes, status,
                      stream, nullptr, nullptr);

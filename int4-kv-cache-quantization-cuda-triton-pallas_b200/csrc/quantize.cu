@@ -23,6 +23,8 @@
 //                            shared memory, so no global scratch is needed.
 #include <cooperative_groups.h>
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -59,7 +61,8 @@ struct OutPaged {
   const int32_t* block_table;// [B, max_pages]
   int max_pages, page, num_pages, heads, head_dim;
   uint8_t* k_pool;           // [num_pages, H, page, D/2]
-  float* v_pool;             // [num_pages, H, page, D]
+  void* v_pool;              // [num_pages, H, page, D] of value kind `vk`
+  int vk;                    // INT4KV_VALUES_*
   float* sz_pool;            // [num_pages, H, 2, D]
   uint32_t* status;          // nullable
 };
@@ -193,7 +196,22 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
         if (op.v) {
           const float4 vv =
               __ldg(reinterpret_cast<const float4*>(op.v + (size_t)(row_base + r0 + r) * C + c0));
-          *reinterpret_cast<float4*>(op.v_pool + ph * op.head_dim + d) = vv;
+          const size_t vi = ph * op.head_dim + d;
+          if (op.vk == INT4KV_VALUES_F32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(op.v_pool) + vi) = vv;
+          } else if (op.vk == INT4KV_VALUES_F16) {
+            const __half2 a = __floats2half2_rn(vv.x, vv.y), b = __floats2half2_rn(vv.z, vv.w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&a);
+            w.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(static_cast<__half*>(op.v_pool) + vi) = w;
+          } else {
+            const __nv_bfloat162 a = __floats2bfloat162_rn(vv.x, vv.y), b = __floats2bfloat162_rn(vv.z, vv.w);
+            uint2 w;
+            w.x = *reinterpret_cast<const uint32_t*>(&a);
+            w.y = *reinterpret_cast<const uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(op.v_pool) + vi) = w;
+          }
         }
       }
     }
@@ -622,15 +640,18 @@ cudaError_t int4kv_quantize_grouped(const float* kv, int num_tokens, int num_hea
   return cudaGetLastError();
 }
 
-cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* tok_offsets,
-                               const int32_t* start_pos, int batch, int max_rows_per_seq,
-                               int num_heads, int head_dim, int group_tokens, int page_tokens,
-                               const int32_t* block_table, int max_pages, int num_pages,
-                               uint8_t* k_pool, float* v_pool, float* sz_pool, uint32_t* status,
-                               cudaStream_t stream) {
+cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t* tok_offsets,
+                                  const int32_t* start_pos, int batch, int max_rows_per_seq,
+                                  int num_heads, int head_dim, int group_tokens, int page_tokens,
+                                  const int32_t* block_table, int max_pages, int num_pages,
+                                  uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
+                                  uint32_t* status, cudaStream_t stream) {
   if (batch <= 0 || max_rows_per_seq < 0 || num_heads <= 0 || head_dim <= 0) return cudaErrorInvalidValue;
   if (head_dim % 4 != 0 || page_tokens <= 0 || group_tokens <= 0) return cudaErrorInvalidValue;
   if (group_tokens % page_tokens != 0 || group_tokens > kRegGroupMax) return cudaErrorInvalidValue;
+  if (value_dtype != INT4KV_VALUES_F32 && value_dtype != INT4KV_VALUES_F16 &&
+      value_dtype != INT4KV_VALUES_BF16)
+    return cudaErrorInvalidValue;
   if (!k || !tok_offsets || !block_table || !k_pool || !sz_pool || !aligned16(k)) return cudaErrorInvalidValue;
   if (v && (!v_pool || !aligned16(v) || !aligned16(v_pool))) return cudaErrorInvalidValue;
   if (max_pages <= 0 || num_pages <= 0 || batch > 65535) return cudaErrorInvalidValue;
@@ -641,10 +662,22 @@ cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* to
   if (groups > 65535) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((C + kSlab - 1) / kSlab), groups, batch);
   OutPaged op{v, tok_offsets, start_pos, block_table, max_pages, page_tokens, num_pages,
-              num_heads, head_dim, k_pool, v_pool, sz_pool, status};
+              num_heads, head_dim, k_pool, v_pool, value_dtype, sz_pool, status};
   grouped_quant_kernel<true><<<grid, kQuantThreads, 0, stream>>>(k, max_rows_per_seq, (int)C,
                                                                   group_tokens, OutContig{}, op);
   return cudaGetLastError();
+}
+
+cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* tok_offsets,
+                               const int32_t* start_pos, int batch, int max_rows_per_seq,
+                               int num_heads, int head_dim, int group_tokens, int page_tokens,
+                               const int32_t* block_table, int max_pages, int num_pages,
+                               uint8_t* k_pool, float* v_pool, float* sz_pool, uint32_t* status,
+                               cudaStream_t stream) {
+  return int4kv_cache_write_ex(k, v, tok_offsets, start_pos, batch, max_rows_per_seq, num_heads,
+                               head_dim, group_tokens, page_tokens, block_table, max_pages,
+                               num_pages, k_pool, v_pool, INT4KV_VALUES_F32, sz_pool, status,
+                               stream);
 }
 
 }  // extern "C"

@@ -4,7 +4,7 @@ Same entry points, argument meaning and return types as the reference
 (src/ops.py:86-344): ``quantize_int4``, ``flash_decode``,
 ``prepare_quantize_int4_cuda``, ``prepare_flash_decode_cuda``,
 ``backend_status``, the backend tuples, ``CUDA_MAX_HEAD_DIM`` and the
-``HAS_*`` flags. Plus the paged-cache operators the BASELINE configurations
+``HAS_*`` flags. Plus the paged-cache operators the benchmark configurations
 need: ``quantize_int4_grouped``, ``flash_decode_paged`` and their
 ``prepare_*`` forms.
 
@@ -192,7 +192,7 @@ def prepare_flash_decode_cuda(query, k_q_blocks, k_scales, k_zps, v_blocks,
 
 
 # --------------------------------------------------------------------------
-# paged attention (per-(sequence, kv-head) streams, BASELINE configs 0/2/3/4)
+# paged attention (per-(sequence, kv-head) streams, benchmark configs 0/2/3/4)
 # --------------------------------------------------------------------------
 
 def prepare_flash_decode_paged(query, k_pool, v_pool, sz_pool, block_table, seq_lens,

@@ -5,7 +5,7 @@ lists done on every call (src/ops.py:293-308) and the dict-of-pages cache of
 the vLLM shim (src/vllm_integration.py:42-60). Everything lives in HBM:
 
   k_pool  uint8   [num_pages, kv_heads, 16, head_dim/2]  nibble-packed keys
-  v_pool  float32 [num_pages, kv_heads, 16, head_dim]    values
+  v_pool  float32 / float16 / bfloat16 [num_pages, kv_heads, 16, head_dim] values
   sz_pool float32 [num_pages, kv_heads, 2, head_dim]     [scale; zp] of the
           128-token group whose first token lives in this page
 
@@ -28,7 +28,7 @@ PAGE_TOKENS = 16
 class PagedKVCache:
     def __init__(self, num_pages: int, num_kv_heads: int, head_dim: int,
                  group_tokens: int = 128, device="cuda", seed: Optional[int] = None,
-                 values: bool = True):
+                 values: bool = True, value_dtype=torch.float32):
         if head_dim % 4:
             raise ValueError(f"head_dim must be a multiple of 4, got {head_dim}")
         if group_tokens % PAGE_TOKENS or group_tokens <= 0 or group_tokens > 128:
@@ -40,8 +40,11 @@ class PagedKVCache:
         self.device = torch.device(device)
         self.k_pool = torch.zeros((num_pages, num_kv_heads, PAGE_TOKENS, head_dim // 2),
                                   dtype=torch.uint8, device=self.device)
+        if value_dtype not in _C.VALUE_KINDS:
+            raise ValueError(f"value_dtype must be one of {list(_C.VALUE_KINDS)}")
+        self.value_dtype = value_dtype
         self.v_pool = (torch.zeros((num_pages, num_kv_heads, PAGE_TOKENS, head_dim),
-                                   dtype=torch.float32, device=self.device) if values else None)
+                                   dtype=value_dtype, device=self.device) if values else None)
         self.sz_pool = torch.zeros((num_pages, num_kv_heads, 2, head_dim), dtype=torch.float32,
                                    device=self.device)
         order = (np.random.default_rng(seed).permutation(num_pages) if seed is not None

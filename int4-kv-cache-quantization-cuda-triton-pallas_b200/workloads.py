@@ -1,7 +1,7 @@
-"""Seeded synthetic inputs with the BASELINE configurations' shapes and distributions.
+"""Seeded synthetic inputs with the benchmark configurations' shapes and distributions.
 
 The reference measures on synthetic data too (benchmarks/bench_three_backend.py:113-129);
-these generators produce the anchor distribution of the BASELINE configs:
+these generators produce the anchor distribution of the benchmark configs:
 
 * query ~ N(0, 1)
 * keys ~ N(0, 1) * scale_c + offset_c per (sequence, head, channel), with
@@ -49,6 +49,7 @@ class DecodeShape:
     seq_lens: List[int]
     pool_pages: int
     group_tokens: int = 128
+    value_bytes: int = 4  # 4 float32, 2 float16 / bfloat16 value pool
 
     @property
     def pages(self):
@@ -56,19 +57,19 @@ class DecodeShape:
 
     def algorithmic_bytes(self):
         """Bytes a decode step must move: valid-token K (packed) + V + per-group scale/zp
-        + query + output + block-table entries (SURVEY 8(d) byte model)."""
+        + query + output + block-table entries."""
         d = self.head_dim
         total = 0
         for n in self.seq_lens:
             groups = (n + self.group_tokens - 1) // self.group_tokens
             pages = (n + PAGE_TOKENS - 1) // PAGE_TOKENS
-            total += self.heads * (n * d // 2 + 4 * n * d + 8 * d * groups) + 4 * pages
+            total += self.heads * (n * d // 2 + self.value_bytes * n * d + 8 * d * groups) + 4 * pages
         total += 2 * 4 * self.batch * self.heads * d
         return total
 
 
 def config_shape(name: str, seed: int = 0) -> DecodeShape:
-    """The decode configurations of BASELINE.json (per GPU)."""
+    """The decode configurations of the benchmark definition (per GPU)."""
     if name == "cfg0":
         return DecodeShape(8, 32, 128, [2048] * 8, pool_pages=8 * 128)
     if name.startswith("cfg2_"):
@@ -88,7 +89,7 @@ def config_shape(name: str, seed: int = 0) -> DecodeShape:
     raise ValueError(f"unknown config {name}")
 
 
-def torch_build_cache(shape: DecodeShape, seed: int = 0, device="cuda"):
+def torch_build_cache(shape: DecodeShape, seed: int = 0, device="cuda", value_dtype=None):
     """Build a full-size paged problem in HBM with the GPU quantizer.
 
     Returns dict(query, cache) where cache is a ``paged.PagedKVCache`` holding
@@ -101,7 +102,8 @@ def torch_build_cache(shape: DecodeShape, seed: int = 0, device="cuda"):
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     cache = PagedKVCache(shape.pool_pages, shape.heads, shape.head_dim, shape.group_tokens,
-                         device=device, seed=seed)
+                         device=device, seed=seed,
+                         value_dtype=value_dtype if value_dtype is not None else torch.float32)
     h, d = shape.heads, shape.head_dim
     for b, n in enumerate(shape.seq_lens):
         if n == 0:

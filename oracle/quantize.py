@@ -4,7 +4,7 @@ Restates ``src/quantize_int4_ref.py`` of the reference:
 
 * ``quantize_int4``   -- ``quantize_int4_ref`` (per_channel=True), :23-84
 * ``dequantize_int4`` -- ``dequantize_int4_ref`` (per_channel=True), :87-136
-* ``quantize_grouped`` -- the grouped driver the BASELINE configs need: the
+* ``quantize_grouped`` -- the grouped driver the benchmark configs need: the
   reference realises "per block" by calling ``quantize_int4_ref`` once per
   block on a 2-D ``[rows, head_dim]`` slice (``src/vllm_integration.py:51``,
   ``benchmarks/bench_three_backend.py:120-124``); here the block is a

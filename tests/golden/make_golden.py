@@ -16,7 +16,7 @@ mixed-magnitude inputs (:89-103, :174-201), the dispatch parity shapes
 (tests/test_int4_pack.py:33-35), ragged / empty-page attention
 (tests/test_ops_dispatch.py:245-251, tests/test_pallas_flash_decode.py:119-148),
 head_dim and page-row boundaries (tests/test_ops_dispatch.py:263-291), plus
-the BASELINE anchor distribution on the paged layout (16-token pages,
+the benchmark anchor distribution on the paged layout (16-token pages,
 128-token groups, seeded block table).
 """
 
@@ -71,7 +71,7 @@ def main():
               np.random.RandomState(shape[0]).randn(*shape).astype(np.float32))
     add_q("randn_3d", np.random.RandomState(42).randn(4, 8, 64).astype(np.float32))
 
-    # grouped (BASELINE config 1 layout): one reference call per (group, head)
+    # grouped (benchmark config 1 layout): one reference call per (group, head)
     for name, (n, h, d, seed) in {"grouped_300x4x64": (300, 4, 64, 7),
                                   "grouped_256x1x128": (256, 1, 128, 8),
                                   "grouped_77x3x32": (77, 3, 32, 9)}.items():

@@ -2,7 +2,7 @@
 
 Tolerances (float32 attention is not bit-reproducible across summation orders):
 
-* BASELINE gate: max |gpu - reference fp32 path| <= 1e-5 on every golden case
+* reference gate: max |gpu - reference fp32 path| <= 1e-5 on every golden case
   (the reference's own outputs) and every reference-distribution case.
 * Exactness gate: max |gpu - float64 arbiter| <= 1e-6. The arbiter is the
   reference's own float64 evaluation of the same mathematics
@@ -29,7 +29,7 @@ ops = pkg("ops")
 W = pkg("workloads")
 
 ATTN = golden("golden_attn")
-BASELINE_TOL = 1e-5
+REF_TOL = 1e-5
 EXACT_TOL = 1e-6
 
 
@@ -48,7 +48,7 @@ def _problem(batch=2, heads=3, dim=32, n_blocks=3, rows=64, seed=0, scale_query=
     return query, kq, ks, kz, vv
 
 
-def _check_shared(query, kq, ks, kz, vv, lens, tol=BASELINE_TOL, golden_out=None):
+def _check_shared(query, kq, ks, kz, vv, lens, tol=REF_TOL, golden_out=None):
     got = ops.flash_decode(query, kq, ks, kz, vv, lens, backend="cuda")
     pages = list(zip(kq, ks, kz))
     ref = golden_out if golden_out is not None else oracle.online_softmax(query, pages, vv, lens)[0]
@@ -149,7 +149,7 @@ def test_paged_golden(name):
     args = (c["query"], c["k_pool"], c["v_pool"], c["sz_pool"], c["block_table"], c["seq_lens"])
     got = ops.flash_decode_paged(*args)
     exact = oracle.decode_paged(*args, method="f64")
-    assert np.abs(got - c["out"]).max() <= BASELINE_TOL
+    assert np.abs(got - c["out"]).max() <= REF_TOL
     assert np.abs(got - exact).max() <= EXACT_TOL
     assert np.all(got[c["seq_lens"] == 0] == 0)
 
@@ -186,7 +186,7 @@ def test_paged_reference_distribution_meets_baseline_gate():
     pools = oracle_build_pools(prob)
     got = _paged_on_gpu(prob, pools)
     ref = oracle.decode_paged(prob["query"], *pools, prob["block_table"], prob["seq_lens"])
-    assert np.abs(got - ref).max() <= BASELINE_TOL
+    assert np.abs(got - ref).max() <= REF_TOL
 
 
 def test_paged_gpu_built_cache_end_to_end():
@@ -224,7 +224,7 @@ def test_paged_bad_page_is_flagged_not_read():
 
 
 def test_paged_full_anchor_config():
-    """BASELINE config 0 at full size (8 x 32 x d128 x 2048), GPU-built cache.
+    """benchmark config 0 at full size (8 x 32 x d128 x 2048), GPU-built cache.
 
     Checked against the float64 arbiter on a seeded sample of 24 streams, and
     all 256 outputs finite.

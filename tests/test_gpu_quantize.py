@@ -2,7 +2,7 @@
 
 Bar: codes, scales and zero-points identical to the reference's NumPy oracle
 (bit for bit -- `view(uint32)` equality), on the golden vectors, on the
-reference's own test shapes, and on BASELINE config 1 sizes. At the largest
+reference's own test shapes, and on benchmark config 1 sizes. At the largest
 sizes the whole output is checked through size-independent properties
 (per-group scale recomputed with exact device min/max, round-trip error
 bound) plus exact comparison of a seeded sample of groups.
@@ -68,7 +68,7 @@ def test_binding_rejects_bad_quantizer_input():
         C.quantize_int4(torch.zeros(4, 4))
 
 
-# ---------------- grouped, packed ----------------
+# ---------------- grouped, packed (benchmark config 1) ----------------
 
 @pytest.mark.parametrize("name", sorted(k for k in QUANT if k.startswith("grouped")))
 def test_grouped_golden(name):
@@ -97,7 +97,7 @@ def test_grouped_half_even_ties():
 
 @pytest.mark.parametrize("n_tokens", [2048, 8192, 32768, 131072])
 def test_grouped_baseline_sizes(n_tokens):
-    """[N, 32, 128], 128-token groups."""
+    """benchmark config 1: [N, 32, 128], 128-token groups."""
     h, d, group = 32, 128, 128
     g = torch.Generator(device="cuda").manual_seed(n_tokens)
     sc = torch.rand((h, d), generator=g, device="cuda") * 2.5 + 0.5
