@@ -323,8 +323,11 @@ __device__ __forceinline__ float exp_neg(double x) {
   return r;
 }
 
+// 16-bit value pools halve the stage size, so four CTAs fit an SM's shared
+// memory; registers are capped to let them all be resident (measured: 6 %
+// faster at 32K context than three CTAs with uncapped registers).
 template <int D, int WARPS, int STAGES, int VK>
-__global__ void __launch_bounds__(WARPS * 32)
+__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? 1 : 4)
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
