@@ -178,6 +178,25 @@ cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t*
                                   uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
                                   uint32_t* status, cudaStream_t stream);
 
+/* Append one token to each of `batch` sequences (a decode step's KV write).
+ * Sequence b's new token has absolute position positions[b]; its 128-token
+ * group is still open and is quantized again over its valid rows only (the
+ * reference's rule for a partial group, min/max over the rows it holds), so
+ * after any number of appends the pools equal a bulk int4kv_cache_write of the
+ * same tokens bit for bit. The float32 keys of each open group are kept in
+ * k_stage [num_slots, group_tokens, num_heads * head_dim]: stage_slots[b]
+ * names sequence b's slot, whose rows 0 .. positions[b] % group_tokens - 1
+ * must hold the group's earlier keys (this call writes the new row there).
+ * k_new / v_new [batch, num_heads, head_dim] float32 (v_new nullable); the
+ * pages of the group must already be in block_table. No counterpart in the
+ * reference (its shim writes whole blocks, src/vllm_integration.py:48-58). */
+cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const int32_t* positions,
+                                const int32_t* stage_slots, float* k_stage, int num_slots,
+                                int batch, int num_heads, int head_dim, int group_tokens,
+                                int page_tokens, const int32_t* block_table, int max_pages,
+                                int num_pages, uint8_t* k_pool, void* v_pool, int value_dtype,
+                                float* sz_pool, uint32_t* status, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Sequence split across GPUs (one long sequence, tokens partitioned into
  * 128-token-group-aligned ranges, one range per GPU). Each GPU decodes its

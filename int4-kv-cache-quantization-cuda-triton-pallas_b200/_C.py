@@ -219,6 +219,40 @@ def cache_write(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, max_row
                    "cache_write")
 
 
+def cache_append(k_new, v_new, positions, stage_slots, k_stage, block_table, k_pool, v_pool,
+                 sz_pool, group_tokens=128, status=None):
+    """Append one token per sequence (int4kv_cache_append): k_new / v_new [B, H, D]."""
+    lib = _lib.load()
+    num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
+    _check_input(k_new, "k_new")
+    if k_new.dtype != torch.float32 or k_new.dim() != 3 or tuple(k_new.shape[1:]) != (hkv, d):
+        raise RuntimeError(f"k_new must be float32 [batch, {hkv}, {d}]")
+    b = k_new.shape[0]
+    if v_new is not None:
+        _check_input(v_new, "v_new")
+        if v_new.dtype != torch.float32 or v_new.shape != k_new.shape:
+            raise RuntimeError("v_new must be float32 with the shape of k_new")
+    for t, name in ((positions, "positions"), (stage_slots, "stage_slots")):
+        _check_input(t, name)
+        if t.dtype != torch.int32 or tuple(t.shape) != (b,):
+            raise RuntimeError(f"{name} must be int32 [batch]")
+    _check_input(k_stage, "k_stage")
+    if k_stage.dtype != torch.float32 or k_stage.dim() != 3 or \
+            tuple(k_stage.shape[1:]) != (group_tokens, hkv * d):
+        raise RuntimeError(f"k_stage must be float32 [slots, {group_tokens}, {hkv * d}]")
+    max_pages = _check_table(block_table, b)
+    _same_device(k_new, v_new, positions, stage_slots, k_stage, block_table, k_pool, v_pool,
+                 sz_pool, status)
+    vk = VALUE_KINDS[v_pool.dtype] if v_pool is not None else 0
+    with torch.cuda.device(k_new.device):
+        _lib.check(lib.int4kv_cache_append(_p(k_new), _p(v_new), _p(positions), _p(stage_slots),
+                                           _p(k_stage), k_stage.shape[0], b, hkv, d, group_tokens,
+                                           page, _p(block_table), max_pages, num_pages,
+                                           _p(k_pool), _p(v_pool), vk, _p(sz_pool), _p(status),
+                                           _stream(k_new)),
+                   "cache_append")
+
+
 def paged_decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, device=None,
                                  value_dtype=torch.float32):
     import ctypes

@@ -406,6 +406,114 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
   }
 }
 
+// Token append for decode steps: sequence b adds one token at position
+// pos_b; its group (the R tokens starting at pos_b - pos_b % R) is still open,
+// so the whole group is quantized again over its valid rows only -- the
+// reference's rule for a partial group (min / max over the rows it holds) --
+// and after the last append of a group the cache equals a bulk write of the
+// same tokens bit for bit. The float32 keys of the open group live in a
+// staging slot [R, C] per sequence: rows 0 .. pos%R-1 from earlier appends
+// (or the prefill), row pos%R is the new token, written into the slot here.
+// Grid: x = 128-channel slabs, y = sequences; codes, the group's scale/zp and
+// the new value row land in the pools like grouped_quant_kernel<true>.
+struct AppendArgs {
+  const float* k_new;        // [B, C]
+  const float* v_new;        // [B, C] (nullable)
+  const int32_t* pos;        // [B] position of the new token
+  const int32_t* slot;       // [B] staging slot of each sequence
+  float* stage;              // [slots, R, C]
+  int num_slots;
+};
+
+__global__ void __launch_bounds__(kQuantThreads)
+append_quant_kernel(AppendArgs ap, int C, int R, OutPaged op) {
+  __shared__ __align__(16) float s_min[kQuantWarps * kSlab];
+  __shared__ __align__(16) float s_max[kQuantWarps * kSlab];
+  __shared__ __align__(16) float s_lo[kSlab];
+  __shared__ __align__(16) float s_sc[kSlab];
+  __shared__ __align__(16) float s_rc[kSlab];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int slab_c0 = blockIdx.x * kSlab;
+  const int c0 = slab_c0 + lane * 4;
+  const int b = blockIdx.y;
+  const int pos = ap.pos[b], sl = ap.slot[b];
+  if (pos < 0 || sl < 0 || sl >= ap.num_slots || pos / op.page >= op.max_pages) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && op.status) atomicOr(op.status, kStatusBadLength);
+    return;
+  }
+  const int rows = pos % R + 1, gpos = pos - (rows - 1);
+  const bool lane_ok = c0 < C;
+  float* stage = ap.stage + (size_t)sl * R * C;
+
+  float4 vals[kMaxRowsPerWarp];
+  float4 mn = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+  float4 mx = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+  for (int i = 0; i < kMaxRowsPerWarp; ++i) {
+    const int r = warp + i * kQuantWarps;
+    if (lane_ok && r < rows) {
+      if (r == rows - 1) {  // the new token: from the input, and into the slot
+        vals[i] = __ldg(reinterpret_cast<const float4*>(ap.k_new + (size_t)b * C + c0));
+        *reinterpret_cast<float4*>(stage + (size_t)r * C + c0) = vals[i];
+      } else {
+        vals[i] = *reinterpret_cast<const float4*>(stage + (size_t)r * C + c0);
+      }
+      minmax4(vals[i], mn, mx);
+    }
+  }
+  const int gpage = gpos / op.page;
+  const int32_t* row_bt = op.block_table + (size_t)b * op.max_pages;
+  int gslot = row_bt[gpage];
+  if (gslot < 0 || gslot >= op.num_pages) gslot = -1;
+  reduce_params(mn, mx, s_min, s_max, s_lo, s_sc, s_rc, slab_c0, C, [&](int ch, float sc, float zp) {
+    if (gslot < 0) return;
+    const int h = ch / op.head_dim, d = ch - h * op.head_dim;
+    float* dst = op.sz_pool + ((size_t)gslot * op.heads + h) * 2 * op.head_dim;
+    dst[d] = sc;
+    dst[op.head_dim + d] = zp;
+  });
+  if (gslot < 0 && threadIdx.x == 0 && op.status) atomicOr(op.status, kStatusBadPage);
+  if (!lane_ok) return;
+  const float4 lo = reinterpret_cast<const float4*>(s_lo)[lane];
+  const float4 sc = reinterpret_cast<const float4*>(s_sc)[lane];
+  const float4 rc = reinterpret_cast<const float4*>(s_rc)[lane];
+  const int h = c0 / op.head_dim, d = c0 - h * op.head_dim;
+#pragma unroll
+  for (int i = 0; i < kMaxRowsPerWarp; ++i) {
+    const int r = warp + i * kQuantWarps;
+    if (r < rows) {
+      const int p = gpos + r;
+      const int pg = p / op.page, t = p - pg * op.page;
+      const int phys = row_bt[pg];
+      if (phys < 0 || phys >= op.num_pages) {
+        if (op.status) atomicOr(op.status, kStatusBadPage);
+        continue;
+      }
+      const size_t ph = ((size_t)phys * op.heads + h) * op.page + t;
+      *reinterpret_cast<uint16_t*>(op.k_pool + ph * (op.head_dim / 2) + d / 2) = pack4(vals[i], lo, sc, rc);
+      if (r == rows - 1 && ap.v_new) {
+        const float4 vv = __ldg(reinterpret_cast<const float4*>(ap.v_new + (size_t)b * C + c0));
+        const size_t vi = ph * op.head_dim + d;
+        if (op.vk == INT4KV_VALUES_F32) {
+          *reinterpret_cast<float4*>(static_cast<float*>(op.v_pool) + vi) = vv;
+        } else if (op.vk == INT4KV_VALUES_F16) {
+          const __half2 x = __floats2half2_rn(vv.x, vv.y), y = __floats2half2_rn(vv.z, vv.w);
+          uint2 w;
+          w.x = *reinterpret_cast<const uint32_t*>(&x);
+          w.y = *reinterpret_cast<const uint32_t*>(&y);
+          *reinterpret_cast<uint2*>(static_cast<__half*>(op.v_pool) + vi) = w;
+        } else {
+          const __nv_bfloat162 x = __floats2bfloat162_rn(vv.x, vv.y), y = __floats2bfloat162_rn(vv.z, vv.w);
+          uint2 w;
+          w.x = *reinterpret_cast<const uint32_t*>(&x);
+          w.y = *reinterpret_cast<const uint32_t*>(&y);
+          *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(op.v_pool) + vi) = w;
+        }
+      }
+    }
+  }
+}
+
 // Groups longer than 128 rows: pass 1 min/max, pass 2 quantize (re-read, L2-resident).
 __global__ void __launch_bounds__(kQuantThreads)
 grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, OutContig oc) {
@@ -665,6 +773,34 @@ cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t*
               num_heads, head_dim, k_pool, v_pool, value_dtype, sz_pool, status};
   grouped_quant_kernel<true><<<grid, kQuantThreads, 0, stream>>>(k, max_rows_per_seq, (int)C,
                                                                   group_tokens, OutContig{}, op);
+  return cudaGetLastError();
+}
+
+cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const int32_t* positions,
+                                const int32_t* stage_slots, float* k_stage, int num_slots,
+                                int batch, int num_heads, int head_dim, int group_tokens,
+                                int page_tokens, const int32_t* block_table, int max_pages,
+                                int num_pages, uint8_t* k_pool, void* v_pool, int value_dtype,
+                                float* sz_pool, uint32_t* status, cudaStream_t stream) {
+  if (batch <= 0 || batch > 65535 || num_heads <= 0 || head_dim <= 0 || num_slots <= 0)
+    return cudaErrorInvalidValue;
+  if (head_dim % 4 != 0 || page_tokens <= 0 || group_tokens <= 0) return cudaErrorInvalidValue;
+  if (group_tokens % page_tokens != 0 || group_tokens > kRegGroupMax) return cudaErrorInvalidValue;
+  if (value_dtype != INT4KV_VALUES_F32 && value_dtype != INT4KV_VALUES_F16 &&
+      value_dtype != INT4KV_VALUES_BF16)
+    return cudaErrorInvalidValue;
+  if (!k_new || !positions || !stage_slots || !k_stage || !block_table || !k_pool || !sz_pool)
+    return cudaErrorInvalidValue;
+  if (!aligned16(k_new) || !aligned16(k_stage)) return cudaErrorInvalidValue;
+  if (v_new && (!v_pool || !aligned16(v_new) || !aligned16(v_pool))) return cudaErrorInvalidValue;
+  if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
+  const long long C = (long long)num_heads * head_dim;
+  if (C > (1 << 30)) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)((C + kSlab - 1) / kSlab), batch, 1);
+  AppendArgs ap{k_new, v_new, positions, stage_slots, k_stage, num_slots};
+  OutPaged op{nullptr, nullptr, nullptr, block_table, max_pages, page_tokens, num_pages,
+              num_heads, head_dim, k_pool, v_pool, value_dtype, sz_pool, status};
+  append_quant_kernel<<<grid, kQuantThreads, 0, stream>>>(ap, (int)C, group_tokens, op);
   return cudaGetLastError();
 }
 

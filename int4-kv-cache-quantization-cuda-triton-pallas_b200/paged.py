@@ -28,7 +28,7 @@ PAGE_TOKENS = 16
 class PagedKVCache:
     def __init__(self, num_pages: int, num_kv_heads: int, head_dim: int,
                  group_tokens: int = 128, device="cuda", seed: Optional[int] = None,
-                 values: bool = True, value_dtype=torch.float32):
+                 values: bool = True, value_dtype=torch.float32, max_open_sequences: int = 64):
         if head_dim % 4:
             raise ValueError(f"head_dim must be a multiple of 4, got {head_dim}")
         if group_tokens % PAGE_TOKENS or group_tokens <= 0 or group_tokens > 128:
@@ -52,6 +52,12 @@ class PagedKVCache:
         self._free: List[int] = [int(p) for p in order[::-1]]
         self.pages: Dict[int, List[int]] = {}
         self.lens: Dict[int, int] = {}
+        # float32 keys of each sequence's open (partial) group, for appends:
+        # slot [group_tokens, heads * head_dim], allocated on first need
+        self.max_open = max_open_sequences
+        self.k_stage: Optional[torch.Tensor] = None
+        self._stage_slot: Dict[int, int] = {}
+        self._stage_free: List[int] = list(range(max_open_sequences - 1, -1, -1))
 
     # ---- page allocation ----
     def _alloc(self, n: int) -> List[int]:
@@ -63,6 +69,25 @@ class PagedKVCache:
         for p in self.pages.pop(seq_id, []):
             self._free.append(p)
         self.lens.pop(seq_id, None)
+        slot = self._stage_slot.pop(seq_id, None)
+        if slot is not None:
+            self._stage_free.append(slot)
+
+    def _slot_of(self, seq_id: int) -> int:
+        if seq_id not in self._stage_slot:
+            if not self._stage_free:  # grow the staging pool (twice the slots)
+                old, n = self.k_stage, self.max_open
+                self.max_open = 2 * n
+                self.k_stage = torch.zeros((self.max_open,) + tuple(old.shape[1:]),
+                                           dtype=torch.float32, device=self.device)
+                self.k_stage[:n] = old
+                self._stage_free = list(range(self.max_open - 1, n - 1, -1))
+            if self.k_stage is None:
+                self.k_stage = torch.zeros((self.max_open, self.group_tokens,
+                                            self.heads * self.head_dim), dtype=torch.float32,
+                                           device=self.device)
+            self._stage_slot[seq_id] = self._stage_free.pop()
+        return self._stage_slot[seq_id]
 
     # ---- writes ----
     def write_sequences(self, seq_ids: Sequence[int], keys: Sequence[torch.Tensor],
@@ -91,11 +116,54 @@ class PagedKVCache:
         bt, _ = self.block_table(seq_ids)
         _C.cache_write(k, v, offs, bt, self.k_pool, self.v_pool, self.sz_pool,
                        max_rows_per_seq=max(lens), group_tokens=self.group_tokens)
+        # keep the float32 keys of each open last group, so appends can requantize it
+        for s, n, o in zip(seq_ids, lens, offs[:-1].tolist()):
+            open_rows = n % self.group_tokens
+            if open_rows:
+                slot = self._slot_of(s)
+                self.k_stage[slot, :open_rows] = k[o + n - open_rows:o + n].reshape(open_rows, -1)
+
+    def append(self, seq_ids: Sequence[int], keys: torch.Tensor,
+               values: Optional[torch.Tensor] = None) -> None:
+        """Append one token to each sequence: keys / values [B, heads, head_dim].
+
+        One kernel launch: each sequence's open 128-token group is quantized
+        again over its valid rows (the new token included), so the cache equals
+        a bulk write of the same tokens after every step. Sequences may be new
+        (length 0); a new page is taken whenever a sequence crosses a 16-token
+        boundary.
+        """
+        ids = list(seq_ids)
+        if len(set(ids)) != len(ids):
+            raise ValueError("a sequence may append only one token per call")
+        k = keys.to(self.device, torch.float32).contiguous()
+        if k.dim() != 3 or tuple(k.shape) != (len(ids), self.heads, self.head_dim):
+            raise ValueError(f"keys must be [{len(ids)}, {self.heads}, {self.head_dim}]")
+        v = None
+        if values is not None and self.v_pool is not None:
+            v = values.to(self.device, torch.float32).contiguous()
+            if v.shape != k.shape:
+                raise ValueError("values must have the shape of keys")
+        pos = []
+        for s in ids:
+            n = self.lens.setdefault(s, 0)
+            self.pages.setdefault(s, [])
+            if n % PAGE_TOKENS == 0:
+                self.pages[s].extend(self._alloc(1))
+            pos.append(n)
+        slots = [self._slot_of(s) for s in ids]
+        bt, _ = self.block_table(ids)
+        positions = torch.tensor(pos, dtype=torch.int32, device=self.device)
+        slot_t = torch.tensor(slots, dtype=torch.int32, device=self.device)
+        _C.cache_append(k, v, positions, slot_t, self.k_stage, bt, self.k_pool, self.v_pool,
+                        self.sz_pool, group_tokens=self.group_tokens)
+        for s in ids:
+            self.lens[s] += 1
 
     # ---- reads ----
     def block_table(self, seq_ids: Sequence[int]):
         """(block_table int32 [B, max_pages], seq_lens int32 [B]) on the cache's device."""
-        maxp = max(1, max(len(self.pages[s]) for s in seq_ids))
+        maxp = max([1] + [len(self.pages[s]) for s in seq_ids])
         bt = np.zeros((len(seq_ids), maxp), np.int32)
         for i, s in enumerate(seq_ids):
             bt[i, :len(self.pages[s])] = self.pages[s]
