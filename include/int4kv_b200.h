@@ -178,6 +178,25 @@ cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t*
                                   uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
                                   uint32_t* status, cudaStream_t stream);
 
+/* Shared-stream decode over a list of blocks of a vLLM-style block cache,
+ * read in place: every query of [batch_size, num_heads] attends to blocks
+ * block_ids[0 .. num_listed) of the storage, in that order. Storage, indexed
+ * by block id: k_packed uint8 [*, block_size, ceil(head_dim/2)] (two codes per
+ * byte, low nibble = even dim), k_scale / k_zp float32 [*, head_dim] (one
+ * group = the block), value [*, block_size, head_dim] of `value_dtype`,
+ * block_lens int32 [*] valid rows per block; `num_blocks` blocks in all (a
+ * listed id outside [0, num_blocks) is skipped, never read). Workspace as
+ * int4kv_dense_decode_workspace_size(batch_size, num_heads, head_dim,
+ * num_listed, block_size). Replaces the per-call host unpack + cast + gather
+ * of the reference's shim (src/vllm_integration.py:62-78) with reads of the
+ * stored bytes; same math as cu_flash_decode_int4. */
+cudaError_t int4kv_block_decode(const float* query, const uint8_t* k_packed, const float* k_scale,
+                                const float* k_zp, const void* value, int value_dtype,
+                                const int32_t* block_lens, const int32_t* block_ids,
+                                int num_listed, int num_blocks, int batch_size, int num_heads,
+                                int head_dim, int block_size, float* output, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+
 /* Append one token to each of `batch` sequences (a decode step's KV write).
  * Sequence b's new token has absolute position positions[b]; its 128-token
  * group is still open and is quantized again over its valid rows only (the

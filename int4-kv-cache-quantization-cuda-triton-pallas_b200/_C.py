@@ -219,6 +219,48 @@ def cache_write(k, v, tok_offsets, block_table, k_pool, v_pool, sz_pool, max_row
                    "cache_write")
 
 
+def block_decode(query, k_packed, k_scale, k_zp, value, block_lens, block_ids):
+    """Shared-stream decode over listed blocks of a block cache, read in place
+    (int4kv_block_decode). query [B, H, D] -> [B, H, D] float32."""
+    import ctypes
+    lib = _lib.load()
+    for t, name in ((query, "query"), (k_packed, "k_packed"), (k_scale, "k_scale"),
+                    (k_zp, "k_zp"), (value, "value"), (block_lens, "block_lens"),
+                    (block_ids, "block_ids")):
+        _check_input(t, name)
+    if query.dtype != torch.float32 or query.dim() != 3:
+        raise RuntimeError("query must be float32 [batch, heads, head_dim]")
+    b, h, d = query.shape
+    if d > MAX_HEAD_DIM:
+        raise RuntimeError(f"head_dim {d} exceeds {MAX_HEAD_DIM}")
+    if k_packed.dtype != torch.uint8 or k_packed.dim() != 3 or k_packed.shape[2] != (d + 1) // 2:
+        raise RuntimeError("k_packed must be uint8 [blocks, block_size, ceil(head_dim/2)]")
+    nblk, bs = k_packed.shape[:2]
+    if value.dtype not in VALUE_KINDS or tuple(value.shape) != (nblk, bs, d):
+        raise RuntimeError("value must be float32/float16/bfloat16 [blocks, block_size, head_dim]")
+    for t, name in ((k_scale, "k_scale"), (k_zp, "k_zp")):
+        if t.dtype != torch.float32 or tuple(t.shape) != (nblk, d):
+            raise RuntimeError(f"{name} must be float32 [blocks, head_dim]")
+    if block_lens.dtype != torch.int32 or tuple(block_lens.shape) != (nblk,):
+        raise RuntimeError("block_lens must be int32 [blocks]")
+    if block_ids.dtype != torch.int32 or block_ids.dim() != 1:
+        raise RuntimeError("block_ids must be int32 [listed]")
+    _same_device(query, k_packed, k_scale, k_zp, value, block_lens, block_ids)
+    nl = block_ids.shape[0]
+    with torch.cuda.device(query.device):
+        out = torch.empty((b, h, d), dtype=torch.float32, device=query.device)
+        need = ctypes.c_size_t(0)
+        _lib.check(lib.int4kv_dense_decode_workspace_size(b, h, d, nl, bs, ctypes.byref(need)),
+                   "dense_decode_workspace_size")
+        ws = torch.empty((max(16, need.value),), dtype=torch.uint8, device=query.device)
+        _lib.check(lib.int4kv_block_decode(_p(query), _p(k_packed), _p(k_scale), _p(k_zp),
+                                           _p(value), VALUE_KINDS[value.dtype], _p(block_lens),
+                                           _p(block_ids), nl, nblk, b, h, d, bs, _p(out), _p(ws),
+                                           ws.numel(), _stream(query)),
+                   "block_decode")
+    return out
+
+
 def cache_append(k_new, v_new, positions, stage_slots, k_stage, block_table, k_pool, v_pool,
                  sz_pool, group_tokens=128, status=None):
     """Append one token per sequence (int4kv_cache_append): k_new / v_new [B, H, D]."""

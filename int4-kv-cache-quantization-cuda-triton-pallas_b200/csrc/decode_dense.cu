@@ -18,6 +18,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "../../include/int4kv_b200.h"
 
@@ -37,17 +40,42 @@ struct DenseArgs {
   const uint8_t* kq;
   const float* ks;
   const float* kz;
-  const float* v;
+  const void* v;
   const int* lens;
   int nq, D, nb, bs, splits;
   float* out;       // final output (splits == 1)
   char* ws;         // partial records (splits > 1)
+  const int* ids;   // nullable: page pg of the stream is block ids[pg] of the storage
+  int num_blocks;   // storage blocks (ids outside [0, num_blocks) are skipped)
 };
+
+// Code of dim d in a key row: one code per byte, or two per byte (low
+// nibble = even dim) in the packed storage of the vLLM-style block cache.
+template <bool PACKED>
+__device__ __forceinline__ double key_code(const uint8_t* krow, int d) {
+  if constexpr (PACKED) {
+    return (double)((krow[d >> 1] >> ((d & 1) << 2)) & 15);
+  } else {
+    return (double)krow[d];
+  }
+}
+
+template <int VK>
+__device__ __forceinline__ float value_at(const void* vrow, int d) {
+  if constexpr (VK == 0) {
+    return static_cast<const float*>(vrow)[d];
+  } else if constexpr (VK == 1) {
+    return __half2float(static_cast<const __half*>(vrow)[d]);
+  } else {
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(vrow)[d]);
+  }
+}
 
 // Partial record: [m f64][l f32][pad][acc D f32], padded to a multiple of 16
 // bytes so every record (and its double) stays aligned for any head_dim.
 __host__ __device__ inline size_t dense_rec_bytes(int D) { return 16 + 16 * (((size_t)D + 3) / 4); }
 
+template <bool PACKED, int VK>
 __global__ void __launch_bounds__(kThreads)
 dense_decode_kernel(DenseArgs a) {
   __shared__ float s_q[kQT][kMaxD];
@@ -81,7 +109,11 @@ dense_decode_kernel(DenseArgs a) {
     for (int k = 0; k < kDPL; ++k) acc[qi][k] = 0.f;
   }
 
-  for (int pg = pb; pg < pe; ++pg) {
+  const int row_bytes = PACKED ? (D + 1) / 2 : D;
+  constexpr int VB = VK == 0 ? 4 : 2;
+  for (int pi = pb; pi < pe; ++pi) {
+    const int pg = a.ids ? a.ids[pi] : pi;  // storage block of the stream's page pi
+    if (pg < 0 || pg >= a.num_blocks) continue;  // uniform across the CTA
     __syncthreads();  // previous page's folded constants no longer in use
     for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
       const int qi = i / D, d = i - qi * D;
@@ -98,8 +130,8 @@ dense_decode_kernel(DenseArgs a) {
     }
     __syncthreads();
     const int blen = min(max(a.lens[pg], 0), a.bs);  // defence in depth, as the reference
-    const uint8_t* kpage = a.kq + (size_t)pg * a.bs * D;
-    const float* vpage = a.v + (size_t)pg * a.bs * D;
+    const uint8_t* kpage = a.kq + (size_t)pg * a.bs * row_bytes;
+    const char* vpage = static_cast<const char*>(a.v) + (size_t)pg * a.bs * D * VB;
     for (int r0 = warp * 32; r0 < blen; r0 += kThreads) {
       const int r = r0 + lane;
       const bool valid = r < blen;
@@ -107,9 +139,9 @@ dense_decode_kernel(DenseArgs a) {
 #pragma unroll
       for (int qi = 0; qi < kQT; ++qi) lg[qi] = 0.0;
       if (valid) {
-        const uint8_t* krow = kpage + (size_t)r * D;
+        const uint8_t* krow = kpage + (size_t)r * row_bytes;
         for (int d = 0; d < D; ++d) {
-          const double code = (double)krow[d];
+          const double code = key_code<PACKED>(krow, d);
 #pragma unroll
           for (int qi = 0; qi < kQT; ++qi) lg[qi] = fma(s_qs[qi][d], code, lg[qi]);
         }
@@ -133,7 +165,7 @@ dense_decode_kernel(DenseArgs a) {
         lg[qi] = p;  // reuse as this lane's probability
       }
       for (int j = 0; j < nrow; ++j) {
-        const float* vrow = vpage + (size_t)(r0 + j) * D;
+        const char* vrow = vpage + (size_t)(r0 + j) * D * VB;
         float pj[kQT];
 #pragma unroll
         for (int qi = 0; qi < kQT; ++qi) pj[qi] = __shfl_sync(kFull, (float)lg[qi], j);
@@ -141,7 +173,7 @@ dense_decode_kernel(DenseArgs a) {
         for (int k = 0; k < kDPL; ++k) {
           const int d = lane + 32 * k;
           if (d < D) {
-            const float vv = vrow[d];
+            const float vv = value_at<VK>(vrow, d);
 #pragma unroll
             for (int qi = 0; qi < kQT; ++qi) acc[qi][k] = fmaf(pj[qi], vv, acc[qi][k]);
           }
@@ -253,8 +285,8 @@ cudaError_t cu_flash_decode_int4(const float* query, const uint8_t* k_q, const f
   if (e != cudaSuccess) return e;
   const int nq = batch_size * num_heads;
   DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
-              1, output, nullptr};
-  dense_decode_kernel<<<dim3((nq + kQT - 1) / kQT, 1), kThreads, 0, stream>>>(a);
+              1, output, nullptr, nullptr, num_blocks};
+  dense_decode_kernel<false, 0><<<dim3((nq + kQT - 1) / kQT, 1), kThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -285,8 +317,44 @@ cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const fl
       return cudaErrorInvalidValue;
   }
   DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
-              splits, output, static_cast<char*>(workspace)};
-  dense_decode_kernel<<<dim3((nq + kQT - 1) / kQT, splits), kThreads, 0, stream>>>(a);
+              splits, output, static_cast<char*>(workspace), nullptr, num_blocks};
+  dense_decode_kernel<false, 0><<<dim3((nq + kQT - 1) / kQT, splits), kThreads, 0, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || splits == 1) return e;
+  dense_combine_kernel<<<nq, 128, 0, stream>>>(static_cast<const char*>(workspace), nq, head_dim,
+                                               splits, output);
+  return cudaGetLastError();
+}
+
+cudaError_t int4kv_block_decode(const float* query, const uint8_t* k_packed, const float* k_scale,
+                                const float* k_zp, const void* value, int value_dtype,
+                                const int32_t* block_lens, const int32_t* block_ids,
+                                int num_listed, int num_blocks, int batch_size, int num_heads,
+                                int head_dim, int block_size, float* output, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+  if ((!block_ids && num_listed > 0) || num_blocks < 0) return cudaErrorInvalidValue;
+  cudaError_t e = check(query, k_packed, k_scale, k_zp, static_cast<const float*>(value),
+                        block_lens, batch_size, num_heads, head_dim, num_listed, block_size,
+                        output);
+  if (e != cudaSuccess) return e;
+  if (value_dtype != INT4KV_VALUES_F32 && value_dtype != INT4KV_VALUES_F16 &&
+      value_dtype != INT4KV_VALUES_BF16)
+    return cudaErrorInvalidValue;
+  const int nq = batch_size * num_heads;
+  const int splits = choose_splits(nq, num_listed);
+  if (splits > 1) {
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
+        workspace_bytes < (size_t)nq * splits * dense_rec_bytes(head_dim))
+      return cudaErrorInvalidValue;
+  }
+  DenseArgs a{query, k_packed, k_scale, k_zp, value, block_lens, nq, head_dim, num_listed,
+              block_size, splits, output, static_cast<char*>(workspace), block_ids, num_blocks};
+  const dim3 grid((nq + kQT - 1) / kQT, splits);
+  switch (value_dtype) {
+    case INT4KV_VALUES_F32: dense_decode_kernel<true, 0><<<grid, kThreads, 0, stream>>>(a); break;
+    case INT4KV_VALUES_F16: dense_decode_kernel<true, 1><<<grid, kThreads, 0, stream>>>(a); break;
+    default: dense_decode_kernel<true, 2><<<grid, kThreads, 0, stream>>>(a); break;
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
   dense_combine_kernel<<<nq, 128, 0, stream>>>(static_cast<const char*>(workspace), nq, head_dim,

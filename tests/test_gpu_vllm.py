@@ -90,3 +90,51 @@ def test_int4_decode_close_to_fp32():
     p = np.exp(lg - lg.max(-1, keepdims=True))
     fp32 = (p @ vv) / p.sum(-1, keepdims=True)
     assert np.abs(out[0] - fp32).mean() < 0.05
+
+
+@pytest.mark.parametrize("head_dim,block_size", [(64, 256), (128, 128), (30, 48)])
+def test_append_token_equals_write_block(head_dim, block_size):
+    """A block filled token by token (each append re-quantizes the block's rows)
+    stores exactly what write_block stores for the same rows, at every length."""
+    rng = np.random.RandomState(head_dim + block_size)
+    k = rng.randn(block_size, head_dim).astype(np.float32) * 2
+    v = rng.randn(block_size, head_dim).astype(np.float32)
+    inc = V.INT4PagedKVCache(num_blocks=4, block_size=block_size, head_dim=head_dim)
+    ref = V.INT4PagedKVCache(num_blocks=4, block_size=block_size, head_dim=head_dim)
+    for n in range(block_size):
+        inc.append_token(2, k[n], v[n])
+        if n in (0, 1, 16, block_size // 2, block_size - 1):
+            ref.write_block(2, k[:n + 1], v[:n + 1])
+            for name in ("k_packed", "k_scale", "k_zp", "v"):
+                a = getattr(inc, name)[2].cpu().numpy()
+                b = getattr(ref, name)[2].cpu().numpy()
+                np.testing.assert_array_equal(a.view(np.uint8), b.view(np.uint8))
+    q = rng.randn(2, 3, head_dim).astype(np.float32)
+    np.testing.assert_array_equal(inc.decode_attention(q, [2]), ref.decode_attention(q, [2]))
+    with pytest.raises(ValueError, match="full"):
+        inc.append_token(2, k[0], v[0])
+
+
+def test_decode_reads_blocks_in_listed_order_and_skips_nothing():
+    """The in-place block decode over a permuted, repeated block list equals the
+    oracle over the same list (blocks are read where they are stored)."""
+    rng = np.random.RandomState(3)
+    d = 64
+    cache = V.INT4PagedKVCache(num_blocks=8, block_size=64, head_dim=d)
+    blocks = {}
+    for b in (5, 0, 3):
+        k = rng.randn(64 if b != 3 else 20, d).astype(np.float32)
+        v = rng.randn(*k.shape).astype(np.float32)
+        cache.write_block(b, k, v)
+        blocks[b] = (k, v)
+    table = [3, 5, 0, 5]
+    q = (rng.randn(2, 2, d) / 8).astype(np.float32)
+    got = cache.decode_attention(q, table)
+    pages, vals = [], []
+    for b in table:
+        k, v = blocks[b]
+        qk, s, z = oracle.quantize_int4(k)
+        pages.append((qk, s, z))
+        vals.append(v.astype(np.float16).astype(np.float32))
+    exact = oracle.attention_f64(q, pages, vals)
+    assert np.abs(got - exact).max() <= 1e-6
