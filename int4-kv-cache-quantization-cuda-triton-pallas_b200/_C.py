@@ -325,8 +325,8 @@ def paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, group_to
         raise RuntimeError(f"paged decode supports head_dim in (64, 128, 256), got {d}")
     if page != PAGE_TOKENS:
         raise RuntimeError(f"paged decode needs {PAGE_TOKENS}-token pages, got {page}")
-    if hq != hkv:
-        raise RuntimeError(f"query heads ({hq}) must equal kv heads ({hkv})")
+    if hq < hkv or hq % hkv:
+        raise RuntimeError(f"query heads ({hq}) must be a multiple of kv heads ({hkv})")
     max_pages = _check_table(block_table, b)
     _check_input(seq_lens, "seq_lens")
     if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,):
@@ -370,8 +370,8 @@ def paged_decode_partials(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
     if query.dtype != torch.float32 or query.dim() != 3:
         raise RuntimeError("query must be float32 [batch, heads, head_dim]")
     b, hq, qd = query.shape
-    if qd != d or hq != hkv:
-        raise RuntimeError("query must be [batch, kv_heads, pool head_dim]")
+    if qd != d or hq < hkv or hq % hkv:
+        raise RuntimeError("query must be [batch, G * kv_heads, pool head_dim]")
     max_pages = _check_table(block_table, b)
     _check_input(seq_lens, "seq_lens")
     if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,):

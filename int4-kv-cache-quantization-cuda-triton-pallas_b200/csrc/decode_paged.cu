@@ -2,9 +2,15 @@
 // is HBM-bound GEMV work, so no tensor cores).
 //
 // Semantics: the reference's online softmax (src/flash_decode_ref.py:30-139),
-// run once per (sequence b, kv head h) stream: raw logits q.k (no 1/sqrt(d)),
-// keys dequantized as code*scale - zp*scale with the scale/zp of the key's
+// run once per (sequence b, query head h) stream over the pages of kv head
+// h / G, G = query heads / kv heads (G = 1 without GQA): raw logits q.k (no
+// 1/sqrt(d)), keys dequantized as code*scale - zp*scale with the scale/zp of the key's
 // 128-token group, output o / max(l, 1e-10); empty streams give exact zeros.
+//
+// The G query streams of a kv head are adjacent in the work order, so the
+// warps running them read the same pages at about the same time (L2 serves
+// the repeats); each query stream still costs a full page pass of work, so a
+// GQA step takes the time of an MHA step with as many heads as queries.
 //
 // Work decomposition (stream-K over pages): the page-heads of all streams are
 // laid end to end in (b, h, page) order -- T of them -- and the grid's NW warps
@@ -97,6 +103,8 @@ struct DecodeArgs {
   char* ws;
   uint32_t* status;
   char* part_out;  // nullable: write per-stream partial records instead of outputs
+  int kv_heads;    // heads of the pools; `heads` (query heads, one stream each) is a
+  int group_q;     // multiple: query head h reads kv head h / group_q (GQA)
 };
 
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
@@ -203,13 +211,14 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (ntok) {
-    const size_t ph = (size_t)d.phys * a.heads + h;
+    const size_t ph = (size_t)d.phys * a.kv_heads + h / a.group_q;
     bulk_g2s(slot + C::V_OFF, static_cast<const char*>(a.v_pool) + ph * kPage * D * C::VB,
              (uint32_t)ntok * D * C::VB, bar);
     bulk_g2s(slot + C::K_OFF, a.k_pool + ph * kPage * (D / 2), (uint32_t)ntok * (D / 2), bar);
   }
   if (has_sz) {
-    bulk_g2s(slot + C::SZ_OFF, a.sz_pool + ((size_t)d.gphys * a.heads + h) * 2 * D, 2 * D * 4, bar);
+    bulk_g2s(slot + C::SZ_OFF,
+             a.sz_pool + ((size_t)d.gphys * a.kv_heads + h / a.group_q) * 2 * D, 2 * D * 4, bar);
   }
   if (has_q) bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * D, D * 4, bar);
 }
@@ -895,20 +904,21 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v
                         float* out, char* part_out, void* workspace, size_t workspace_bytes,
                         uint32_t* status, cudaStream_t stream, cudaEvent_t ev_before,
                         cudaEvent_t ev_after) {
-  if (batch <= 0 || batch > kMaxPagedBatch || num_kv_heads <= 0 || num_q_heads != num_kv_heads)
+  if (batch <= 0 || batch > kMaxPagedBatch || num_kv_heads <= 0 || num_q_heads < num_kv_heads ||
+      num_q_heads % num_kv_heads != 0)
     return cudaErrorInvalidValue;
   if (page_tokens != kPage || group_tokens <= 0 || group_tokens % kPage != 0) return cudaErrorInvalidValue;
   if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
-  if ((long long)batch * num_kv_heads * max_pages >= (1LL << 31) - 1024) return cudaErrorInvalidValue;
+  if ((long long)batch * num_q_heads * max_pages >= (1LL << 31) - 1024) return cudaErrorInvalidValue;
   if (!query || !k_pool || !v_pool || !sz_pool || !block_table || !seq_lens || !workspace)
     return cudaErrorInvalidValue;
   if (!out && !part_out) return cudaErrorInvalidValue;
   if (!al16(query) || !al16(k_pool) || !al16(v_pool) || !al16(sz_pool) || !al16(workspace))
     return cudaErrorInvalidValue;
   if ((out && !al16(out)) || (part_out && !al16(part_out))) return cudaErrorInvalidValue;
-  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_kv_heads,
+  DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_q_heads,
                max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status,
-               part_out};
+               part_out, num_kv_heads, num_q_heads / num_kv_heads};
   switch (head_dim) {
     case 64: return launch_kind<64>(vk, a, workspace_bytes, stream, ev_before, ev_after);
     case 128: return launch_kind<128>(vk, a, workspace_bytes, stream, ev_before, ev_after);
@@ -923,24 +933,28 @@ extern "C" {
 
 cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
                                                int head_dim, size_t* bytes) {
-  if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads) return cudaErrorInvalidValue;
+  if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads < num_kv_heads ||
+      num_q_heads % num_kv_heads != 0)
+    return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size<64, 0>(batch, num_kv_heads, bytes);
-    case 128: return ws_size<128, 0>(batch, num_kv_heads, bytes);
-    case 256: return ws_size<256, 0>(batch, num_kv_heads, bytes);
+    case 64: return ws_size<64, 0>(batch, num_q_heads, bytes);
+    case 128: return ws_size<128, 0>(batch, num_q_heads, bytes);
+    case 256: return ws_size<256, 0>(batch, num_q_heads, bytes);
     default: return cudaErrorInvalidValue;
   }
 }
 
 cudaError_t int4kv_paged_decode_workspace_size_ex(int batch, int num_q_heads, int num_kv_heads,
                                                   int head_dim, int value_dtype, size_t* bytes) {
-  if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads) return cudaErrorInvalidValue;
+  if (!bytes || batch <= 0 || num_kv_heads <= 0 || num_q_heads < num_kv_heads ||
+      num_q_heads % num_kv_heads != 0)
+    return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size_kind<64>(value_dtype, batch, num_kv_heads, bytes);
-    case 128: return ws_size_kind<128>(value_dtype, batch, num_kv_heads, bytes);
-    case 256: return ws_size_kind<256>(value_dtype, batch, num_kv_heads, bytes);
+    case 64: return ws_size_kind<64>(value_dtype, batch, num_q_heads, bytes);
+    case 128: return ws_size_kind<128>(value_dtype, batch, num_q_heads, bytes);
+    case 256: return ws_size_kind<256>(value_dtype, batch, num_q_heads, bytes);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1086,7 +1100,7 @@ extern "C" cudaError_t int4kv_paged_decode_static_scratch(
   void* scratch = nullptr;
   e = static_scratch_ptr(&scratch);
   if (e != cudaSuccess) return e;
-  const size_t zero_bytes = cnt_bytes((long long)batch * num_kv_heads);
+  const size_t zero_bytes = cnt_bytes((long long)batch * num_q_heads);
   e = cudaMemsetAsync(scratch, 0, zero_bytes, stream);
   if (e != cudaSuccess) return e;
   return int4kv_paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch,

@@ -70,17 +70,17 @@ def test_paged_launchers_reject_bad_sizes(lib):
     # group longer than 128 rows is not a paged-write group
     assert lib.int4kv_cache_write(n, n, n, n, 1, 16, 2, 64, 256, 16, n, 4, 4, n, n, n, n, n) \
         == CUDA_ERROR_INVALID_VALUE
-    # page size other than 16, GQA ratio other than 1
+    # page size other than 16, query heads not a multiple of kv heads
     assert lib.int4kv_paged_decode(n, n, n, n, n, n, 1, 2, 2, 128, 32, 128, 4, 4, n, n, 0, n, n) \
         == CUDA_ERROR_INVALID_VALUE
-    assert lib.int4kv_paged_decode(n, n, n, n, n, n, 1, 4, 2, 128, 16, 128, 4, 4, n, n, 0, n, n) \
+    assert lib.int4kv_paged_decode(n, n, n, n, n, n, 1, 3, 2, 128, 16, 128, 4, 4, n, n, 0, n, n) \
         == CUDA_ERROR_INVALID_VALUE
     size = ctypes.c_size_t(0)
     assert lib.int4kv_paged_decode_workspace_size(1, 2, 2, 96, ctypes.byref(size)) \
         == CUDA_ERROR_INVALID_VALUE
     # the allocation-free variant checks the same sizes before touching its scratch
     need = ctypes.c_size_t(12345)
-    assert lib.int4kv_paged_decode_static_scratch(n, n, n, n, n, n, 1, 4, 2, 128, 16, 128, 4, 4,
+    assert lib.int4kv_paged_decode_static_scratch(n, n, n, n, n, n, 1, 3, 2, 128, 16, 128, 4, 4,
                                                   n, n, ctypes.byref(need), n) \
         == CUDA_ERROR_INVALID_VALUE
     assert need.value == 12345
