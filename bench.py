@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-quantizer", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="sequence split (cfg4_long, N>1): fused peer-memory exchange kernel "
+                         "or NCCL all-gather + merge kernel")
     ap.add_argument("--values", default="f32", choices=["f32", "f16", "bf16"],
                     help="value-pool storage type (keys are INT4 either way)")
     return ap.parse_args()
@@ -498,8 +501,10 @@ def run_reference(args):
 
 def run_split(args):
     """One long sequence split across the ranks by 128-token groups; a step is
-    each rank's partial decode + one NCCL all-gather of the partial records +
-    the merge kernel. Total work is fixed as N grows (strong scaling)."""
+    each rank's partial decode + the exchange of the partial records and their
+    merge: one fused peer-memory kernel (``--exchange p2p``) or one NCCL
+    all-gather + the merge kernel (``--exchange nccl``). Total work is fixed as
+    N grows (strong scaling)."""
     import datetime
     import importlib
     import torch
@@ -526,8 +531,9 @@ def run_split(args):
     cache.write_sequences([0], [keys[t0:t1]], [vals[t0:t1]])
     store = dist.distributed_c10d._get_default_store()
     dec = par.SequenceSplitDecoder(cache, rank, world,
-                                   monitor=par.PeerMonitor(store, rank, world, timeout=60.0))
-    out = dec.decode(query)  # correctness gate: against a whole-sequence decode on rank 0
+                                   monitor=par.PeerMonitor(store, rank, world, timeout=60.0),
+                                   exchange=args.exchange)
+    out = dec.decode(query).clone()  # correctness gate: against a whole-sequence decode on rank 0
     gate = torch.zeros((1,), device="cuda")
     if rank == 0:
         whole = P.PagedKVCache((L + 15) // 16 + 8, h, d, device="cuda", seed=99)
@@ -537,6 +543,8 @@ def run_split(args):
     del keys, vals
     dist.all_reduce(gate, op=dist.ReduceOp.MAX)
     gate_err = float(gate.item())
+    if dec.peer_status():
+        raise RuntimeError(f"peer exchange reported status {dec.peer_status()}")
     if not gate_err <= 2e-6:
         raise RuntimeError(f"sequence-split decode failed its gate (max err {gate_err})")
     dec.monitor = None  # host liveness checks stay out of the timed loop
@@ -566,7 +574,12 @@ def run_split(args):
     torch.cuda.synchronize()
     mean = sum(a.elapsed_time(b) for a, b in ev) / K
     mean = _all_reduce_max(mean, world)
+    if dec.peer_status():
+        raise RuntimeError(f"peer exchange reported status {dec.peer_status()} in the timed loop")
     total = shape.algorithmic_bytes()
+    step_desc = ("partial decode kernel + fused peer-exchange/merge kernel (NVLink stores, "
+                 "flags, bounded waits; no NCCL)" if args.exchange == "p2p" else
+                 "partial decode kernel + NCCL all-gather + merge kernel")
     peak, peak_kind = measured_peak()
     value = total / (mean * 1e-3) / 1e9
     if rank == 0:
@@ -577,16 +590,17 @@ def run_split(args):
             "data": "synthetic (seeded, config-0 distributions)",
             "config": {"workload": f"{args.config}: one sequence of {L} tokens x {h} heads x d{d}, "
                                    f"split across {world} GPUs by 128-token groups; step = "
-                                   "partial decode + one NCCL all-gather + merge kernel",
+                                   + step_desc,
+                       "exchange": args.exchange,
                        "global_batch": 1, "seq_len": L, "heads": h, "head_dim": d,
                        "l2": "flushed before every timed step",
                        "parallelism": f"sequence split x{world}"},
             "hbm_frac_of_peak": round(value / world / peak, 4), "peak_source": peak_kind,
             "gpu_launches": K * 2,
-            "step": "CUDA graph: partial decode kernel + NCCL all-gather + merge kernel",
+            "step": "CUDA graph: " + step_desc,
             "parity": {"max_abs_vs_whole_sequence_decode": gate_err},
         }), flush=True)
-    dec.release()  # the graph holds an NCCL call: release it before the process group
+    dec.close()  # graph (may hold an NCCL call) and peer mappings go before the process group
     torch.cuda.synchronize()
     dist.destroy_process_group()
 

@@ -42,6 +42,7 @@ static constexpr int kMaxPagedBatch = INT4KV_MAX_PAGED_BATCH;
 #define INT4KV_STATUS_BAD_PAGE 1u      /* block-table entry outside [0, num_pages) */
 #define INT4KV_STATUS_BAD_LENGTH 2u    /* length < 0, beyond its table row, or misaligned start */
 #define INT4KV_STATUS_WAIT_TIMEOUT 4u  /* an async-copy wait hit its time limit */
+#define INT4KV_STATUS_PEER_TIMEOUT 8u  /* a peer GPU's exchange flag did not arrive in time */
 
 /* ---------------------------------------------------------------------------
  * Drop-in replacements for the reference's two C launchers.
@@ -247,6 +248,36 @@ cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_po
  * csrc/flash_decode_int4.cu:199-220), evaluated in float64. */
 cudaError_t int4kv_merge_partials(const void* partials, int num_parts, int streams, int head_dim,
                                   float* out, cudaStream_t stream);
+
+/* Fused exchange + merge over NVLink peer memory, in place of the gather and
+ * int4kv_merge_partials: each GPU stores its partial records straight into
+ * every GPU's exchange buffer, raises a per-chunk flag there (release, system
+ * scope), waits for the other GPUs' flags of the same chunk (acquire; bounded
+ * to 2 s, then INT4KV_STATUS_PEER_TIMEOUT is set in *status and the chunk's
+ * outputs are NaN) and merges as int4kv_merge_partials does.
+ * peer_bufs[r] = rank r's exchange buffer as mapped on this GPU (the own one
+ * for r == rank; int4kv_ipc_open for the others), each
+ * int4kv_exchange_bytes large, 128-byte aligned and zero-filled once before
+ * the first call. Every rank calls it once per step with the same sizes; the
+ * steps of one buffer set must be issued in the same order on every rank. */
+#define INT4KV_EXCHANGE_MAX_RANKS 8
+cudaError_t int4kv_exchange_bytes(int world, int streams, int head_dim, size_t* bytes);
+cudaError_t int4kv_exchange_merge(const void* partials, void* const* peer_bufs, int world, int rank,
+                                  int streams, int head_dim, float* out, uint32_t* status,
+                                  cudaStream_t stream);
+
+/* Exchange buffers and their CUDA IPC between the processes of one node:
+ * int4kv_exchange_alloc makes a zero-filled allocation of its own on `device`
+ * (synchronous); int4kv_ipc_handle writes INT4KV_IPC_HANDLE_BYTES opaque bytes
+ * for such an allocation (the pointer must be the allocation's start: a
+ * handle names a whole allocation); int4kv_ipc_open maps a peer's handle on
+ * the current device (peer access enabled) and int4kv_ipc_close unmaps it. */
+#define INT4KV_IPC_HANDLE_BYTES 64
+cudaError_t int4kv_exchange_alloc(int device, size_t bytes, void** ptr);
+cudaError_t int4kv_exchange_free(void* ptr);
+cudaError_t int4kv_ipc_handle(const void* dev_ptr, void* handle);
+cudaError_t int4kv_ipc_open(const void* handle, void** dev_ptr);
+cudaError_t int4kv_ipc_close(void* dev_ptr);
 
 /* Scratch capacity of int4kv_paged_decode_static_scratch, per device: a
  * file-scope device array in the library (8 MiB; enough for 8192 streams at

@@ -412,3 +412,79 @@ def merge_partials(partials, streams, head_dim, out=None):
         _lib.check(lib.int4kv_merge_partials(_p(partials), parts, streams, head_dim, _p(out),
                                              _stream(partials)), "merge_partials")
     return out
+
+
+# --------------------------------------------------------------------------
+# fused peer exchange (sequence split over NVLink peer memory)
+# --------------------------------------------------------------------------
+
+def exchange_bytes(world, streams, head_dim):
+    """Bytes of one rank's exchange buffer (int4kv_exchange_bytes)."""
+    import ctypes
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    _lib.check(lib.int4kv_exchange_bytes(world, streams, head_dim, ctypes.byref(n)), "exchange_bytes")
+    return n.value
+
+
+def exchange_alloc(device, nbytes):
+    """A zero-filled device allocation of its own (IPC-shareable); returns its address."""
+    import ctypes
+    lib = _lib.load()
+    ptr = ctypes.c_void_p(None)
+    _lib.check(lib.int4kv_exchange_alloc(int(device), int(nbytes), ctypes.byref(ptr)), "exchange_alloc")
+    return int(ptr.value)
+
+
+def exchange_free(ptr):
+    _lib.check(_lib.load().int4kv_exchange_free(ptr), "exchange_free")
+
+
+def ipc_handle(ptr):
+    """64 opaque bytes naming the allocation that starts at ``ptr``."""
+    import ctypes
+    buf = ctypes.create_string_buffer(64)
+    _lib.check(_lib.load().int4kv_ipc_handle(ptr, buf), "ipc_handle")
+    return bytes(buf.raw)
+
+
+def ipc_open(handle):
+    """Map a peer process's allocation on the current device; returns its address here."""
+    import ctypes
+    if not isinstance(handle, (bytes, bytearray)) or len(handle) != 64:
+        raise RuntimeError("an IPC handle is 64 bytes")
+    ptr = ctypes.c_void_p(None)
+    _lib.check(_lib.load().int4kv_ipc_open(bytes(handle), ctypes.byref(ptr)), "ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr):
+    _lib.check(_lib.load().int4kv_ipc_close(ptr), "ipc_close")
+
+
+def exchange_merge(partials, peer_bufs, rank, streams, head_dim, out, status=None):
+    """Push this rank's partial records to every rank's exchange buffer, wait
+    (bounded) for theirs and merge: out [streams, head_dim] float32 on every rank.
+
+    ``peer_bufs`` = addresses of the ranks' exchange buffers as mapped on this
+    GPU, in rank order (``exchange_alloc`` / ``ipc_open``).
+    """
+    import ctypes
+    lib = _lib.load()
+    _check_input(partials, "partials")
+    _check_input(out, "out")
+    _same_device(partials, out, status)
+    rec = 16 + 4 * head_dim
+    if partials.dtype != torch.uint8 or partials.numel() != streams * rec:
+        raise RuntimeError(f"partials must be uint8 [{streams} x {rec}]")
+    if out.dtype != torch.float32 or out.numel() != streams * head_dim:
+        raise RuntimeError("out must be contiguous float32 [streams, head_dim]")
+    if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
+        raise RuntimeError("status must be an int32 tensor")
+    world = len(peer_bufs)
+    arr = (ctypes.c_void_p * max(world, 1))(*[int(p) for p in peer_bufs])
+    with torch.cuda.device(partials.device):
+        _lib.check(lib.int4kv_exchange_merge(_p(partials), arr, world, rank, streams, head_dim,
+                                             _p(out), _p(status), _stream(partials)),
+                   "exchange_merge")
+    return out

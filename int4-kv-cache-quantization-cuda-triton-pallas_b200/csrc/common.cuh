@@ -20,6 +20,7 @@ enum StatusBits : uint32_t {
   kStatusBadPage = 1u << 0,     // block-table entry outside [0, num_pages)
   kStatusBadLength = 1u << 1,   // sequence length < 0 or beyond its block-table row
   kStatusWaitTimeout = 1u << 2, // an mbarrier wait hit its iteration limit
+  kStatusPeerTimeout = 1u << 3, // a peer GPU's exchange flag did not arrive in time
 };
 
 I4KV_DEVINL uint32_t smem_addr(const void* p) {
@@ -41,6 +42,18 @@ I4KV_DEVINL void fence_barrier_init() {
 // after it.
 I4KV_DEVINL void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// System-scope ordering for stores into another GPU's memory (peer mappings
+// over NVLink): release the stores before a flag, acquire after reading one.
+I4KV_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+I4KV_DEVINL void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+I4KV_DEVINL uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 I4KV_DEVINL void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -61,6 +74,35 @@ I4KV_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_addr(bar)), "r"(parity)
       : "memory");
   return done != 0;
+}
+
+// Store o[DPL] (this lane's dims of a D-vector) at dst with the P.V lane layout.
+template <int D>
+I4KV_DEVINL void store_lane_vec(float* dst, const float* o, int lane) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    *reinterpret_cast<float2*>(dst + 2 * lane) = make_float2(o[0], o[1]);
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4)
+      *reinterpret_cast<float4*>(dst + v4 * 128 + 4 * lane) =
+          make_float4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
+  }
+}
+
+template <int D>
+I4KV_DEVINL void load_lane_vec_cg(const float* src, float* o, int lane) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(src + 2 * lane));
+    o[0] = v.x; o[1] = v.y;
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + v4 * 128 + 4 * lane));
+      o[4 * v4] = v.x; o[4 * v4 + 1] = v.y; o[4 * v4 + 2] = v.z; o[4 * v4 + 3] = v.w;
+    }
+  }
 }
 
 I4KV_DEVINL uint64_t global_ns() {

@@ -230,35 +230,6 @@ __device__ __forceinline__ double code_plus16(uint32_t w, uint32_t sel) {
   return __hiloint2double((int)__byte_perm(w, 0x40000000u, 0x7044u | (sel << 8)), 0);
 }
 
-// Store o[DPL] (this lane's dims of a D-vector) at dst with the P.V lane layout.
-template <int D>
-__device__ __forceinline__ void store_lane_vec(float* dst, const float* o, int lane) {
-  constexpr int DPL = D / 32;
-  if constexpr (DPL == 2) {
-    *reinterpret_cast<float2*>(dst + 2 * lane) = make_float2(o[0], o[1]);
-  } else {
-#pragma unroll
-    for (int v4 = 0; v4 < DPL / 4; ++v4)
-      *reinterpret_cast<float4*>(dst + v4 * 128 + 4 * lane) =
-          make_float4(o[4 * v4], o[4 * v4 + 1], o[4 * v4 + 2], o[4 * v4 + 3]);
-  }
-}
-
-template <int D>
-__device__ __forceinline__ void load_lane_vec_cg(const float* src, float* o, int lane) {
-  constexpr int DPL = D / 32;
-  if constexpr (DPL == 2) {
-    const float2 v = __ldcg(reinterpret_cast<const float2*>(src + 2 * lane));
-    o[0] = v.x; o[1] = v.y;
-  } else {
-#pragma unroll
-    for (int v4 = 0; v4 < DPL / 4; ++v4) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + v4 * 128 + 4 * lane));
-      o[4 * v4] = v.x; o[4 * v4 + 1] = v.y; o[4 * v4 + 2] = v.z; o[4 * v4 + 3] = v.w;
-    }
-  }
-}
-
 // sum = sum*r + x with a running compensation term c (Kahan): the rescale
 // applies to both, the addition captures its own rounding error in c.
 __device__ __forceinline__ void kahan_rescale_add(float& sum, float& c, float r, float x) {

@@ -16,7 +16,11 @@ Two layouts, both of which keep every KV page on the GPU that owns it:
   (``int4kv_paged_decode_partials``); ONE all-gather over NCCL lands every
   rank's records in every rank's memory; ``int4kv_merge_partials`` combines
   them (the log-sum-exp merge of the reference's kernel,
-  csrc/flash_decode_int4.cu:199-220, across GPUs instead of warps).
+  csrc/flash_decode_int4.cu:199-220, across GPUs instead of warps). With
+  ``exchange="p2p"`` the gather and the merge are one kernel instead
+  (``PeerExchange``): each rank stores its records straight into every
+  rank's buffer over NVLink (CUDA IPC mappings), raises a flag per chunk of
+  streams, waits (bounded) for the peers' flags and merges.
 
 Failure detection stays on the host: ``PeerMonitor`` has every rank post a
 heartbeat key to the process group's store before each collective step and
@@ -182,6 +186,101 @@ def exchange_partials(local: torch.Tensor, world: int, group=None) -> torch.Tens
     return out.view(world, local.numel())
 
 
+# --------------------------------------------------------------------------
+# fused peer exchange (push + flag + merge in one kernel, no NCCL)
+# --------------------------------------------------------------------------
+
+EXCHANGE_MAX_RANKS = 8
+EXCHANGE_CHUNK = 8  # streams per CTA of the exchange kernel
+
+
+def _align128(x: int) -> int:
+    return (x + 127) // 128 * 128
+
+
+def exchange_layout(streams: int, head_dim: int) -> dict:
+    """Byte offsets of one rank's exchange buffer (csrc/exchange.cu):
+    ``step u32[chunks]``, ``flag u32[2][8][chunks]``, ``recs [2][8][streams]``
+    partial records. Used by tests that stand in for a peer on the host."""
+    chunks = -(-streams // EXCHANGE_CHUNK)
+    off_flag = _align128(chunks * 4)
+    off_recs = off_flag + _align128(2 * EXCHANGE_MAX_RANKS * chunks * 4)
+    rec = partial_record_bytes(head_dim)
+    return {"chunks": chunks, "off_flag": off_flag, "off_recs": off_recs, "record": rec,
+            "bytes": off_recs + 2 * EXCHANGE_MAX_RANKS * streams * rec}
+
+
+class _DeviceBytes:
+    """``__cuda_array_interface__`` of a raw device allocation (uint8)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (int(ptr), False), "version": 3}
+
+
+def device_bytes(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor viewing ``nbytes`` at device address ``ptr`` (no copy)."""
+    return torch.as_tensor(_DeviceBytes(ptr, nbytes), device=device)
+
+
+class PeerExchange:
+    """Every rank's exchange buffer, mapped on this rank's GPU over CUDA IPC.
+
+    Each rank allocates one zero-filled buffer (``int4kv_exchange_alloc``),
+    all-gathers its IPC handle over the process group (a host object
+    exchange, once), and maps the other ranks' buffers (``int4kv_ipc_open``;
+    NVLink peer access). ``merge(partials, out)`` then runs the fused
+    exchange kernel: one launch per step, no collective library call.
+    ``close()`` must be called on every rank (it synchronizes and barriers
+    before unmapping, so no peer is still writing).
+    """
+
+    def __init__(self, rank: int, world: int, streams: int, head_dim: int, device, group=None):
+        import torch.distributed as dist
+        if not 1 <= world <= EXCHANGE_MAX_RANKS:
+            raise ValueError(f"the peer exchange supports 1..{EXCHANGE_MAX_RANKS} ranks")
+        self.rank, self.world, self.group = rank, world, group
+        self.streams, self.head_dim = streams, head_dim
+        self.device = torch.device(device)
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.nbytes = _C.exchange_bytes(world, streams, head_dim)
+        self.own = _C.exchange_alloc(idx, self.nbytes)
+        self._opened = []
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, _C.ipc_handle(self.own), group=group)
+        self.ptrs = []
+        with torch.cuda.device(self.device):
+            for r in range(world):
+                if r == rank:
+                    self.ptrs.append(self.own)
+                else:
+                    ptr = _C.ipc_open(handles[r])
+                    self._opened.append(ptr)
+                    self.ptrs.append(ptr)
+        if world > 1:
+            dist.barrier(group=group)  # every buffer is mapped before the first push
+        self.status = torch.zeros((1,), dtype=torch.int32, device=self.device)
+
+    def merge(self, partials: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if self.ptrs is None:
+            raise RuntimeError("exchange closed")
+        return _C.exchange_merge(partials, self.ptrs, self.rank, self.streams, self.head_dim, out,
+                                 self.status)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        if self.ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no peer kernel is still pushing into our buffer
+        for ptr in self._opened:
+            _C.ipc_close(ptr)
+        _C.exchange_free(self.own)
+        self.ptrs, self._opened = None, []
+
+
 class SequenceSplitDecoder:
     """Decode of one long sequence whose token range is split across ranks.
 
@@ -192,7 +291,10 @@ class SequenceSplitDecoder:
     rank.
     """
 
-    def __init__(self, cache, rank: int, world: int, group=None, monitor: Optional[PeerMonitor] = None):
+    def __init__(self, cache, rank: int, world: int, group=None, monitor: Optional[PeerMonitor] = None,
+                 exchange: str = "nccl"):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.cache, self.rank, self.world, self.group = cache, rank, world, group
         self.monitor = monitor
         d, h = cache.head_dim, cache.heads
@@ -202,6 +304,11 @@ class SequenceSplitDecoder:
         self.workspace = torch.zeros((_C.paged_decode_workspace_bytes(1, h, h, d, dev),),
                                      dtype=torch.uint8, device=dev)
         self._tables = {}
+        self.exchange = exchange
+        self.peers = None
+        if exchange == "p2p":
+            self.peers = PeerExchange(rank, world, h, d, dev, group)
+            self.out = torch.empty((h, d), dtype=torch.float32, device=dev)
 
     def refresh(self) -> None:
         """Forget cached block tables (call after the cache's pages change)."""
@@ -218,6 +325,8 @@ class SequenceSplitDecoder:
 
     def _step(self, query: torch.Tensor, seq_id: int) -> torch.Tensor:
         parts = self.local_partials(query, seq_id)
+        if self.peers is not None:
+            return self.peers.merge(parts, self.out).view(1, self.cache.heads, self.cache.head_dim)
         gathered = exchange_partials(parts, self.world, self.group)
         return _C.merge_partials(gathered, self.cache.heads, self.cache.head_dim).view(
             1, self.cache.heads, self.cache.head_dim)
@@ -258,6 +367,18 @@ class SequenceSplitDecoder:
         self.graph.replay()
         return self.graph_out
 
+    def peer_status(self) -> int:
+        """INT4KV_STATUS_* bits the peer exchange raised (PEER_TIMEOUT = 8); 0 for NCCL."""
+        return int(self.peers.status.item()) if self.peers is not None else 0
+
     def release(self) -> None:
         self.graph = None
         self.graph_out = None
+
+    def close(self) -> None:
+        """Release the graph and unmap the peer buffers (every rank, before
+        ``destroy_process_group``)."""
+        self.release()
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None

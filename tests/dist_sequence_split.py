@@ -1,11 +1,12 @@
-"""Sequence split over NCCL, one process per GPU (run under torchrun).
+"""Sequence split across GPUs, one process per GPU (run under torchrun).
 
-    torchrun --nproc-per-node N --master-addr 127.0.0.1 tests/dist_sequence_split.py [L] [heads]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 tests/dist_sequence_split.py \
+        [L] [heads] [nccl|p2p]
 
 Every rank generates the same seeded sequence, keeps its group-aligned token
 range in a paged cache on its own GPU, decodes it into partial records, and
-``SequenceSplitDecoder`` all-gathers the records (one NCCL collective) and
-merges them. Each rank checks the merged output against a whole-sequence
+``SequenceSplitDecoder`` exchanges the records -- one NCCL all-gather, or the
+fused peer-memory exchange kernel (``p2p``) -- and merges them. Each rank checks the merged output against a whole-sequence
 decode on its own GPU; exit status 0 means every rank matched.
 """
 
@@ -27,6 +28,7 @@ PKG = "int4-kv-cache-quantization-cuda-triton-pallas_b200"
 def main():
     L = int(sys.argv[1]) if len(sys.argv) > 1 else 131072
     heads = int(sys.argv[2]) if len(sys.argv) > 2 else 32
+    exchange = sys.argv[3] if len(sys.argv) > 3 else "nccl"
     d = 128
     rank, world, local = (int(os.environ[k]) for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"))
     torch.cuda.set_device(local)
@@ -45,7 +47,8 @@ def main():
     cache.write_sequences([0], [k[t0:t1]], [v[t0:t1]])
     store = dist.distributed_c10d._get_default_store()
     dec = par.SequenceSplitDecoder(cache, rank, world,
-                                   monitor=par.PeerMonitor(store, rank, world, timeout=30.0))
+                                   monitor=par.PeerMonitor(store, rank, world, timeout=30.0),
+                                   exchange=exchange)
     out = dec.decode(q)
     full = P.PagedKVCache((L + 15) // 16 + 8, heads, d, device="cuda", seed=99)
     full.write_sequences([0], [k], [v])
@@ -56,13 +59,17 @@ def main():
     q.copy_(torch.randn((1, heads, d), generator=g, device="cuda"))
     got = dec.replay().clone()
     gerr = float((got - full.decode(q, [0])).abs().max())
-    dec.release()
+    # a second eager step after the replays (the exchange's step counters advance)
+    q.copy_(torch.randn((1, heads, d), generator=g, device="cuda"))
+    serr = float((dec.decode(q) - full.decode(q, [0])).abs().max())
+    status = dec.peer_status()
+    dec.close()
     torch.cuda.synchronize()
-    ok = torch.tensor([1.0 if max(err, gerr) <= 2e-6 and bool(torch.isfinite(out).all()) else 0.0],
-                      device="cuda")
+    good_rank = max(err, gerr, serr) <= 2e-6 and bool(torch.isfinite(out).all()) and status == 0
+    ok = torch.tensor([1.0 if good_rank else 0.0], device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    print(f"rank {rank}: range [{t0}, {t1}) max|split - whole| = {err:.3e}, graph replay {gerr:.3e}",
-          flush=True)
+    print(f"rank {rank} ({exchange}): range [{t0}, {t1}) max|split - whole| = {err:.3e}, "
+          f"graph replay {gerr:.3e}, next step {serr:.3e}, status {status}", flush=True)
     good = bool(ok.item() == 1.0)
     dist.destroy_process_group()
     sys.exit(0 if good else 1)

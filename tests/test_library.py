@@ -86,3 +86,23 @@ def test_paged_launchers_reject_bad_sizes(lib):
     assert need.value == 12345
     assert lib.int4kv_dense_decode_workspace_size(1, 1, 300, 1, 1, ctypes.byref(size)) \
         == CUDA_ERROR_INVALID_VALUE
+
+
+def test_exchange_layout_and_argument_checks(lib):
+    par = pkg("parallel")
+    for streams, d in [(1, 64), (20, 128), (64, 128), (9, 256), (4096, 128)]:
+        size = ctypes.c_size_t(0)
+        assert lib.int4kv_exchange_bytes(8, streams, d, ctypes.byref(size)) == 0
+        assert size.value == par.exchange_layout(streams, d)["bytes"]
+    size = ctypes.c_size_t(0)
+    assert lib.int4kv_exchange_bytes(9, 8, 128, ctypes.byref(size)) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_exchange_bytes(2, 8, 96, ctypes.byref(size)) == CUDA_ERROR_INVALID_VALUE
+    n = None
+    bufs = (ctypes.c_void_p * 2)(4096, 8192)
+    # rank outside the world, too many ranks, misaligned peer buffer
+    assert lib.int4kv_exchange_merge(n, bufs, 2, 2, 8, 128, n, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_exchange_merge(n, bufs, 9, 0, 8, 128, n, n, n) == CUDA_ERROR_INVALID_VALUE
+    odd = (ctypes.c_void_p * 2)(4096, 8200)
+    assert lib.int4kv_exchange_merge(ctypes.c_void_p(4096), odd, 2, 0, 8, 128, ctypes.c_void_p(4096),
+                                     n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_ipc_open(n, n) == CUDA_ERROR_INVALID_VALUE
