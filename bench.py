@@ -100,12 +100,15 @@ def workload_config(shape, name, world):
     else:
         tokens = f"{min(lens)}..{max(lens)} tokens (mean {sum(lens) / len(lens):.0f}, ragged)"
         seq_len = {"min": min(lens), "max": max(lens), "mean": round(sum(lens) / len(lens), 1)}
-    return {"workload": f"{name}: decode step, batch {shape.batch} x {shape.heads} heads x "
+    heads = (f"{shape.heads} heads" if shape.query_heads == shape.heads else
+             f"{shape.query_heads} query heads over {shape.heads} kv heads (GQA)")
+    return {"workload": f"{name}: decode step, batch {shape.batch} x {heads} x "
                         f"d{shape.head_dim} x {tokens} per GPU, 16-token pages "
                         "(seeded random block table), INT4 keys / 128-token groups, fp32 q, "
                         f"{'fp32' if shape.value_bytes == 4 else '16-bit'} values",
             "batch_per_gpu": shape.batch, "global_batch": shape.batch * world,
-            "heads": shape.heads, "head_dim": shape.head_dim, "seq_len": seq_len,
+            "heads": shape.query_heads, "kv_heads": shape.heads, "head_dim": shape.head_dim,
+            "seq_len": seq_len,
             "page_tokens": 16, "group_tokens": shape.group_tokens,
             "l2": "flushed (256 MiB write + 256 MiB read, untimed) before every timed step; inputs "
                   f"{shape.algorithmic_bytes() / 1e6:.1f} MB/GPU > 126 MB L2",
@@ -240,9 +243,9 @@ def run_ours(args):
     cache, query = prob["cache"], prob["query"]
     ids = list(range(shape.batch))
     bt, sl = cache.block_table(ids)
-    d, h = shape.head_dim, shape.heads
+    d, h, hq = shape.head_dim, shape.heads, shape.query_heads
     out = torch.empty_like(query)
-    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, h, h, d, value_dtype=vdtype)
+    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, hq, h, d, value_dtype=vdtype)
     vk = C.VALUE_KINDS[vdtype]
     ws = torch.zeros((ws_bytes,), dtype=torch.uint8, device="cuda")  # zero-filled once
     stream = torch.cuda.current_stream()
@@ -250,7 +253,7 @@ def run_ours(args):
 
     def call_args(q_ptr, out_ptr, ev0=None, ev1=None):
         return (q_ptr, cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), vk,
-                cache.sz_pool.data_ptr(), bt.data_ptr(), sl.data_ptr(), shape.batch, h, h, d, 16,
+                cache.sz_pool.data_ptr(), bt.data_ptr(), sl.data_ptr(), shape.batch, hq, h, d, 16,
                 shape.group_tokens, maxp, npages, out_ptr, ws.data_ptr(), ws_bytes, None,
                 stream.cuda_stream, ev0, ev1)
 
@@ -264,7 +267,7 @@ def run_ours(args):
             "block_table": bt.cpu().numpy(), "seq_lens": sl.cpu().numpy()}
     rng = np.random.default_rng(rank)
     gate_streams = [(int(b), int(hh)) for b, hh in zip(rng.integers(0, shape.batch, 4),
-                                                       rng.integers(0, h, 4))]
+                                                       rng.integers(0, hq, 4))]
     ex = oracle.decode_paged(host["query"], host["k_pool"], host["v_pool"], host["sz_pool"],
                              host["block_table"], host["seq_lens"], method="f64",
                              streams=gate_streams)

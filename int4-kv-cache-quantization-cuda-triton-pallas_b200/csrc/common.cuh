@@ -105,6 +105,25 @@ I4KV_DEVINL void load_lane_vec_cg(const float* src, float* o, int lane) {
   }
 }
 
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32; every
+// lane of each participating warp executes it): bar.sync, and the form that
+// also ORs a predicate across the participants.
+I4KV_DEVINL void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+I4KV_DEVINL bool named_bar_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 I4KV_DEVINL uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -73,7 +73,7 @@ struct Cfg {
   static constexpr int K_OFF = kPage * D * VB;
   static constexpr int SZ_OFF = K_OFF + kPage * D / 2;
   static constexpr int Q_OFF = SZ_OFF + 2 * D * 4;
-  static constexpr int STAGE_BYTES = Q_OFF + D * 4;
+  static constexpr int STAGE_BYTES = Q_OFF + D * 4;  // one query (gs == 1)
   static constexpr int P_BYTES = kPage * 4;  // per-warp softmax weights of the current page
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + P_BYTES;
   static constexpr int REC_BYTES = 16 + 4 * D;  // [m f64][l f64][acc D f32]
@@ -105,6 +105,8 @@ struct DecodeArgs {
   char* part_out;  // nullable: write per-stream partial records instead of outputs
   int kv_heads;    // heads of the pools; `heads` (query heads, one stream each) is a
   int group_q;     // multiple: query head h reads kv head h / group_q (GQA)
+  int gs;          // warps sharing one ring (query heads served per staged page)
+  int vheads;      // heads / gs: the page streams of the work decomposition
 };
 
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
@@ -152,14 +154,14 @@ struct Desc {
   int phys;   // physical page (valid when ntok > 0)
   int gphys;  // physical page holding the group's scale/zp (valid when has_sz)
   int meta;   // ntok | has_q << 8 | has_sz << 9 | h << 16
-  int stream; // b * heads + h
+  int stream; // b * vheads + h (queries stream * gs + j, j < gs, read it)
 };
 
 __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx, int g, int g0,
                                           int g1) {
   Desc d{0, 0, 0, -1};
   if (g >= g1) return d;
-  const int gq = g / a.heads;
+  const int gq = g / a.vheads;
   int lo = 0, hi = a.batch - 1;  // last b with pfx[b] <= gq
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -167,7 +169,7 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   }
   const int b = lo;
   const int np = s_pfx[b + 1] - s_pfx[b];
-  const int rem = g - a.heads * s_pfx[b];
+  const int rem = g - a.vheads * s_pfx[b];
   const int h = rem / np;
   const int p = rem - h * np;
   const int len = clamp_len(a.seq_lens[b], a.max_pages * kPage);
@@ -184,7 +186,7 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   d.gphys = gphys;
   d.meta = ((gok && pok) ? ntok : 0) | (first ? (1 << 8) : 0) | ((grp && gok) ? (1 << 9) : 0) |
            (h << 16);
-  d.stream = b * a.heads + h;
+  d.stream = b * a.vheads + h;
   return d;
 }
 
@@ -207,20 +209,22 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   uint32_t bytes = 0;
   if (ntok) bytes += (uint32_t)ntok * (D * C::VB + D / 2);
   if (has_sz) bytes += 2 * D * 4;
-  if (has_q) bytes += D * 4;
+  if (has_q) bytes += (uint32_t)a.gs * D * 4;
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (ntok) {
-    const size_t ph = (size_t)d.phys * a.kv_heads + h / a.group_q;
+    const size_t ph = (size_t)d.phys * a.kv_heads + (h * a.gs) / a.group_q;
     bulk_g2s(slot + C::V_OFF, static_cast<const char*>(a.v_pool) + ph * kPage * D * C::VB,
              (uint32_t)ntok * D * C::VB, bar);
     bulk_g2s(slot + C::K_OFF, a.k_pool + ph * kPage * (D / 2), (uint32_t)ntok * (D / 2), bar);
   }
   if (has_sz) {
     bulk_g2s(slot + C::SZ_OFF,
-             a.sz_pool + ((size_t)d.gphys * a.kv_heads + h / a.group_q) * 2 * D, 2 * D * 4, bar);
+             a.sz_pool + ((size_t)d.gphys * a.kv_heads + (h * a.gs) / a.group_q) * 2 * D, 2 * D * 4,
+             bar);
   }
-  if (has_q) bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * D, D * 4, bar);
+  if (has_q)
+    bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * D, (uint32_t)a.gs * D * 4, bar);
 }
 
 // float64 value 16 + code of the low nibble held in byte `sel` of `w`, where
@@ -319,6 +323,14 @@ paged_decode_kernel(DecodeArgs a) {
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = lane % C::LPT, tsub = lane / C::LPT;
+  // Ring groups: gs warps share one ring of STAGES * gs slots; warp gj of the
+  // group serves query head vh * gs + gj of every page the group stages
+  // (gs = 1 without GQA: one warp, one ring, one query).
+  const int gs = a.gs, gpc = WARPS / gs;
+  const int gi = warp / gs, gj = warp - gi * gs;
+  const int depth = STAGES * gs;
+  const int sb = C::Q_OFF + gs * D * 4;  // stage bytes with gs queries
+  const bool leader = gj == 0;
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
   const long long streams = (long long)a.batch * a.heads;
 
@@ -339,29 +351,27 @@ paged_decode_kernel(DecodeArgs a) {
     }
   }
 
-  const long long T = (long long)a.heads * total_pages;  // < 2^31 (checked on the host)
-  const long long NW = (long long)gridDim.x * WARPS;
-  const long long gw = (long long)blockIdx.x * WARPS + warp;
+  const long long T = (long long)a.vheads * total_pages;  // < 2^31 (checked on the host)
+  const long long NW = (long long)gridDim.x * gpc;         // ring groups in the grid
+  const long long gw = (long long)blockIdx.x * gpc + gi;
   const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
   const int n = g1 - g0;
   if (n <= 0) return;
 
-  uint64_t* bar = bars + warp * STAGES;
-  char* ring = stages + (size_t)warp * C::WARP_BYTES;
-  float* p_tab = reinterpret_cast<float*>(ring + STAGES * C::STAGE_BYTES);
-  if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bar[s], 1);
+  uint64_t* bar = bars + gi * depth;
+  char* ring = stages + (size_t)gi * depth * sb;
+  float* p_tab = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + warp * C::P_BYTES);
+  if (leader && lane == 0) {
+    for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
   }
-  __syncwarp();
+  if (gs == 1) __syncwarp(); else named_bar_sync(1 + gi, gs * 32);
 
   Desc cur = make_desc(a, s_pfx, g0 + lane, g0, g1);
   Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
-#pragma unroll
-  for (int i = 0; i < STAGES; ++i) {  // prologue: the first STAGES pages (all in chunk 0)
+  for (int i = 0; i < depth; ++i) {  // prologue: the first `depth` pages (all in chunk 0)
     const Desc d = shfl_desc(cur, i);
-    if (lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * C::STAGE_BYTES, &bar[i]);
+    if (leader && lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
   }
 
   float q16[16];     // this lane's 16 query dims [16c, 16c+16)
@@ -386,10 +396,10 @@ paged_decode_kernel(DecodeArgs a) {
   // Warps [w_lo, w_hi] whose runs touch `stream`; returns how many of them
   // hold a non-empty run (those are the stream's contributors).
   auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
-    const int b = stream / a.heads, h = stream - b * a.heads;
+    const int b = stream / a.vheads, h = stream - b * a.vheads;
     const int np = s_pfx[b + 1] - s_pfx[b];
-    const long long gs = (long long)a.heads * s_pfx[b] + (long long)h * np, ge = gs + np;
-    w_lo = ((gs + 1) * NW - 1) / T;
+    const long long gs0 = (long long)a.vheads * s_pfx[b] + (long long)h * np, ge = gs0 + np;
+    w_lo = ((gs0 + 1) * NW - 1) / T;
     w_hi = (ge * NW - 1) / T;
     return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
   };
@@ -413,18 +423,19 @@ paged_decode_kernel(DecodeArgs a) {
   // A stream this warp covered alone: write its output (or, in partial mode,
   // its record) straight from the running state.
   auto finish_alone = [&](int stream) {
+    const size_t qstream = (size_t)stream * gs + gj;
     const double lsum = lane_sum();
     float o[DPL];
     if (a.part_out) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-      put_record(a.part_out + (size_t)stream * C::REC_BYTES, m_run, lsum, o);
+      put_record(a.part_out + qstream * C::REC_BYTES, m_run, lsum, o);
       return;
     }
     const double den = fmax(lsum, 1e-10);
 #pragma unroll
     for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[k] - (double)acc_c[k]) / den);
-    store_lane_vec<D>(a.out + (size_t)stream * D, o, lane);
+    store_lane_vec<D>(a.out + qstream * D, o, lane);
   };
 
   // Merge every contributor's record of `stream` (this warp arrived last) and
@@ -445,7 +456,7 @@ paged_decode_kernel(DecodeArgs a) {
       const bool okj = lane < cnt && (all_run || (wj * T) / NW != ((wj + 1) * T) / NW);
       double mj = -INFINITY, lj = 0.0;
       if (okj) {
-        const char* r = recs + (size_t)(wj + stream) * C::REC_BYTES;
+        const char* r = recs + ((size_t)(wj + stream) * gs + gj) * C::REC_BYTES;
         mj = __ldcg(reinterpret_cast<const double*>(r));
         lj = __ldcg(reinterpret_cast<const double*>(r + 8));
       }
@@ -454,7 +465,7 @@ paged_decode_kernel(DecodeArgs a) {
       for (int j = 0; j < CH; ++j) {
         if (j < cnt) {
           load_lane_vec_cg<D>(reinterpret_cast<const float*>(
-              recs + (size_t)(base + j + stream) * C::REC_BYTES + 16), v[j], lane);
+              recs + ((size_t)(base + j + stream) * gs + gj) * C::REC_BYTES + 16), v[j], lane);
         }
       }
       double cm = mj;
@@ -481,17 +492,18 @@ paged_decode_kernel(DecodeArgs a) {
       }
       M = m_new;
     }
+    const size_t qstream = (size_t)stream * gs + gj;
     float o[DPL];
     if (a.part_out) {  // partial mode: the merged (M, L, O) of this GPU's share of the stream
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
-      put_record(a.part_out + (size_t)stream * C::REC_BYTES, M, L, o);
+      put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
       return;
     }
     const double den = fmax(L, 1e-10);
 #pragma unroll
     for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
-    store_lane_vec<D>(a.out + (size_t)stream * D, o, lane);
+    store_lane_vec<D>(a.out + qstream * D, o, lane);
   };
 
   // The warp's first segment, when its stream is shared with earlier warps and
@@ -535,19 +547,22 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
       const double lsum = lane_sum();
-      put_record(recs + (size_t)(gw + seg_stream) * C::REC_BYTES, m_run, lsum, o);
+      put_record(recs + ((size_t)(gw + seg_stream) * gs + gj) * C::REC_BYTES, m_run, lsum, o);
     }
-    if (pub_held) put_record(recs + (size_t)(gw + held_stream) * C::REC_BYTES, held_m, held_l, held_o);
+    if (pub_held)
+      put_record(recs + ((size_t)(gw + held_stream) * gs + gj) * C::REC_BYTES, held_m, held_l, held_o);
     fence_acq_rel_gpu();
     __syncwarp();
     int last = 0;
     if (lane == 0 && pub_held) {
-      last = atomicAdd(&counters[held_stream], 1) == n_held - 1;
-      if (last) counters[held_stream] = 0;  // leave the workspace zero-filled
+      int* ctr = &counters[(size_t)held_stream * gs + gj];
+      last = atomicAdd(ctr, 1) == n_held - 1;
+      if (last) *ctr = 0;  // leave the workspace zero-filled
     }
     if (lane == 1 && pub_cur) {
-      last = atomicAdd(&counters[seg_stream], 1) == n_cur - 1;
-      if (last) counters[seg_stream] = 0;
+      int* ctr = &counters[(size_t)seg_stream * gs + gj];
+      last = atomicAdd(ctr, 1) == n_cur - 1;
+      if (last) *ctr = 0;
     }
     const bool last_held = __shfl_sync(kFull, last, 0) != 0;
     const bool last_cur = __shfl_sync(kFull, last, 1) != 0;
@@ -562,151 +577,167 @@ paged_decode_kernel(DecodeArgs a) {
       cur = nxt;
       nxt = make_desc(a, s_pfx, g0 + i + 32 + lane, g0, g1);
     }
-    const int st = i % STAGES;
-    char* slot = ring + st * C::STAGE_BYTES;
+    const int st = i % depth;
+    char* slot = ring + st * sb;
     const Desc d = shfl_desc(cur, i & 31);
     const int ntok = d.meta & 0xff;
     const bool has_q = (d.meta >> 8) & 1, has_sz = (d.meta >> 9) & 1;
 
-    if (!mbar_wait_bounded(&bar[st], (uint32_t)((i / STAGES) & 1), kWaitNs)) {
+    // every lane waits (each needs the copy's completion); the verdict is made
+    // warp-uniform, and group-uniform below, so a timeout never splits a warp
+    // or a ring group
+    const bool ok = __all_sync(kFull, mbar_wait_bounded(&bar[st], (uint32_t)((i / depth) & 1), kWaitNs));
+    if (!ok && gs == 1) {
       set_status(a.status, kStatusWaitTimeout);
       aborted = true;
       abort_at = i;
       break;
     }
 
-    if (has_q) {
-      if (seg_stream >= 0) end_segment(seg_stream);
-      seg_stream = d.stream;
-      m_run = -INFINITY;
-      l_lane = 0.f;
-      l_c = 0.f;
+    if (ok) {
+      if (has_q) {
+        if (seg_stream >= 0) end_segment(seg_stream);
+        seg_stream = d.stream;
+        m_run = -INFINITY;
+        l_lane = 0.f;
+        l_c = 0.f;
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
-      const float4* qv = reinterpret_cast<const float4*>(slot + C::Q_OFF) + 4 * c;
+        for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
+        const float4* qv = reinterpret_cast<const float4*>(slot + C::Q_OFF + gj * D * 4) + 4 * c;
 #pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        const float4 x = qv[k4];
-        q16[4 * k4] = x.x; q16[4 * k4 + 1] = x.y; q16[4 * k4 + 2] = x.z; q16[4 * k4 + 3] = x.w;
-      }
-    }
-    if (has_sz) {
-      const float4* sv = reinterpret_cast<const float4*>(slot + C::SZ_OFF) + 4 * c;
-      const float4* zv = reinterpret_cast<const float4*>(slot + C::SZ_OFF + D * 4) + 4 * c;
-      double bsum = 0.0;
-#pragma unroll
-      for (int k4 = 0; k4 < 4; ++k4) {
-        const float4 sx = sv[k4], zx = zv[k4];
-        const float s4[4] = {sx.x, sx.y, sx.z, sx.w};
-        const float z4[4] = {zx.x, zx.y, zx.z, zx.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const double qd = (double)q16[4 * k4 + k], sd = (double)s4[k];
-          qs[4 * k4 + k] = qd * sd;  // exact product
-          bsum = fma(16.0, qs[4 * k4 + k], bsum);
-          bsum = fma(qd, (double)z4[k] * sd, bsum);
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const float4 x = qv[k4];
+          q16[4 * k4] = x.x; q16[4 * k4 + 1] = x.y; q16[4 * k4 + 2] = x.z; q16[4 * k4 + 3] = x.w;
         }
       }
+      if (has_sz) {
+        const float4* sv = reinterpret_cast<const float4*>(slot + C::SZ_OFF) + 4 * c;
+        const float4* zv = reinterpret_cast<const float4*>(slot + C::SZ_OFF + D * 4) + 4 * c;
+        double bsum = 0.0;
 #pragma unroll
-      for (int o = 1; o < C::LPT; o <<= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
-      bias = bsum;
-    }
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const float4 sx = sv[k4], zx = zv[k4];
+          const float s4[4] = {sx.x, sx.y, sx.z, sx.w};
+          const float z4[4] = {zx.x, zx.y, zx.z, zx.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const double qd = (double)q16[4 * k4 + k], sd = (double)s4[k];
+            qs[4 * k4 + k] = qd * sd;  // exact product
+            bsum = fma(16.0, qs[4 * k4 + k], bsum);
+            bsum = fma(qd, (double)z4[k] * sd, bsum);
+          }
+        }
+#pragma unroll
+        for (int o = 1; o < C::LPT; o <<= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
+        bias = bsum;
+      }
 
-    if (ntok > 0) {
-      // ---- logits: lane (c, tsub) dots dims [16c, 16c+16) of tokens j*TPP + tsub ----
-      const uint2* kw = reinterpret_cast<const uint2*>(slot + C::K_OFF);
-      double part[C::NJ];
+      if (ntok > 0) {
+        // ---- logits: lane (c, tsub) dots dims [16c, 16c+16) of tokens j*TPP + tsub ----
+        const uint2* kw = reinterpret_cast<const uint2*>(slot + C::K_OFF);
+        double part[C::NJ];
 #pragma unroll
-      for (int j = 0; j < C::NJ; ++j) {
-        const uint2 w = kw[j * 32 + lane];
-        const uint32_t lo0 = (w.x & 0x0F0F0F0Fu) | 0x30303030u;
-        const uint32_t hi0 = ((w.x >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
-        const uint32_t lo1 = (w.y & 0x0F0F0F0Fu) | 0x30303030u;
-        const uint32_t hi1 = ((w.y >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
-        double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+        for (int j = 0; j < C::NJ; ++j) {
+          const uint2 w = kw[j * 32 + lane];
+          const uint32_t lo0 = (w.x & 0x0F0F0F0Fu) | 0x30303030u;
+          const uint32_t hi0 = ((w.x >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
+          const uint32_t lo1 = (w.y & 0x0F0F0F0Fu) | 0x30303030u;
+          const uint32_t hi1 = ((w.y >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
+          double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          s0 = fma(qs[2 * b], code_plus16(lo0, b), s0);
-          s1 = fma(qs[2 * b + 1], code_plus16(hi0, b), s1);
-          s2 = fma(qs[8 + 2 * b], code_plus16(lo1, b), s2);
-          s3 = fma(qs[8 + 2 * b + 1], code_plus16(hi1, b), s3);
+          for (int b = 0; b < 4; ++b) {
+            s0 = fma(qs[2 * b], code_plus16(lo0, b), s0);
+            s1 = fma(qs[2 * b + 1], code_plus16(hi0, b), s1);
+            s2 = fma(qs[8 + 2 * b], code_plus16(lo1, b), s2);
+            s3 = fma(qs[8 + 2 * b + 1], code_plus16(hi1, b), s3);
+          }
+          part[j] = (s0 + s1) + (s2 + s3);
         }
-        part[j] = (s0 + s1) + (s2 + s3);
-      }
-      // reduce-scatter over the LPT lanes of a token group: lane c ends with token j = c >> 1
+        // reduce-scatter over the LPT lanes of a token group: lane c ends with token j = c >> 1
 #pragma unroll
-      for (int step = 0; (C::NJ >> step) > 1; ++step) {
-        const int half = (C::NJ >> step) >> 1;
-        const int mask = C::LPT >> (step + 1);
-        const bool upper = (c & mask) != 0;
+        for (int step = 0; (C::NJ >> step) > 1; ++step) {
+          const int half = (C::NJ >> step) >> 1;
+          const int mask = C::LPT >> (step + 1);
+          const bool upper = (c & mask) != 0;
 #pragma unroll
-        for (int k = 0; k < half; ++k) {
-          const double send = upper ? part[k] : part[k + half];
-          const double keep = upper ? part[k + half] : part[k];
-          part[k] = keep + __shfl_xor_sync(kFull, send, mask);
+          for (int k = 0; k < half; ++k) {
+            const double send = upper ? part[k] : part[k + half];
+            const double keep = upper ? part[k + half] : part[k];
+            part[k] = keep + __shfl_xor_sync(kFull, send, mask);
+          }
         }
-      }
-      double logit = part[0] + __shfl_xor_sync(kFull, part[0], 1) - bias;
-      const int tok = (c >> 1) * C::TPP + tsub;
-      if (tok >= ntok) logit = -INFINITY;
+        double logit = part[0] + __shfl_xor_sync(kFull, part[0], 1) - bias;
+        const int tok = (c >> 1) * C::TPP + tsub;
+        if (tok >= ntok) logit = -INFINITY;
 
-      // ---- online softmax: rescale only when the running max moves ----
-      if (__any_sync(kFull, logit > m_run)) {
-        double pmax = logit;
+        // ---- online softmax: rescale only when the running max moves ----
+        if (__any_sync(kFull, logit > m_run)) {
+          double pmax = logit;
 #pragma unroll
-        for (int o = 16; o > 1; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
-        const double m_new = fmax(m_run, pmax);
-        const float corr = exp_neg(m_run - m_new);
-        l_lane *= corr;
-        l_c *= corr;
+          for (int o = 16; o > 1; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
+          const double m_new = fmax(m_run, pmax);
+          const float corr = exp_neg(m_run - m_new);
+          l_lane *= corr;
+          l_c *= corr;
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) { acc[k] *= corr; acc_c[k] *= corr; }
-        m_run = m_new;
+          for (int k = 0; k < DPL; ++k) { acc[k] *= corr; acc_c[k] *= corr; }
+          m_run = m_new;
+        }
+        const float p = exp_neg(logit - m_run);
+        if ((c & 1) == 0) {
+          kahan_rescale_add(l_lane, l_c, 1.f, p);
+          p_tab[tok] = p;  // tok < 16; lanes c and c^1 hold the same token
+        }
+        __syncwarp();
+
+        // ---- P.V over the page's valid rows (float32 page sum, Kahan into the run) ----
+        const char* vs = slot + C::V_OFF;
+        float ps[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) ps[k] = 0.f;
+        if (ntok == kPage) {
+#pragma unroll
+          for (int t4 = 0; t4 < kPage / 4; ++t4) {
+            const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
+            pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps);
+            pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, ps);
+            pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps);
+            pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < kPage; ++t)
+            if (t < ntok) pv_row<D, VK>(vs, p_tab[t], t, lane, ps);
+        }
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[k], acc_c[k], 1.f, ps[k]);
       }
-      const float p = exp_neg(logit - m_run);
-      if ((c & 1) == 0) {
-        kahan_rescale_add(l_lane, l_c, 1.f, p);
-        p_tab[tok] = p;  // tok < 16; lanes c and c^1 hold the same token
-      }
+
+    }
+    // the slot is free once every warp of the group is done with it
+    if (gs == 1) {
       __syncwarp();
-
-      // ---- P.V over the page's valid rows (float32 page sum, Kahan into the run) ----
-      const char* vs = slot + C::V_OFF;
-      float ps[DPL];
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) ps[k] = 0.f;
-      if (ntok == kPage) {
-#pragma unroll
-        for (int t4 = 0; t4 < kPage / 4; ++t4) {
-          const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
-          pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps);
-          pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, ps);
-          pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps);
-          pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps);
-        }
-      } else {
-#pragma unroll
-        for (int t = 0; t < kPage; ++t)
-          if (t < ntok) pv_row<D, VK>(vs, p_tab[t], t, lane, ps);
-      }
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[k], acc_c[k], 1.f, ps[k]);
+    } else if (named_bar_or(1 + gi, gs * 32, !ok)) {
+      if (!ok) set_status(a.status, kStatusWaitTimeout);
+      aborted = true;
+      abort_at = i;
+      break;
     }
-
-    __syncwarp();
-    const int nx = i + STAGES;
+    const int nx = i + depth;
     if (nx < n) {
       const int src = nx & 31;
       const Desc dn = (nx >> 5) == (i >> 5) ? shfl_desc(cur, src) : shfl_desc(nxt, src);
-      if (lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
+      if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
     }
   }
 
   if (aborted) {
-    // Drain what this warp still has in flight (bounded) before leaving, so no
-    // bulk copy lands in shared memory after the CTA has exited.
-    for (int k = abort_at; k < n && k < abort_at + STAGES; ++k)
-      (void)mbar_wait_bounded(&bar[k % STAGES], (uint32_t)((k / STAGES) & 1), kWaitNs);
+    // The group's leader drains what the ring still has in flight (bounded)
+    // before leaving, so no bulk copy lands in shared memory after the CTA
+    // has exited.
+    if (leader)
+      for (int k = abort_at; k < n && k < abort_at + depth; ++k)
+        (void)mbar_wait_bounded(&bar[k % depth], (uint32_t)((k / depth) & 1), kWaitNs);
     return;
   }
   end_run();
@@ -762,15 +793,26 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, 
 constexpr int kWarps = I4KV_DECODE_WARPS;    // warps per CTA
 constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 
+// Warps sharing one ring: the largest divisor of kWarps (a power of two) that
+// divides the GQA ratio, so a CTA holds whole groups of query heads.
+int ring_group(int num_q_heads, int num_kv_heads) {
+  const int g = num_q_heads / num_kv_heads;
+  int x = kWarps;
+  while (g % x) x >>= 1;
+  return x;
+}
+
 template <int D, int VK>
-size_t dyn_smem(int batch) {
-  return 256 + pfx_bytes(batch) + (size_t)kWarps * Cfg<D, kWarps, kStages, VK>::WARP_BYTES;
+size_t dyn_smem(int batch, int gs) {
+  using C = Cfg<D, kWarps, kStages, VK>;
+  return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
+         (size_t)kWarps * C::P_BYTES;
 }
 
 struct OccCache {
   std::mutex mu;
   int dev[32] = {};
-  int key[32] = {};  // D * 4 + value kind
+  int key[32] = {};  // (D * 4 + value kind) * 8 + ring group
   size_t smem[32] = {};
   int grid[32] = {};
   int n = 0;
@@ -778,12 +820,12 @@ struct OccCache {
 OccCache g_occ;
 
 template <int D, int VK>
-cudaError_t decode_grid(int batch, int* grid_out) {
+cudaError_t decode_grid(int batch, int gs, int* grid_out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const size_t smem = dyn_smem<D, VK>(batch);
-  const int key = D * 4 + VK;
+  const size_t smem = dyn_smem<D, VK>(batch, gs);
+  const int key = (D * 4 + VK) * 8 + gs;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
     for (int i = 0; i < g_occ.n; ++i)
@@ -814,9 +856,9 @@ cudaError_t decode_grid(int batch, int* grid_out) {
 }
 
 template <int D, int VK>
-cudaError_t ws_size(int batch, int heads, size_t* out) {
+cudaError_t ws_size(int batch, int heads, int gs, size_t* out) {
   int grid = 0;
-  cudaError_t e = decode_grid<D, VK>(batch, &grid);
+  cudaError_t e = decode_grid<D, VK>(batch, gs, &grid);
   if (e != cudaSuccess) return e;
   const long long streams = (long long)batch * heads;
   const size_t nrec = (size_t)grid * kWarps + (size_t)streams;
@@ -828,15 +870,15 @@ template <int D, int VK>
 cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
                    cudaEvent_t ev_before, cudaEvent_t ev_after) {
   int grid = 0;
-  cudaError_t e = decode_grid<D, VK>(a.batch, &grid);
+  cudaError_t e = decode_grid<D, VK>(a.batch, a.gs, &grid);
   if (e != cudaSuccess) return e;
   size_t need = 0;
-  e = ws_size<D, VK>(a.batch, a.heads, &need);
+  e = ws_size<D, VK>(a.batch, a.heads, a.gs, &need);
   if (e != cudaSuccess) return e;
   if (ws_bytes < need) return cudaErrorInvalidValue;
   if (ev_before && (e = cudaEventRecord(ev_before, stream)) != cudaSuccess) return e;
   paged_decode_kernel<D, kWarps, kStages, VK>
-      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch), stream>>>(a);
+      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch, a.gs), stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;
@@ -855,11 +897,11 @@ cudaError_t launch_kind(int vk, const DecodeArgs& a, size_t ws_bytes, cudaStream
 }
 
 template <int D>
-cudaError_t ws_size_kind(int vk, int batch, int heads, size_t* out) {
+cudaError_t ws_size_kind(int vk, int batch, int heads, int gs, size_t* out) {
   switch (vk) {
-    case INT4KV_VALUES_F32: return ws_size<D, 0>(batch, heads, out);
-    case INT4KV_VALUES_F16: return ws_size<D, 1>(batch, heads, out);
-    case INT4KV_VALUES_BF16: return ws_size<D, 2>(batch, heads, out);
+    case INT4KV_VALUES_F32: return ws_size<D, 0>(batch, heads, gs, out);
+    case INT4KV_VALUES_F16: return ws_size<D, 1>(batch, heads, gs, out);
+    case INT4KV_VALUES_BF16: return ws_size<D, 2>(batch, heads, gs, out);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -889,7 +931,9 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v
   if ((out && !al16(out)) || (part_out && !al16(part_out))) return cudaErrorInvalidValue;
   DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_q_heads,
                max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status,
-               part_out, num_kv_heads, num_q_heads / num_kv_heads};
+               part_out, num_kv_heads, num_q_heads / num_kv_heads,
+               ring_group(num_q_heads, num_kv_heads), 0};
+  a.vheads = num_q_heads / a.gs;
   switch (head_dim) {
     case 64: return launch_kind<64>(vk, a, workspace_bytes, stream, ev_before, ev_after);
     case 128: return launch_kind<128>(vk, a, workspace_bytes, stream, ev_before, ev_after);
@@ -909,9 +953,9 @@ cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int n
     return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size<64, 0>(batch, num_q_heads, bytes);
-    case 128: return ws_size<128, 0>(batch, num_q_heads, bytes);
-    case 256: return ws_size<256, 0>(batch, num_q_heads, bytes);
+    case 64: return ws_size<64, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 128: return ws_size<128, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 256: return ws_size<256, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -923,9 +967,9 @@ cudaError_t int4kv_paged_decode_workspace_size_ex(int batch, int num_q_heads, in
     return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size_kind<64>(value_dtype, batch, num_q_heads, bytes);
-    case 128: return ws_size_kind<128>(value_dtype, batch, num_q_heads, bytes);
-    case 256: return ws_size_kind<256>(value_dtype, batch, num_q_heads, bytes);
+    case 64: return ws_size_kind<64>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 128: return ws_size_kind<128>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 256: return ws_size_kind<256>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
     default: return cudaErrorInvalidValue;
   }
 }

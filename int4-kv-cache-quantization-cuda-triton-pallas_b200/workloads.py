@@ -50,6 +50,11 @@ class DecodeShape:
     pool_pages: int
     group_tokens: int = 128
     value_bytes: int = 4  # 4 float32, 2 float16 / bfloat16 value pool
+    q_heads: Optional[int] = None  # query heads (GQA: a multiple of `heads`); None = heads
+
+    @property
+    def query_heads(self):
+        return self.q_heads if self.q_heads is not None else self.heads
 
     @property
     def pages(self):
@@ -57,14 +62,15 @@ class DecodeShape:
 
     def algorithmic_bytes(self):
         """Bytes a decode step must move: valid-token K (packed) + V + per-group scale/zp
-        + query + output + block-table entries."""
+        + query + output + block-table entries. K/V/scale bytes count per kv head
+        (``heads``), query/output per query head."""
         d = self.head_dim
         total = 0
         for n in self.seq_lens:
             groups = (n + self.group_tokens - 1) // self.group_tokens
             pages = (n + PAGE_TOKENS - 1) // PAGE_TOKENS
             total += self.heads * (n * d // 2 + self.value_bytes * n * d + 8 * d * groups) + 4 * pages
-        total += 2 * 4 * self.batch * self.heads * d
+        total += 2 * 4 * self.batch * self.query_heads * d
         return total
 
 
@@ -72,6 +78,11 @@ def config_shape(name: str, seed: int = 0) -> DecodeShape:
     """The decode configurations of the benchmark definition (per GPU)."""
     if name == "cfg0":
         return DecodeShape(8, 32, 128, [2048] * 8, pool_pages=8 * 128)
+    if name.startswith("cfg0_gqa"):  # config 0's 32 query heads over 32 / G kv heads
+        G = int(name[len("cfg0_gqa"):])
+        if G <= 0 or 32 % G:
+            raise ValueError(f"unknown config {name}")
+        return DecodeShape(8, 32 // G, 128, [2048] * 8, pool_pages=8 * 128, q_heads=32)
     if name.startswith("cfg2_"):
         L = int(name.split("_")[1])
         return DecodeShape(8, 32, 128, [L] * 8, pool_pages=8 * ((L + 15) // 16))
@@ -115,7 +126,7 @@ def torch_build_cache(shape: DecodeShape, seed: int = 0, device="cuda", value_dt
         v = torch.randn((n, h, d), generator=g, device=device)
         cache.write_sequences([b], [k], [v])
         del k, v
-    query = torch.randn((shape.batch, h, d), generator=g, device=device)
+    query = torch.randn((shape.batch, shape.query_heads, d), generator=g, device=device)
     return {"query": query, "cache": cache}
 
 
