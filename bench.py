@@ -266,13 +266,16 @@ def run_ours(args):
             "v_pool": cache.v_pool.float().cpu().numpy(), "sz_pool": cache.sz_pool.cpu().numpy(),
             "block_table": bt.cpu().numpy(), "seq_lens": sl.cpu().numpy()}
     rng = np.random.default_rng(rank)
+    # (sequence, kv head) streams; each covers its G = hq / h query heads
     gate_streams = [(int(b), int(hh)) for b, hh in zip(rng.integers(0, shape.batch, 4),
-                                                       rng.integers(0, hq, 4))]
+                                                       rng.integers(0, h, 4))]
     ex = oracle.decode_paged(host["query"], host["k_pool"], host["v_pool"], host["sz_pool"],
                              host["block_table"], host["seq_lens"], method="f64",
                              streams=gate_streams)
     o_host = out.cpu().numpy()
-    gate_err = max(float(np.abs(o_host[b, hh] - ex[b, hh]).max()) for b, hh in gate_streams)
+    G = hq // h
+    gate_err = max(float(np.abs(o_host[b, hh * G:(hh + 1) * G] - ex[b, hh * G:(hh + 1) * G]).max())
+                   for b, hh in gate_streams)
     if not (np.isfinite(o_host).all() and gate_err <= 1e-6):
         raise RuntimeError(f"decode failed its correctness gate (max err {gate_err}); not timing")
 
@@ -377,7 +380,7 @@ def run_ours(args):
     # ---- CPU baseline: the oracle on a bounded sample (rank 0, N == 1) ----
     bytes_step = shape.algorithmic_bytes()
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and hq == h:  # MHA configs
         per_stream = bytes_step / (shape.batch * h)
         sample = [(b, hh) for b in range(shape.batch) for hh in range(h)][::4]
         cpu, outs = cpu_baseline(host, sample, per_stream)

@@ -816,8 +816,33 @@ struct OccCache {
   size_t smem[32] = {};
   int grid[32] = {};
   int n = 0;
+  // Dynamic shared-memory opt-in per (device, kernel): only ever raised, so a
+  // launch whose grid came from the cache never exceeds the kernel's limit.
+  int attr_dev[128] = {};
+  int attr_key[128] = {};  // D * 4 + value kind
+  size_t attr_max[128] = {};
+  int n_attr = 0;
 };
 OccCache g_occ;
+
+// Raise the kernel's dynamic shared-memory limit on `dev` to at least `smem`.
+template <typename K>
+cudaError_t ensure_smem_attr(K kern, int dev, int kkey, size_t smem) {
+  std::lock_guard<std::mutex> lk(g_occ.mu);
+  int i = 0;
+  while (i < g_occ.n_attr && !(g_occ.attr_dev[i] == dev && g_occ.attr_key[i] == kkey)) ++i;
+  if (i < g_occ.n_attr && g_occ.attr_max[i] >= smem) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (i == g_occ.n_attr) {
+    if (g_occ.n_attr == 128) return cudaSuccess;  // 9 kernels x 14 devices fit; never reached
+    g_occ.attr_dev[i] = dev;
+    g_occ.attr_key[i] = kkey;
+    ++g_occ.n_attr;
+  }
+  g_occ.attr_max[i] = smem;
+  return cudaSuccess;
+}
 
 template <int D, int VK>
 cudaError_t decode_grid(int batch, int gs, int* grid_out) {
@@ -835,7 +860,7 @@ cudaError_t decode_grid(int batch, int gs, int* grid_out) {
       }
   }
   auto kern = paged_decode_kernel<D, kWarps, kStages, VK>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = ensure_smem_attr(kern, dev, D * 4 + VK, smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0, sms = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem);
