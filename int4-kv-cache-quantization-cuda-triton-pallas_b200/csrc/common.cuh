@@ -124,6 +124,28 @@ I4KV_DEVINL bool named_bar_or(int id, int nthreads, bool pred) {
   return r != 0;
 }
 
+// ldmatrix.x4: lanes 8i..8i+7 give the row addresses (16-byte aligned, 16
+// bytes each) of 8x8 b16 matrix i; lane L receives 32-bit word (L & 3) of row
+// (L >> 2) of matrix i in r[i] -- the register layout of mma.sync operands.
+I4KV_DEVINL void ldmatrix_x4(uint32_t (&r)[4], const void* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(row_addr))
+               : "memory");
+}
+
+// d += A * B on the tensor cores, exact int32 arithmetic: A 16x32 u8 (row
+// major: a[0] row g cols 4t..4t+3, a[1] row g+8, a[2] row g cols 16+4t..,
+// a[3] row g+8 cols 16+4t..), B 32x8 s8 (column major: b0 rows 4t..4t+3 of
+// column g, b1 rows 16+4t..), d 16x8 (d[0..1] row g cols 2t, 2t+1; d[2..3]
+// row g+8), g = lane >> 2, t = lane & 3.
+I4KV_DEVINL void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 I4KV_DEVINL uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

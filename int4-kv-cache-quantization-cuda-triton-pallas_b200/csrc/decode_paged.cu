@@ -65,9 +65,7 @@ struct ValueKind {
 template <int D, int WARPS, int STAGES, int VK = 0>
 struct Cfg {
   static constexpr int VB = ValueKind<VK>::BYTES;  // bytes per stored value
-  static constexpr int LPT = D / 16;         // lanes per token in the logit phase (16 dims each)
-  static constexpr int TPP = 32 / LPT;       // tokens per pass
-  static constexpr int NJ = kPage / TPP;     // passes per page
+  static constexpr int KT = D / 64;          // 32-byte k-tiles of a packed key row
   static constexpr int DPL = D / 32;         // value dims per lane in the P.V phase
   static constexpr int V_OFF = 0;
   static constexpr int K_OFF = kPage * D * VB;
@@ -77,8 +75,6 @@ struct Cfg {
   static constexpr int P_BYTES = kPage * 4;  // per-warp softmax weights of the current page
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + P_BYTES;
   static constexpr int REC_BYTES = 16 + 4 * D;  // [m f64][l f64][acc D f32]
-  static_assert(LPT * TPP == 32 && NJ * TPP == kPage, "lane mapping");
-  static_assert(LPT == 2 * NJ, "reduce-scatter mapping needs LPT == 2*NJ");
   static_assert(STAGE_BYTES % 16 == 0 && WARP_BYTES % 16 == 0, "stage alignment");
 };
 
@@ -227,13 +223,6 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
     bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * D, (uint32_t)a.gs * D * 4, bar);
 }
 
-// float64 value 16 + code of the low nibble held in byte `sel` of `w`, where
-// `w` holds (code | 0x30) in each byte: the byte becomes bits 16..23 of the
-// high word 0x40300000 + (code << 16), low word zero.
-__device__ __forceinline__ double code_plus16(uint32_t w, uint32_t sel) {
-  return __hiloint2double((int)__byte_perm(w, 0x40000000u, 0x7044u | (sel << 8)), 0);
-}
-
 // sum = sum*r + x with a running compensation term c (Kahan): the rescale
 // applies to both, the addition captures its own rounding error in c.
 __device__ __forceinline__ void kahan_rescale_add(float& sum, float& c, float r, float x) {
@@ -322,7 +311,7 @@ paged_decode_kernel(DecodeArgs a) {
   char* stages = smem + 256 + pfx_bytes(a.batch);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int c = lane % C::LPT, tsub = lane / C::LPT;
+  const int fg = lane >> 2, ft = lane & 3;  // mma fragment row group / thread in group
   // Ring groups: gs warps share one ring of STAGES * gs slots; warp gj of the
   // group serves query head vh * gs + gj of every page the group stages
   // (gs = 1 without GQA: one warp, one ring, one query).
@@ -361,6 +350,12 @@ paged_decode_kernel(DecodeArgs a) {
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
   float* p_tab = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + warp * C::P_BYTES);
+  float* qbuf = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + WARPS * C::P_BYTES +
+                                         (size_t)warp * D * 4);  // this warp's query
+  // this warp's mma B operands for the current group: digs[e][lane] = the
+  // lane's registers {even b0, even b1, odd b0, odd b1} of k-tile e
+  uint4* digs = reinterpret_cast<uint4*>(stages + (size_t)WARPS * STAGES * sb +
+                                         WARPS * (C::P_BYTES + D * 4) + (size_t)warp * C::KT * 512);
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
@@ -374,9 +369,17 @@ paged_decode_kernel(DecodeArgs a) {
     if (leader && lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
   }
 
-  float q16[16];     // this lane's 16 query dims [16c, 16c+16)
-  double qs[16];     // q*s of those dims for the current group (exact products)
-  double bias = 0.0; // sum over all dims of 16*q*s + q*zp*s for the current group
+  // Logits of the current group: q.k = sum_c qs_c code_c - bias with
+  // qs_c = q_c s_c (exact in float64) and bias = sum_c q_c zp_c s_c. The code
+  // sum runs on the tensor cores in exact integer arithmetic: qs_c in fixed
+  // point, X_c = round(qs_c 2^(56-E)) with |qs_c| < 2^E, written as eight
+  // base-128 digits (the top one signed); mma.m16n8k32 (u8 codes x s8 digits,
+  // int32 sums, at most 128 * 15 * 128 in magnitude) gives per token the sum
+  // of code x digit p for the two digits p = 2t, 2t+1 of this lane, and
+  // float64 weights 2^(E - 7 - 7p) recombine them. Truncation is below
+  // 2^(E-56) per channel, as fine as float64 accumulation.
+  double w0 = 0.0, w1 = 0.0;     // weights of digits 2ft and 2ft + 1
+  double bias = 0.0;
   // Value and denominator sums: float32 with a Kahan compensation term, so
   // long page runs accumulate without float64 conversions on the hot path.
   float acc[DPL], acc_c[DPL];
@@ -387,8 +390,6 @@ paged_decode_kernel(DecodeArgs a) {
   int abort_at = 0;
 #pragma unroll
   for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
-#pragma unroll
-  for (int k = 0; k < 16; ++k) { q16[k] = 0.f; qs[k] = 0.0; }
 
   int* counters = reinterpret_cast<int*>(a.ws);
   char* recs = a.ws + cnt_bytes(streams);
@@ -603,78 +604,115 @@ paged_decode_kernel(DecodeArgs a) {
         l_c = 0.f;
 #pragma unroll
         for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
-        const float4* qv = reinterpret_cast<const float4*>(slot + C::Q_OFF + gj * D * 4) + 4 * c;
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const float4 x = qv[k4];
-          q16[4 * k4] = x.x; q16[4 * k4 + 1] = x.y; q16[4 * k4 + 2] = x.z; q16[4 * k4 + 3] = x.w;
-        }
+        // keep this warp's query for the group changes of the segment
+        const float4* qsrc = reinterpret_cast<const float4*>(slot + C::Q_OFF + gj * D * 4);
+        for (int k = lane; k < D / 4; k += 32) reinterpret_cast<float4*>(qbuf)[k] = qsrc[k];
+        __syncwarp();
       }
       if (has_sz) {
-        const float4* sv = reinterpret_cast<const float4*>(slot + C::SZ_OFF) + 4 * c;
-        const float4* zv = reinterpret_cast<const float4*>(slot + C::SZ_OFF + D * 4) + 4 * c;
-        double bsum = 0.0;
+        // Lane (fg, ft) holds, for k-tile e and half h, the channels
+        // 64e + 32h + 8ft + [0, 8): even ones for the low-nibble tile, odd ones
+        // for the high-nibble tile (the mma's B rows 4ft.. and 16 + 4ft..).
+        const float* sv = reinterpret_cast<const float*>(slot + C::SZ_OFF);
+        const float* zv = sv + D;
+        double amax = 0.0, bsum = 0.0;
+#pragma unroll 1
+        for (int eh = 0; eh < 2 * C::KT; ++eh) {
+          {
+            const int base = 32 * eh + 8 * ft;  // 64e + 32h + 8ft
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const float4 sx = sv[k4], zx = zv[k4];
-          const float s4[4] = {sx.x, sx.y, sx.z, sx.w};
-          const float z4[4] = {zx.x, zx.y, zx.z, zx.w};
+            for (int i4 = 0; i4 < 2; ++i4) {
+              const float4 q4 = *reinterpret_cast<const float4*>(qbuf + base + 4 * i4);
+              const float4 s4 = *reinterpret_cast<const float4*>(sv + base + 4 * i4);
+              const float4 z4 = *reinterpret_cast<const float4*>(zv + base + 4 * i4);
+              const float qa[4] = {q4.x, q4.y, q4.z, q4.w};
+              const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
+              const float za[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const double qd = (double)q16[4 * k4 + k], sd = (double)s4[k];
-            qs[4 * k4 + k] = qd * sd;  // exact product
-            bsum = fma(16.0, qs[4 * k4 + k], bsum);
-            bsum = fma(qd, (double)z4[k] * sd, bsum);
+              for (int k = 0; k < 4; ++k) {
+                const double qd = (double)qa[k], sd = (double)sa[k];
+                amax = fmax(amax, fabs(qd * sd));
+                bsum = fma(qd, (double)za[k] * sd, bsum);
+              }
+            }
           }
         }
-#pragma unroll
-        for (int o = 1; o < C::LPT; o <<= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
+        // the four lanes ft = 0..3 of a row group hold every channel once
+        bsum += __shfl_xor_sync(kFull, bsum, 1);
+        bsum += __shfl_xor_sync(kFull, bsum, 2);
+        amax = fmax(amax, __shfl_xor_sync(kFull, amax, 1));
+        amax = fmax(amax, __shfl_xor_sync(kFull, amax, 2));
         bias = bsum;
+        // |qs| < 2^E; q and s are float32, so a nonzero product lies in
+        // [2^-298, 2^256] and every power of two below is a normal double
+        const int E = amax > 0.0 ? ((__double2hiint(amax) >> 20) & 0x7FF) - 1022 : 0;
+        const double scale = __hiloint2double((1023 + 56 - E) << 20, 0);
+        w0 = __hiloint2double((1023 + E - 7 - 14 * ft) << 20, 0);
+        w1 = __hiloint2double((1023 + E - 14 - 14 * ft) << 20, 0);
+        const int sh = 49 - 7 * fg;  // digit fg of X: bits [sh, sh + 7), the top one signed
+        const long long dmask = fg == 0 ? 0xFF : 0x7F;
+#pragma unroll 1
+        for (int e = 0; e < C::KT; ++e) {
+          uint32_t regs[4];  // {even b0, even b1, odd b0, odd b1}
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int base = 64 * e + 32 * h + 8 * ft;
+            float qa[8], sa[8];
+#pragma unroll
+            for (int i4 = 0; i4 < 2; ++i4) {
+              const float4 q4 = *reinterpret_cast<const float4*>(qbuf + base + 4 * i4);
+              const float4 s4 = *reinterpret_cast<const float4*>(sv + base + 4 * i4);
+              qa[4 * i4] = q4.x; qa[4 * i4 + 1] = q4.y; qa[4 * i4 + 2] = q4.z; qa[4 * i4 + 3] = q4.w;
+              sa[4 * i4] = s4.x; sa[4 * i4 + 1] = s4.y; sa[4 * i4 + 2] = s4.z; sa[4 * i4 + 3] = s4.w;
+            }
+#pragma unroll
+            for (int par = 0; par < 2; ++par) {
+              uint32_t reg = 0u;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int ch = 2 * i + par;
+                const long long X = __double2ll_rn((double)qa[ch] * (double)sa[ch] * scale);
+                reg |= (uint32_t)((X >> sh) & dmask) << (8 * i);
+              }
+              regs[2 * par + h] = reg;
+            }
+          }
+          digs[e * 32 + lane] = make_uint4(regs[0], regs[1], regs[2], regs[3]);
+        }
+        __syncwarp();
       }
 
       if (ntok > 0) {
-        // ---- logits: lane (c, tsub) dots dims [16c, 16c+16) of tokens j*TPP + tsub ----
-        const uint2* kw = reinterpret_cast<const uint2*>(slot + C::K_OFF);
-        double part[C::NJ];
+        // ---- logits of tokens fg and fg + 8 (every lane of the row group) ----
+        const char* krow = slot + C::K_OFF + ((lane & 7) + 8 * ((lane >> 3) & 1)) * (D / 2) +
+                           16 * (lane >> 4);
+        int cs[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int j = 0; j < C::NJ; ++j) {
-          const uint2 w = kw[j * 32 + lane];
-          const uint32_t lo0 = (w.x & 0x0F0F0F0Fu) | 0x30303030u;
-          const uint32_t hi0 = ((w.x >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
-          const uint32_t lo1 = (w.y & 0x0F0F0F0Fu) | 0x30303030u;
-          const uint32_t hi1 = ((w.y >> 4) & 0x0F0F0F0Fu) | 0x30303030u;
-          double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            s0 = fma(qs[2 * b], code_plus16(lo0, b), s0);
-            s1 = fma(qs[2 * b + 1], code_plus16(hi0, b), s1);
-            s2 = fma(qs[8 + 2 * b], code_plus16(lo1, b), s2);
-            s3 = fma(qs[8 + 2 * b + 1], code_plus16(hi1, b), s3);
-          }
-          part[j] = (s0 + s1) + (s2 + s3);
+        for (int e = 0; e < C::KT; ++e) {
+          uint32_t r[4];
+          ldmatrix_x4(r, krow + 32 * e);
+          const uint32_t lo[4] = {r[0] & 0x0F0F0F0Fu, r[1] & 0x0F0F0F0Fu, r[2] & 0x0F0F0F0Fu,
+                                  r[3] & 0x0F0F0F0Fu};
+          const uint32_t hi[4] = {(r[0] >> 4) & 0x0F0F0F0Fu, (r[1] >> 4) & 0x0F0F0F0Fu,
+                                  (r[2] >> 4) & 0x0F0F0F0Fu, (r[3] >> 4) & 0x0F0F0F0Fu};
+          const uint4 b = digs[e * 32 + lane];
+          mma_u8s8_16832(cs, lo, b.x, b.y);
+          mma_u8s8_16832(cs, hi, b.z, b.w);
         }
-        // reduce-scatter over the LPT lanes of a token group: lane c ends with token j = c >> 1
-#pragma unroll
-        for (int step = 0; (C::NJ >> step) > 1; ++step) {
-          const int half = (C::NJ >> step) >> 1;
-          const int mask = C::LPT >> (step + 1);
-          const bool upper = (c & mask) != 0;
-#pragma unroll
-          for (int k = 0; k < half; ++k) {
-            const double send = upper ? part[k] : part[k + half];
-            const double keep = upper ? part[k + half] : part[k];
-            part[k] = keep + __shfl_xor_sync(kFull, send, mask);
-          }
-        }
-        double logit = part[0] + __shfl_xor_sync(kFull, part[0], 1) - bias;
-        const int tok = (c >> 1) * C::TPP + tsub;
-        if (tok >= ntok) logit = -INFINITY;
+        double lg0 = fma((double)cs[1], w1, (double)cs[0] * w0);
+        double lg1 = fma((double)cs[3], w1, (double)cs[2] * w0);
+        lg0 += __shfl_xor_sync(kFull, lg0, 1);
+        lg1 += __shfl_xor_sync(kFull, lg1, 1);
+        lg0 += __shfl_xor_sync(kFull, lg0, 2);
+        lg1 += __shfl_xor_sync(kFull, lg1, 2);
+        lg0 = fg < ntok ? lg0 - bias : -INFINITY;
+        lg1 = fg + 8 < ntok ? lg1 - bias : -INFINITY;
 
         // ---- online softmax: rescale only when the running max moves ----
-        if (__any_sync(kFull, logit > m_run)) {
-          double pmax = logit;
+        if (__any_sync(kFull, lg0 > m_run || lg1 > m_run)) {
+          double pmax = fmax(lg0, lg1);
 #pragma unroll
-          for (int o = 16; o > 1; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
+          for (int o = 16; o > 2; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
           const double m_new = fmax(m_run, pmax);
           const float corr = exp_neg(m_run - m_new);
           l_lane *= corr;
@@ -683,10 +721,12 @@ paged_decode_kernel(DecodeArgs a) {
           for (int k = 0; k < DPL; ++k) { acc[k] *= corr; acc_c[k] *= corr; }
           m_run = m_new;
         }
-        const float p = exp_neg(logit - m_run);
-        if ((c & 1) == 0) {
-          kahan_rescale_add(l_lane, l_c, 1.f, p);
-          p_tab[tok] = p;  // tok < 16; lanes c and c^1 hold the same token
+        const float p0 = exp_neg(lg0 - m_run), p1 = exp_neg(lg1 - m_run);
+        if (ft == 0) {  // one lane per row group owns tokens fg and fg + 8
+          kahan_rescale_add(l_lane, l_c, 1.f, p0);
+          kahan_rescale_add(l_lane, l_c, 1.f, p1);
+          p_tab[fg] = p0;
+          p_tab[fg + 8] = p1;
         }
         __syncwarp();
 
@@ -806,7 +846,8 @@ template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
   return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
-         (size_t)kWarps * C::P_BYTES;
+         (size_t)kWarps * (C::P_BYTES + D * 4 + C::KT * 512);  // rings, per-warp weights,
+                                                                 // query and mma digits
 }
 
 struct OccCache {
