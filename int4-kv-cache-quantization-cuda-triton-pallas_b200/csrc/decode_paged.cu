@@ -149,7 +149,7 @@ __device__ int block_page_prefix(const DecodeArgs& a, int* s_pfx, int* s_tmp) {
 struct Desc {
   int phys;   // physical page (valid when ntok > 0)
   int gphys;  // physical page holding the group's scale/zp (valid when has_sz)
-  int meta;   // ntok | has_q << 8 | has_sz << 9 | h << 16
+  int meta;   // ntok | has_q << 8 | has_sz << 9 | kv head << 16
   int stream; // b * vheads + h (queries stream * gs + j, j < gs, read it)
 };
 
@@ -181,7 +181,7 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   d.phys = phys;
   d.gphys = gphys;
   d.meta = ((gok && pok) ? ntok : 0) | (first ? (1 << 8) : 0) | ((grp && gok) ? (1 << 9) : 0) |
-           (h << 16);
+           (((h * a.gs) / a.group_q) << 16);
   d.stream = b * a.vheads + h;
   return d;
 }
@@ -201,7 +201,7 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   using C = Cfg<D, WARPS, STAGES, VK>;
   const int ntok = d.meta & 0xff;
   const bool has_q = (d.meta >> 8) & 1, has_sz = (d.meta >> 9) & 1;
-  const int h = d.meta >> 16;
+  const int kvh = d.meta >> 16;
   uint32_t bytes = 0;
   if (ntok) bytes += (uint32_t)ntok * (D * C::VB + D / 2);
   if (has_sz) bytes += 2 * D * 4;
@@ -209,15 +209,14 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (ntok) {
-    const size_t ph = (size_t)d.phys * a.kv_heads + (h * a.gs) / a.group_q;
+    const size_t ph = (size_t)d.phys * a.kv_heads + kvh;
     bulk_g2s(slot + C::V_OFF, static_cast<const char*>(a.v_pool) + ph * kPage * D * C::VB,
              (uint32_t)ntok * D * C::VB, bar);
     bulk_g2s(slot + C::K_OFF, a.k_pool + ph * kPage * (D / 2), (uint32_t)ntok * (D / 2), bar);
   }
   if (has_sz) {
     bulk_g2s(slot + C::SZ_OFF,
-             a.sz_pool + ((size_t)d.gphys * a.kv_heads + (h * a.gs) / a.group_q) * 2 * D, 2 * D * 4,
-             bar);
+             a.sz_pool + ((size_t)d.gphys * a.kv_heads + kvh) * 2 * D, 2 * D * 4, bar);
   }
   if (has_q)
     bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * D, (uint32_t)a.gs * D * 4, bar);
@@ -350,12 +349,9 @@ paged_decode_kernel(DecodeArgs a) {
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
   float* p_tab = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + warp * C::P_BYTES);
-  float* qbuf = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + WARPS * C::P_BYTES +
-                                         (size_t)warp * D * 4);  // this warp's query
-  // this warp's mma B operands for the current group: digs[e][lane] = the
-  // lane's registers {even b0, even b1, odd b0, odd b1} of k-tile e
-  uint4* digs = reinterpret_cast<uint4*>(stages + (size_t)WARPS * STAGES * sb +
-                                         WARPS * (C::P_BYTES + D * 4) + (size_t)warp * C::KT * 512);
+  // this warp's digit staging bytes: dig[g * D + c] = digit g of channel c
+  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb + WARPS * C::P_BYTES +
+                                            (size_t)warp * 8 * D);
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
@@ -378,6 +374,8 @@ paged_decode_kernel(DecodeArgs a) {
   // of code x digit p for the two digits p = 2t, 2t+1 of this lane, and
   // float64 weights 2^(E - 7 - 7p) recombine them. Truncation is below
   // 2^(E-56) per channel, as fine as float64 accumulation.
+  uint32_t bfrag[2 * C::KT][2];  // mma B operands: [2e + parity][half] of k-tile e
+  float qv[DPL];                 // this warp's query at channels lane * DPL + j
   double w0 = 0.0, w1 = 0.0;     // weights of digits 2ft and 2ft + 1
   double bias = 0.0;
   // Value and denominator sums: float32 with a Kahan compensation term, so
@@ -389,7 +387,9 @@ paged_decode_kernel(DecodeArgs a) {
   bool aborted = false;
   int abort_at = 0;
 #pragma unroll
-  for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
+  for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; qv[k] = 0.f; }
+#pragma unroll
+  for (int k = 0; k < 2 * C::KT; ++k) { bfrag[k][0] = 0u; bfrag[k][1] = 0u; }
 
   int* counters = reinterpret_cast<int*>(a.ws);
   char* recs = a.ws + cnt_bytes(streams);
@@ -573,12 +573,13 @@ paged_decode_kernel(DecodeArgs a) {
     if (last_cur) merge_stream(seg_stream, lo_c, hi_c);
   };
 
+  int st = 0;          // ring slot of page i
+  uint32_t phase = 0;  // parity of that slot's mbarrier phase for page i
   for (int i = 0; i < n; ++i) {
     if (i > 0 && (i & 31) == 0) {
       cur = nxt;
       nxt = make_desc(a, s_pfx, g0 + i + 32 + lane, g0, g1);
     }
-    const int st = i % depth;
     char* slot = ring + st * sb;
     const Desc d = shfl_desc(cur, i & 31);
     const int ntok = d.meta & 0xff;
@@ -587,7 +588,7 @@ paged_decode_kernel(DecodeArgs a) {
     // every lane waits (each needs the copy's completion); the verdict is made
     // warp-uniform, and group-uniform below, so a timeout never splits a warp
     // or a ring group
-    const bool ok = __all_sync(kFull, mbar_wait_bounded(&bar[st], (uint32_t)((i / depth) & 1), kWaitNs));
+    const bool ok = __all_sync(kFull, mbar_wait_bounded(&bar[st], phase, kWaitNs));
     if (!ok && gs == 1) {
       set_status(a.status, kStatusWaitTimeout);
       aborted = true;
@@ -604,82 +605,80 @@ paged_decode_kernel(DecodeArgs a) {
         l_c = 0.f;
 #pragma unroll
         for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
-        // keep this warp's query for the group changes of the segment
-        const float4* qsrc = reinterpret_cast<const float4*>(slot + C::Q_OFF + gj * D * 4);
-        for (int k = lane; k < D / 4; k += 32) reinterpret_cast<float4*>(qbuf)[k] = qsrc[k];
-        __syncwarp();
+        // this lane's query channels lane * DPL + j, kept for the segment's groups
+        const float* qsrc = reinterpret_cast<const float*>(slot + C::Q_OFF + gj * D * 4) + lane * DPL;
+#pragma unroll
+        for (int j = 0; j < DPL; j += 2) {
+          const float2 x = *reinterpret_cast<const float2*>(qsrc + j);
+          qv[j] = x.x;
+          qv[j + 1] = x.y;
+        }
       }
       if (has_sz) {
-        // Lane (fg, ft) holds, for k-tile e and half h, the channels
-        // 64e + 32h + 8ft + [0, 8): even ones for the low-nibble tile, odd ones
-        // for the high-nibble tile (the mma's B rows 4ft.. and 16 + 4ft..).
-        const float* sv = reinterpret_cast<const float*>(slot + C::SZ_OFF);
+        // Each lane takes its DPL channels c = lane * DPL + j: q*s, the bias
+        // terms and the fixed-point digits; the digits go through the warp's
+        // staging bytes to the lanes whose mma B operands hold them (lane
+        // (fg, ft): digit fg of channels 64e + 32h + 8ft + [0, 8)).
+        const float* sv = reinterpret_cast<const float*>(slot + C::SZ_OFF) + lane * DPL;
         const float* zv = sv + D;
+        double qsj[DPL];
         double amax = 0.0, bsum = 0.0;
-#pragma unroll 1
-        for (int eh = 0; eh < 2 * C::KT; ++eh) {
-          {
-            const int base = 32 * eh + 8 * ft;  // 64e + 32h + 8ft
 #pragma unroll
-            for (int i4 = 0; i4 < 2; ++i4) {
-              const float4 q4 = *reinterpret_cast<const float4*>(qbuf + base + 4 * i4);
-              const float4 s4 = *reinterpret_cast<const float4*>(sv + base + 4 * i4);
-              const float4 z4 = *reinterpret_cast<const float4*>(zv + base + 4 * i4);
-              const float qa[4] = {q4.x, q4.y, q4.z, q4.w};
-              const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
-              const float za[4] = {z4.x, z4.y, z4.z, z4.w};
+        for (int j = 0; j < DPL; j += 2) {
+          const float2 s2 = *reinterpret_cast<const float2*>(sv + j);
+          const float2 z2 = *reinterpret_cast<const float2*>(zv + j);
+          const float sa[2] = {s2.x, s2.y}, za[2] = {z2.x, z2.y};
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const double qd = (double)qa[k], sd = (double)sa[k];
-                amax = fmax(amax, fabs(qd * sd));
-                bsum = fma(qd, (double)za[k] * sd, bsum);
-              }
-            }
+          for (int k = 0; k < 2; ++k) {
+            const double qd = (double)qv[j + k], sd = (double)sa[k];
+            qsj[j + k] = qd * sd;  // exact product
+            amax = fmax(amax, fabs(qsj[j + k]));
+            bsum = fma(qd, (double)za[k] * sd, bsum);
           }
         }
-        // the four lanes ft = 0..3 of a row group hold every channel once
-        bsum += __shfl_xor_sync(kFull, bsum, 1);
-        bsum += __shfl_xor_sync(kFull, bsum, 2);
-        amax = fmax(amax, __shfl_xor_sync(kFull, amax, 1));
-        amax = fmax(amax, __shfl_xor_sync(kFull, amax, 2));
+        // butterfly sums: every lane ends with the same value
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
         bias = bsum;
         // |qs| < 2^E; q and s are float32, so a nonzero product lies in
-        // [2^-298, 2^256] and every power of two below is a normal double
-        const int E = amax > 0.0 ? ((__double2hiint(amax) >> 20) & 0x7FF) - 1022 : 0;
+        // [2^-298, 2^256] and every power of two used below is a normal double
+        int bexp = amax > 0.0 ? ((__double2hiint(amax) >> 20) & 0x7FF) : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bexp = max(bexp, __shfl_xor_sync(kFull, bexp, o));
+        const int E = bexp > 0 ? bexp - 1022 : 0;
         const double scale = __hiloint2double((1023 + 56 - E) << 20, 0);
         w0 = __hiloint2double((1023 + E - 7 - 14 * ft) << 20, 0);
         w1 = __hiloint2double((1023 + E - 14 - 14 * ft) << 20, 0);
-        const int sh = 49 - 7 * fg;  // digit fg of X: bits [sh, sh + 7), the top one signed
-        const long long dmask = fg == 0 ? 0xFF : 0x7F;
-#pragma unroll 1
-        for (int e = 0; e < C::KT; ++e) {
-          uint32_t regs[4];  // {even b0, even b1, odd b0, odd b1}
+        long long X[DPL];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int base = 64 * e + 32 * h + 8 * ft;
-            float qa[8], sa[8];
+        for (int j = 0; j < DPL; ++j) X[j] = __double2ll_rn(qsj[j] * scale);  // |X| < 2^56
+        __syncwarp();  // the previous group's staging bytes are consumed
 #pragma unroll
-            for (int i4 = 0; i4 < 2; ++i4) {
-              const float4 q4 = *reinterpret_cast<const float4*>(qbuf + base + 4 * i4);
-              const float4 s4 = *reinterpret_cast<const float4*>(sv + base + 4 * i4);
-              qa[4 * i4] = q4.x; qa[4 * i4 + 1] = q4.y; qa[4 * i4 + 2] = q4.z; qa[4 * i4 + 3] = q4.w;
-              sa[4 * i4] = s4.x; sa[4 * i4 + 1] = s4.y; sa[4 * i4 + 2] = s4.z; sa[4 * i4 + 3] = s4.w;
-            }
+        for (int g = 0; g < 8; ++g) {  // digit g: bits [49 - 7g, 56 - 7g) of X, the top one signed
+          const int sh = 49 - 7 * g;
+          const long long m = g == 0 ? 0xFF : 0x7F;
+          uint8_t* row = dig + g * D + lane * DPL;
+          if constexpr (DPL == 2) {
+            *reinterpret_cast<uint16_t*>(row) = (uint16_t)(((X[0] >> sh) & m) | (((X[1] >> sh) & m) << 8));
+          } else {
 #pragma unroll
-            for (int par = 0; par < 2; ++par) {
-              uint32_t reg = 0u;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int ch = 2 * i + par;
-                const long long X = __double2ll_rn((double)qa[ch] * (double)sa[ch] * scale);
-                reg |= (uint32_t)((X >> sh) & dmask) << (8 * i);
-              }
-              regs[2 * par + h] = reg;
+            for (int j4 = 0; j4 < DPL; j4 += 4) {
+              *reinterpret_cast<uint32_t*>(row + j4) =
+                  (uint32_t)(((X[j4] >> sh) & m) | (((X[j4 + 1] >> sh) & m) << 8) |
+                             (((X[j4 + 2] >> sh) & m) << 16) | (((X[j4 + 3] >> sh) & m) << 24));
             }
           }
-          digs[e * 32 + lane] = make_uint4(regs[0], regs[1], regs[2], regs[3]);
         }
         __syncwarp();
+#pragma unroll
+        for (int e = 0; e < C::KT; ++e) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint2 v = *reinterpret_cast<const uint2*>(dig + fg * D + 64 * e + 32 * h + 8 * ft);
+            bfrag[2 * e][h] = __byte_perm(v.x, v.y, 0x6420);      // even channels
+            bfrag[2 * e + 1][h] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
+          }
+        }
       }
 
       if (ntok > 0) {
@@ -695,9 +694,8 @@ paged_decode_kernel(DecodeArgs a) {
                                   r[3] & 0x0F0F0F0Fu};
           const uint32_t hi[4] = {(r[0] >> 4) & 0x0F0F0F0Fu, (r[1] >> 4) & 0x0F0F0F0Fu,
                                   (r[2] >> 4) & 0x0F0F0F0Fu, (r[3] >> 4) & 0x0F0F0F0Fu};
-          const uint4 b = digs[e * 32 + lane];
-          mma_u8s8_16832(cs, lo, b.x, b.y);
-          mma_u8s8_16832(cs, hi, b.z, b.w);
+          mma_u8s8_16832(cs, lo, bfrag[2 * e][0], bfrag[2 * e][1]);
+          mma_u8s8_16832(cs, hi, bfrag[2 * e + 1][0], bfrag[2 * e + 1][1]);
         }
         double lg0 = fma((double)cs[1], w1, (double)cs[0] * w0);
         double lg1 = fma((double)cs[3], w1, (double)cs[2] * w0);
@@ -768,6 +766,10 @@ paged_decode_kernel(DecodeArgs a) {
       const int src = nx & 31;
       const Desc dn = (nx >> 5) == (i >> 5) ? shfl_desc(cur, src) : shfl_desc(nxt, src);
       if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
+    }
+    if (++st == depth) {
+      st = 0;
+      phase ^= 1u;
     }
   }
 
@@ -846,8 +848,7 @@ template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
   return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
-         (size_t)kWarps * (C::P_BYTES + D * 4 + C::KT * 512);  // rings, per-warp weights,
-                                                                 // query and mma digits
+         (size_t)kWarps * (C::P_BYTES + 8 * D);  // rings, per-warp weights and digit bytes
 }
 
 struct OccCache {
