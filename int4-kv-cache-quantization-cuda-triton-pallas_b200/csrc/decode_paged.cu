@@ -29,15 +29,18 @@
 // query when they change. Each copy has one destination CTA; the sources are
 // this GPU's own pools.
 //
-// Numerics: with qs_d = q_d*s_d and c_d the 4-bit code, the logit is
-//   sum_d qs_d*(16 + c_d) - sum_d (16*qs_d + q_d*zp_d*s_d)
-// evaluated in float64 -- the products q*s and zp*s of float32 operands are
-// exact in float64 and the float64 value 16 + c is assembled from the code's
-// bits with one byte permute (no integer/float conversion on the hot loop).
-// The logits are therefore those of the reference's float64 arbiter
-// (exact dequantization); softmax weights are float32 exponentials, values are
-// summed per page in float32 and across pages in float32 with Kahan
-// compensation; partials are merged in float64.
+// Numerics: with qs_d = q_d*s_d (exact in float64) and c_d the 4-bit code,
+// the logit is sum_d qs_d*c_d - sum_d q_d*zp_d*s_d, i.e. the key dequantized
+// exactly as c*s - zp*s. The first sum runs on the tensor cores in exact
+// integer arithmetic: per (query, group) the qs_d are written in fixed point
+// relative to their largest magnitude (56 bits, eight base-128 digits), one
+// mma.m16n8k32 (u8 codes x s8 digits, int32 sums) per 32 bytes of packed key
+// row and nibble half gives every token's code x digit sums, and float64
+// weights recombine them. The truncation to 56 bits is finer than float64
+// accumulation, so the logits are those of the reference's float64 arbiter
+// to rounding; softmax weights are float32 exponentials, values are summed per
+// page in float32 and across pages in float32 with Kahan compensation;
+// partials are merged in float64.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
