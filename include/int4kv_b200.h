@@ -126,7 +126,8 @@ cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* to
  * every launch that completes leaves it zero-filled again (a launch that set
  * INT4KV_STATUS_WAIT_TIMEOUT does not: zero it again before reuse).
  * query/out [batch, num_q_heads, head_dim] float32; head_dim in {64,128,256};
- * page_tokens == 16; group_tokens a multiple of 16; num_q_heads == num_kv_heads.
+ * page_tokens == 16; group_tokens a multiple of 16; num_q_heads a multiple G
+ * of num_kv_heads (query head h reads kv head h / G: grouped-query attention).
  * Replaces the attention call of the reference's decode path
  * (src/ops.py:176-253 -> csrc/flash_decode_int4.cu:104-221) for distinct
  * per-(sequence, head) KV streams. `status` (nullable) collects
@@ -216,6 +217,38 @@ cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const in
                                 int page_tokens, const int32_t* block_table, int max_pages,
                                 int num_pages, uint8_t* k_pool, void* v_pool, int value_dtype,
                                 float* sz_pool, uint32_t* status, cudaStream_t stream);
+
+/* Rotary position embedding of rows x[rows, num_heads, head_dim] at
+ * positions[rows] into out (no overlap with x), with the arithmetic of
+ * int4kv_cache_append_rope: the prefill's keys are rotated with it before
+ * int4kv_cache_write. head_dim % 8 == 0; a position outside
+ * [0, rope_positions) writes NaN and sets INT4KV_STATUS_BAD_LENGTH. */
+cudaError_t int4kv_rope(const float* x, const int32_t* positions, int rows, int num_heads,
+                        int head_dim, const float* rope_cos, const float* rope_sin,
+                        int rope_positions, float* out, uint32_t* status, cudaStream_t stream);
+
+/* The decode step's write with the rotary position embedding fused in (one
+ * launch): the new key is rotated at its position before it is staged and
+ * quantized (the cache holds post-RoPE keys, as the reference's model path
+ * quantizes them: scripts/validate_llama.py:23-31), and the step's query
+ * q_in [batch, num_q_heads, head_dim] is rotated at the same position into
+ * q_out (q_in nullable). Rotation: Llama's rotate-half form
+ * (transformers' apply_rotary_pos_emb), out_i = x_i c_i - x_{i+D/2} s_i below
+ * D/2 and x_i c_i + x_{i-D/2} s_i above, float32 products and sum each rounded
+ * (no contraction); rope_cos / rope_sin [rope_positions, head_dim / 2] float32
+ * hold c, s per position (both NULL: no rotation). head_dim % 8 == 0 with a
+ * table; a position >= rope_positions sets INT4KV_STATUS_BAD_LENGTH and the
+ * sequence is skipped. Otherwise as int4kv_cache_append, which is this call
+ * with no table and no query. */
+cudaError_t int4kv_cache_append_rope(const float* k_new, const float* v_new,
+                                     const int32_t* positions, const int32_t* stage_slots,
+                                     float* k_stage, int num_slots, int batch, int num_heads,
+                                     int head_dim, int group_tokens, int page_tokens,
+                                     const int32_t* block_table, int max_pages, int num_pages,
+                                     uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
+                                     const float* rope_cos, const float* rope_sin,
+                                     int rope_positions, const float* q_in, float* q_out,
+                                     int num_q_heads, uint32_t* status, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Sequence split across GPUs (one long sequence, tokens partitioned into

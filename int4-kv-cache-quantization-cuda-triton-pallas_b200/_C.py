@@ -262,8 +262,14 @@ def block_decode(query, k_packed, k_scale, k_zp, value, block_lens, block_ids):
 
 
 def cache_append(k_new, v_new, positions, stage_slots, k_stage, block_table, k_pool, v_pool,
-                 sz_pool, group_tokens=128, status=None):
-    """Append one token per sequence (int4kv_cache_append): k_new / v_new [B, H, D]."""
+                 sz_pool, group_tokens=128, status=None, rope=None, q=None, q_out=None):
+    """Append one token per sequence (int4kv_cache_append): k_new / v_new [B, H, D].
+
+    With ``rope = (cos, sin)`` (float32 [positions, D/2] each) the new keys are
+    rotated at their positions before they are staged and quantized, and the
+    query ``q`` [B, Hq, D] (if given) is rotated into ``q_out`` in the same
+    launch (int4kv_cache_append_rope). Returns ``q_out`` (or None).
+    """
     lib = _lib.load()
     num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
     _check_input(k_new, "k_new")
@@ -283,16 +289,39 @@ def cache_append(k_new, v_new, positions, stage_slots, k_stage, block_table, k_p
             tuple(k_stage.shape[1:]) != (group_tokens, hkv * d):
         raise RuntimeError(f"k_stage must be float32 [slots, {group_tokens}, {hkv * d}]")
     max_pages = _check_table(block_table, b)
+    cos = sin = None
+    rope_n = 0
+    if rope is not None:
+        cos, sin = rope
+        for t, name in ((cos, "rope cos"), (sin, "rope sin")):
+            _check_input(t, name)
+            if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != d // 2:
+                raise RuntimeError(f"{name} must be float32 [positions, {d // 2}]")
+        if cos.shape != sin.shape:
+            raise RuntimeError("rope cos and sin must have the same shape")
+        rope_n = cos.shape[0]
+    hq = 0
+    if q is not None:
+        _check_input(q, "q")
+        if q.dtype != torch.float32 or q.dim() != 3 or q.shape[0] != b or q.shape[2] != d:
+            raise RuntimeError(f"q must be float32 [{b}, heads, {d}]")
+        hq = q.shape[1]
+        if q_out is None:
+            q_out = torch.empty_like(q)
+        _check_input(q_out, "q_out")
+        if q_out.dtype != torch.float32 or q_out.shape != q.shape:
+            raise RuntimeError("q_out must be float32 with the shape of q")
     _same_device(k_new, v_new, positions, stage_slots, k_stage, block_table, k_pool, v_pool,
-                 sz_pool, status)
+                 sz_pool, status, cos, sin, q, q_out)
     vk = VALUE_KINDS[v_pool.dtype] if v_pool is not None else 0
     with torch.cuda.device(k_new.device):
-        _lib.check(lib.int4kv_cache_append(_p(k_new), _p(v_new), _p(positions), _p(stage_slots),
-                                           _p(k_stage), k_stage.shape[0], b, hkv, d, group_tokens,
-                                           page, _p(block_table), max_pages, num_pages,
-                                           _p(k_pool), _p(v_pool), vk, _p(sz_pool), _p(status),
-                                           _stream(k_new)),
-                   "cache_append")
+        _lib.check(lib.int4kv_cache_append_rope(
+            _p(k_new), _p(v_new), _p(positions), _p(stage_slots), _p(k_stage), k_stage.shape[0],
+            b, hkv, d, group_tokens, page, _p(block_table), max_pages, num_pages, _p(k_pool),
+            _p(v_pool), vk, _p(sz_pool), _p(cos), _p(sin), rope_n, _p(q),
+            _p(q_out) if q is not None else None, hq, _p(status), _stream(k_new)),
+            "cache_append")
+    return q_out if q is not None else None
 
 
 def paged_decode_workspace_bytes(batch, q_heads, kv_heads, head_dim, device=None,
@@ -487,4 +516,28 @@ def exchange_merge(partials, peer_bufs, rank, streams, head_dim, out, status=Non
         _lib.check(lib.int4kv_exchange_merge(_p(partials), arr, world, rank, streams, head_dim,
                                              _p(out), _p(status), _stream(partials)),
                    "exchange_merge")
+    return out
+
+
+def rope(x, positions, cos, sin, out=None, status=None):
+    """Rotary embedding of rows x [rows, heads, D] at positions [rows] (int4kv_rope)."""
+    lib = _lib.load()
+    _check_input(x, "x")
+    if x.dtype != torch.float32 or x.dim() != 3:
+        raise RuntimeError("x must be float32 [rows, heads, head_dim]")
+    rows, h, d = x.shape
+    _check_input(positions, "positions")
+    if positions.dtype != torch.int32 or tuple(positions.shape) != (rows,):
+        raise RuntimeError("positions must be int32 [rows]")
+    for t, name in ((cos, "rope cos"), (sin, "rope sin")):
+        _check_input(t, name)
+        if t.dtype != torch.float32 or t.dim() != 2 or t.shape[1] != d // 2:
+            raise RuntimeError(f"{name} must be float32 [positions, {d // 2}]")
+    if out is None:
+        out = torch.empty_like(x)
+    _check_input(out, "out")
+    _same_device(x, positions, cos, sin, out, status)
+    with torch.cuda.device(x.device):
+        _lib.check(lib.int4kv_rope(_p(x), _p(positions), rows, h, d, _p(cos), _p(sin),
+                                   cos.shape[0], _p(out), _p(status), _stream(x)), "rope")
     return out

@@ -39,6 +39,11 @@ _PROTOS = {
                              + [_c_void_p] * 3,
     "int4kv_cache_append": [_c_void_p] * 5 + [_c_int] * 6 + [_c_void_p, _c_int, _c_int]
                            + [_c_void_p, _c_void_p, _c_int] + [_c_void_p] * 3,
+    "int4kv_rope": [_c_void_p, _c_void_p] + [_c_int] * 3 + [_c_void_p, _c_void_p, _c_int]
+                   + [_c_void_p] * 3,
+    "int4kv_cache_append_rope": [_c_void_p] * 5 + [_c_int] * 6 + [_c_void_p, _c_int, _c_int]
+                                + [_c_void_p, _c_void_p, _c_int] + [_c_void_p] * 3 + [_c_int]
+                                + [_c_void_p, _c_void_p, _c_int] + [_c_void_p, _c_void_p],
     "int4kv_block_decode": [_c_void_p] * 5 + [_c_int] + [_c_void_p] * 2 + [_c_int] * 6
                            + [_c_void_p, _c_void_p, _c_size_t, _c_void_p],
     "int4kv_paged_decode_partials": [_c_void_p] * 6 + [_c_int] * 8

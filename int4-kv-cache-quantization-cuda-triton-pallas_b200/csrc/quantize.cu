@@ -423,7 +423,45 @@ struct AppendArgs {
   const int32_t* slot;       // [B] staging slot of each sequence
   float* stage;              // [slots, R, C]
   int num_slots;
+  // Rotary position embedding of the new token's key and of the step's query
+  // (nullable: no rotation). cos/sin [rope_positions, head_dim / 2] float32.
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_positions;
+  const float* q_in;         // [B, q_heads * head_dim] (nullable)
+  float* q_out;              // [B, q_heads * head_dim]
+  int q_heads;
 };
+
+// Rotary embedding (the rotate-half form of Llama,
+// transformers.models.llama.modeling_llama.apply_rotary_pos_emb) of the four
+// channels d .. d+3 of one head row `x` (head_dim hd, d % 4 == 0) at table row
+// `cs`/`sn`: out_i = x_i c_i - x_{i+hd/2} s_i below hd/2, x_i c_i + x_{i-hd/2} s_i
+// above, each product and the sum rounded to float32 (no contraction), as the
+// reference model computes (q * cos) + (rotate_half(q) * sin).
+__device__ __forceinline__ float4 rope4(const float* x, int d, int hd, const float* cs,
+                                        const float* sn) {
+  const int half = hd >> 1;
+  const bool low = d < half;
+  const int f = low ? d : d - half;
+  const float4 a = __ldg(reinterpret_cast<const float4*>(x + d));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(x + (low ? d + half : d - half)));
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cs + f));
+  const float4 s = __ldg(reinterpret_cast<const float4*>(sn + f));
+  float4 o;
+  if (low) {
+    o.x = __fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, s.x));
+    o.y = __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, s.y));
+    o.z = __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, s.z));
+    o.w = __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, s.w));
+  } else {
+    o.x = __fadd_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, s.x));
+    o.y = __fadd_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, s.y));
+    o.z = __fadd_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, s.z));
+    o.w = __fadd_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, s.w));
+  }
+  return o;
+}
 
 __global__ void __launch_bounds__(kQuantThreads)
 append_quant_kernel(AppendArgs ap, int C, int R, OutPaged op) {
@@ -437,9 +475,24 @@ append_quant_kernel(AppendArgs ap, int C, int R, OutPaged op) {
   const int c0 = slab_c0 + lane * 4;
   const int b = blockIdx.y;
   const int pos = ap.pos[b], sl = ap.slot[b];
-  if (pos < 0 || sl < 0 || sl >= ap.num_slots || pos / op.page >= op.max_pages) {
+  if (pos < 0 || sl < 0 || sl >= ap.num_slots || pos / op.page >= op.max_pages ||
+      (ap.rope_cos && pos >= ap.rope_positions)) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && op.status) atomicOr(op.status, kStatusBadLength);
     return;
+  }
+  const int half = op.head_dim >> 1;
+  const float* rcos = ap.rope_cos ? ap.rope_cos + (size_t)pos * half : nullptr;
+  const float* rsin = ap.rope_cos ? ap.rope_sin + (size_t)pos * half : nullptr;
+  if (ap.q_in) {  // the step's query, rotated at the same position (spread over the slab CTAs)
+    const long long cq = (long long)ap.q_heads * op.head_dim;
+    const float* qrow = ap.q_in + (size_t)b * cq;
+    for (long long c = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; c < cq;
+         c += (long long)gridDim.x * blockDim.x * 4) {
+      const int hq = (int)(c / op.head_dim), d = (int)(c - (long long)hq * op.head_dim);
+      const float* x = qrow + (size_t)hq * op.head_dim;
+      *reinterpret_cast<float4*>(ap.q_out + (size_t)b * cq + c) =
+          rcos ? rope4(x, d, op.head_dim, rcos, rsin) : __ldg(reinterpret_cast<const float4*>(x + d));
+    }
   }
   const int rows = pos % R + 1, gpos = pos - (rows - 1);
   const bool lane_ok = c0 < C;
@@ -452,8 +505,14 @@ append_quant_kernel(AppendArgs ap, int C, int R, OutPaged op) {
   for (int i = 0; i < kMaxRowsPerWarp; ++i) {
     const int r = warp + i * kQuantWarps;
     if (lane_ok && r < rows) {
-      if (r == rows - 1) {  // the new token: from the input, and into the slot
-        vals[i] = __ldg(reinterpret_cast<const float4*>(ap.k_new + (size_t)b * C + c0));
+      if (r == rows - 1) {  // the new token: from the input (rotated), and into the slot
+        if (rcos) {
+          const int hk = c0 / op.head_dim;
+          vals[i] = rope4(ap.k_new + (size_t)b * C + (size_t)hk * op.head_dim, c0 - hk * op.head_dim,
+                          op.head_dim, rcos, rsin);
+        } else {
+          vals[i] = __ldg(reinterpret_cast<const float4*>(ap.k_new + (size_t)b * C + c0));
+        }
         *reinterpret_cast<float4*>(stage + (size_t)r * C + c0) = vals[i];
       } else {
         vals[i] = *reinterpret_cast<const float4*>(stage + (size_t)r * C + c0);
@@ -511,6 +570,37 @@ append_quant_kernel(AppendArgs ap, int C, int R, OutPaged op) {
         }
       }
     }
+  }
+}
+
+// Rotary embedding of rows x[rows, heads, head_dim] at positions[rows] into
+// out (a separate buffer: each channel reads its partner channel of x): the
+// prefill's keys before they are quantized, with the arithmetic of rope4.
+// One thread per four channels; a position outside the table gives NaN and
+// INT4KV_STATUS_BAD_LENGTH.
+__global__ void __launch_bounds__(256)
+rope_rows_kernel(const float* __restrict__ x, const int32_t* __restrict__ positions, int rows,
+                 int heads, int hd, const float* __restrict__ cs, const float* __restrict__ sn,
+                 int rope_positions, float* out, uint32_t* status) {
+  const long long row_ch = (long long)heads * hd;
+  const long long total4 = (long long)rows * row_ch / 4;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long c = i * 4;
+    const long long r = c / row_ch;
+    const int ch = (int)(c - r * row_ch);
+    const int h = ch / hd, d = ch - h * hd;
+    const int pos = positions[r];
+    float4 o;
+    if (pos < 0 || pos >= rope_positions) {
+      if (status) atomicOr(status, kStatusBadLength);
+      o = make_float4(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000),
+                      __int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+    } else {
+      o = rope4(x + r * row_ch + (long long)h * hd, d, hd, cs + (size_t)pos * (hd / 2),
+                sn + (size_t)pos * (hd / 2));
+    }
+    *reinterpret_cast<float4*>(out + c) = o;
   }
 }
 
@@ -776,12 +866,37 @@ cudaError_t int4kv_cache_write_ex(const float* k, const float* v, const int32_t*
   return cudaGetLastError();
 }
 
-cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const int32_t* positions,
-                                const int32_t* stage_slots, float* k_stage, int num_slots,
-                                int batch, int num_heads, int head_dim, int group_tokens,
-                                int page_tokens, const int32_t* block_table, int max_pages,
-                                int num_pages, uint8_t* k_pool, void* v_pool, int value_dtype,
-                                float* sz_pool, uint32_t* status, cudaStream_t stream) {
+cudaError_t int4kv_rope(const float* x, const int32_t* positions, int rows, int num_heads,
+                        int head_dim, const float* rope_cos, const float* rope_sin,
+                        int rope_positions, float* out, uint32_t* status, cudaStream_t stream) {
+  if (rows < 0 || num_heads <= 0 || head_dim <= 0 || head_dim % 8 != 0 || rope_positions <= 0)
+    return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  if (!x || !positions || !rope_cos || !rope_sin || !out) return cudaErrorInvalidValue;
+  if (!aligned16(x) || !aligned16(out) || !aligned16(rope_cos) || !aligned16(rope_sin))
+    return cudaErrorInvalidValue;
+  {  // each output channel reads its partner channel of x: no overlap at all
+    const char *xb = reinterpret_cast<const char*>(x), *ob = reinterpret_cast<const char*>(out);
+    const size_t n = (size_t)rows * num_heads * head_dim * 4;
+    if (xb < ob + n && ob < xb + n) return cudaErrorInvalidValue;
+  }
+  const long long total4 = (long long)rows * num_heads * head_dim / 4;
+  const long long blocks = (total4 + 255) / 256;
+  const unsigned grid = (unsigned)(blocks < 148 * 16 ? blocks : 148 * 16);
+  rope_rows_kernel<<<grid, 256, 0, stream>>>(x, positions, rows, num_heads, head_dim, rope_cos,
+                                             rope_sin, rope_positions, out, status);
+  return cudaGetLastError();
+}
+
+cudaError_t int4kv_cache_append_rope(const float* k_new, const float* v_new,
+                                     const int32_t* positions, const int32_t* stage_slots,
+                                     float* k_stage, int num_slots, int batch, int num_heads,
+                                     int head_dim, int group_tokens, int page_tokens,
+                                     const int32_t* block_table, int max_pages, int num_pages,
+                                     uint8_t* k_pool, void* v_pool, int value_dtype, float* sz_pool,
+                                     const float* rope_cos, const float* rope_sin,
+                                     int rope_positions, const float* q_in, float* q_out,
+                                     int num_q_heads, uint32_t* status, cudaStream_t stream) {
   if (batch <= 0 || batch > 65535 || num_heads <= 0 || head_dim <= 0 || num_slots <= 0)
     return cudaErrorInvalidValue;
   if (head_dim % 4 != 0 || page_tokens <= 0 || group_tokens <= 0) return cudaErrorInvalidValue;
@@ -794,14 +909,33 @@ cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const in
   if (!aligned16(k_new) || !aligned16(k_stage)) return cudaErrorInvalidValue;
   if (v_new && (!v_pool || !aligned16(v_new) || !aligned16(v_pool))) return cudaErrorInvalidValue;
   if (max_pages <= 0 || num_pages <= 0) return cudaErrorInvalidValue;
+  if ((rope_cos != nullptr) != (rope_sin != nullptr)) return cudaErrorInvalidValue;
+  if (rope_cos && (head_dim % 8 != 0 || rope_positions <= 0 || !aligned16(rope_cos) ||
+                   !aligned16(rope_sin)))
+    return cudaErrorInvalidValue;
+  if (q_in && (!q_out || num_q_heads <= 0 || !aligned16(q_in) || !aligned16(q_out)))
+    return cudaErrorInvalidValue;
   const long long C = (long long)num_heads * head_dim;
-  if (C > (1 << 30)) return cudaErrorInvalidValue;
+  if (C > (1 << 30) || (q_in && (long long)num_q_heads * head_dim > (1 << 30))) return cudaErrorInvalidValue;
   dim3 grid((unsigned)((C + kSlab - 1) / kSlab), batch, 1);
-  AppendArgs ap{k_new, v_new, positions, stage_slots, k_stage, num_slots};
+  AppendArgs ap{k_new, v_new, positions, stage_slots, k_stage, num_slots,
+                rope_cos, rope_sin, rope_positions, q_in, q_out, q_in ? num_q_heads : 0};
   OutPaged op{nullptr, nullptr, nullptr, block_table, max_pages, page_tokens, num_pages,
               num_heads, head_dim, k_pool, v_pool, value_dtype, sz_pool, status};
   append_quant_kernel<<<grid, kQuantThreads, 0, stream>>>(ap, (int)C, group_tokens, op);
   return cudaGetLastError();
+}
+
+cudaError_t int4kv_cache_append(const float* k_new, const float* v_new, const int32_t* positions,
+                                const int32_t* stage_slots, float* k_stage, int num_slots,
+                                int batch, int num_heads, int head_dim, int group_tokens,
+                                int page_tokens, const int32_t* block_table, int max_pages,
+                                int num_pages, uint8_t* k_pool, void* v_pool, int value_dtype,
+                                float* sz_pool, uint32_t* status, cudaStream_t stream) {
+  return int4kv_cache_append_rope(k_new, v_new, positions, stage_slots, k_stage, num_slots, batch,
+                                  num_heads, head_dim, group_tokens, page_tokens, block_table,
+                                  max_pages, num_pages, k_pool, v_pool, value_dtype, sz_pool,
+                                  nullptr, nullptr, 0, nullptr, nullptr, 0, status, stream);
 }
 
 cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* tok_offsets,

@@ -91,11 +91,13 @@ class PagedKVCache:
 
     # ---- writes ----
     def write_sequences(self, seq_ids: Sequence[int], keys: Sequence[torch.Tensor],
-                        values: Optional[Sequence[torch.Tensor]] = None) -> None:
+                        values: Optional[Sequence[torch.Tensor]] = None, rope=None) -> None:
         """Quantize and store whole sequences ([len, heads, head_dim] float32 each).
 
         One kernel launch quantizes every 128-token group of every sequence and
-        scatters keys and values into freshly allocated pages.
+        scatters keys and values into freshly allocated pages. With
+        ``rope = (cos, sin)`` the keys are first rotated at positions 0..len-1
+        on the GPU (``int4kv_rope``): the cache holds post-RoPE keys.
         """
         if len(seq_ids) != len(keys):
             raise ValueError("one key tensor per sequence")
@@ -108,6 +110,9 @@ class PagedKVCache:
         if sum(lens) == 0:
             return
         k = torch.cat([t.to(self.device, torch.float32) for t in keys]).contiguous()
+        if rope is not None:
+            pos = torch.from_numpy(np.concatenate([np.arange(n, dtype=np.int32) for n in lens]))
+            k = _C.rope(k, pos.to(self.device), rope[0], rope[1])
         v = None
         if values is not None and self.v_pool is not None:
             v = torch.cat([t.to(self.device, torch.float32) for t in values]).contiguous()
@@ -124,14 +129,17 @@ class PagedKVCache:
                 self.k_stage[slot, :open_rows] = k[o + n - open_rows:o + n].reshape(open_rows, -1)
 
     def append(self, seq_ids: Sequence[int], keys: torch.Tensor,
-               values: Optional[torch.Tensor] = None) -> None:
+               values: Optional[torch.Tensor] = None, rope=None,
+               query: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
         """Append one token to each sequence: keys / values [B, heads, head_dim].
 
         One kernel launch: each sequence's open 128-token group is quantized
         again over its valid rows (the new token included), so the cache equals
         a bulk write of the same tokens after every step. Sequences may be new
         (length 0); a new page is taken whenever a sequence crosses a 16-token
-        boundary.
+        boundary. With ``rope = (cos, sin)`` the new keys are rotated at their
+        positions first, and ``query`` [B, q_heads, head_dim] (optional) is
+        rotated at the same positions in the same launch and returned.
         """
         ids = list(seq_ids)
         if len(set(ids)) != len(ids):
@@ -155,10 +163,24 @@ class PagedKVCache:
         bt, _ = self.block_table(ids)
         positions = torch.tensor(pos, dtype=torch.int32, device=self.device)
         slot_t = torch.tensor(slots, dtype=torch.int32, device=self.device)
-        _C.cache_append(k, v, positions, slot_t, self.k_stage, bt, self.k_pool, self.v_pool,
-                        self.sz_pool, group_tokens=self.group_tokens)
+        q = None
+        if query is not None:
+            q = query.to(self.device, torch.float32).contiguous()
+        q_rot = _C.cache_append(k, v, positions, slot_t, self.k_stage, bt, self.k_pool,
+                                self.v_pool, self.sz_pool, group_tokens=self.group_tokens,
+                                rope=rope, q=q)
         for s in ids:
             self.lens[s] += 1
+        return q_rot
+
+    def decode_step(self, seq_ids: Sequence[int], query: torch.Tensor, keys: torch.Tensor,
+                    values: torch.Tensor, rope) -> torch.Tensor:
+        """One decode step of a Llama-style attention layer: RoPE of the step's
+        query and key at each sequence's position, quantize-on-append of the
+        rotated key and the value, then the paged decode of the rotated query
+        over the cache (the new token included). Two launches."""
+        q_rot = self.append(seq_ids, keys, values, rope=rope, query=query)
+        return self.decode(q_rot, seq_ids)
 
     # ---- reads ----
     def block_table(self, seq_ids: Sequence[int]):

@@ -34,3 +34,4 @@ from .attention import (  # noqa: F401
     paged_stream_pages,
     decode_paged,
 )
+from .rope import apply_rope, rope_table_f32  # noqa: F401

@@ -106,3 +106,18 @@ def test_exchange_layout_and_argument_checks(lib):
     assert lib.int4kv_exchange_merge(ctypes.c_void_p(4096), odd, 2, 0, 8, 128, ctypes.c_void_p(4096),
                                      n, n) == CUDA_ERROR_INVALID_VALUE
     assert lib.int4kv_ipc_open(n, n) == CUDA_ERROR_INVALID_VALUE
+
+
+def test_rope_entry_points_reject_bad_arguments(lib):
+    n = None
+    p = ctypes.c_void_p(4096)
+    # head_dim not a multiple of 8, empty table, overlapping in/out
+    assert lib.int4kv_rope(p, p, 4, 2, 12, p, p, 8, ctypes.c_void_p(1 << 20), n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_rope(p, p, 4, 2, 64, p, p, 0, ctypes.c_void_p(1 << 20), n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_rope(p, p, 4, 2, 64, p, p, 8, ctypes.c_void_p(4096 + 256), n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_rope(p, p, 0, 2, 64, p, p, 8, p, n, n) == 0  # nothing to do
+    # a rope table without its partner, a query without an output
+    assert lib.int4kv_cache_append_rope(p, n, p, p, p, 1, 1, 2, 64, 128, 16, p, 4, 4, p, n, 0, p,
+                                        p, n, 8, n, n, 0, n, n) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_cache_append_rope(p, n, p, p, p, 1, 1, 2, 64, 128, 16, p, 4, 4, p, n, 0, p,
+                                        p, p, 8, p, n, 2, n, n) == CUDA_ERROR_INVALID_VALUE
