@@ -396,7 +396,7 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": K, "warmup": Wm, "ms_per_step": round(mean_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": f"fp32 (fp64 logits), int4 keys, {args.values} values",
+        "dtype": f"fp32 (exact integer logits, fp64 recombination), int4 keys, {args.values} values",
         "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
         "config": workload_config(shape, args.config, world),
         "decode_us": round(mean_step * 1e3, 2),
@@ -592,7 +592,7 @@ def run_split(args):
         print(json.dumps({
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": K, "warmup": Wm, "ms_per_step": round(mean, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (fp64 logits), int4 keys",
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (exact integer logits, fp64 recombination), int4 keys",
             "data": "synthetic (seeded, config-0 distributions)",
             "config": {"workload": f"{args.config}: one sequence of {L} tokens x {h} heads x d{d}, "
                                    f"split across {world} GPUs by 128-token groups; step = "
