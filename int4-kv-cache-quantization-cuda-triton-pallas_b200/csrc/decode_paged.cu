@@ -322,6 +322,12 @@ paged_decode_kernel(DecodeArgs a) {
   const int depth = STAGES * gs;
   const int sb = C::Q_OFF + gs * D * 4;  // stage bytes with gs queries
   const bool leader = gj == 0;
+  {  // the block table into L2 while the lengths load (first descriptors hit L2)
+    const size_t bt_bytes = (size_t)a.batch * a.max_pages * 4;
+    const size_t off = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * 128;
+    if (off < bt_bytes)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.block_table) + off));
+  }
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
   const long long streams = (long long)a.batch * a.heads;
 
@@ -351,10 +357,11 @@ paged_decode_kernel(DecodeArgs a) {
 
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
-  float* p_tab = reinterpret_cast<float*>(stages + (size_t)WARPS * STAGES * sb + warp * C::P_BYTES);
-  // this warp's digit staging bytes: dig[g * D + c] = digit g of channel c
-  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb + WARPS * C::P_BYTES +
-                                            (size_t)warp * 8 * D);
+  // this warp's digit staging bytes (4 * D: rows of four digits), dig[g * D + c]
+  // = digit g (mod 4) of channel c; the page's softmax weights reuse its
+  // first 64 bytes between group changes
+  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb + (size_t)warp * 4 * D);
+  float* p_tab = reinterpret_cast<float*>(dig);
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
@@ -655,33 +662,42 @@ paged_decode_kernel(DecodeArgs a) {
         long long X[DPL];
 #pragma unroll
         for (int j = 0; j < DPL; ++j) X[j] = __double2ll_rn(qsj[j] * scale);  // |X| < 2^56
-        __syncwarp();  // the previous group's staging bytes are consumed
+        // Two rounds of four digits through the warp's 4*D staging bytes
+        // (rows g & 3); the lanes whose digit is in the round load their B operands.
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {  // digit g: bits [49 - 7g, 56 - 7g) of X, the top one signed
-          const int sh = 49 - 7 * g;
-          const long long m = g == 0 ? 0xFF : 0x7F;
-          uint8_t* row = dig + g * D + lane * DPL;
-          if constexpr (DPL == 2) {
-            *reinterpret_cast<uint16_t*>(row) = (uint16_t)(((X[0] >> sh) & m) | (((X[1] >> sh) & m) << 8));
-          } else {
+        for (int half = 0; half < 2; ++half) {
+          __syncwarp();  // the staging bytes (and the page weights aliased on them) are free
 #pragma unroll
-            for (int j4 = 0; j4 < DPL; j4 += 4) {
-              *reinterpret_cast<uint32_t*>(row + j4) =
-                  (uint32_t)(((X[j4] >> sh) & m) | (((X[j4 + 1] >> sh) & m) << 8) |
-                             (((X[j4 + 2] >> sh) & m) << 16) | (((X[j4 + 3] >> sh) & m) << 24));
+          for (int g4 = 0; g4 < 4; ++g4) {  // digit g: bits [49 - 7g, 56 - 7g) of X, the top one signed
+            const int g = 4 * half + g4;
+            const int sh = 49 - 7 * g;
+            const long long m = g == 0 ? 0xFF : 0x7F;
+            uint8_t* row = dig + g4 * D + lane * DPL;
+            if constexpr (DPL == 2) {
+              *reinterpret_cast<uint16_t*>(row) = (uint16_t)(((X[0] >> sh) & m) | (((X[1] >> sh) & m) << 8));
+            } else {
+#pragma unroll
+              for (int j4 = 0; j4 < DPL; j4 += 4) {
+                *reinterpret_cast<uint32_t*>(row + j4) =
+                    (uint32_t)(((X[j4] >> sh) & m) | (((X[j4 + 1] >> sh) & m) << 8) |
+                               (((X[j4 + 2] >> sh) & m) << 16) | (((X[j4 + 3] >> sh) & m) << 24));
+              }
+            }
+          }
+          __syncwarp();
+          if ((fg >> 2) == half) {
+#pragma unroll
+            for (int e = 0; e < C::KT; ++e) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint2 v = *reinterpret_cast<const uint2*>(dig + (fg & 3) * D + 64 * e + 32 * h + 8 * ft);
+                bfrag[2 * e][h] = __byte_perm(v.x, v.y, 0x6420);      // even channels
+                bfrag[2 * e + 1][h] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
+              }
             }
           }
         }
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < C::KT; ++e) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint2 v = *reinterpret_cast<const uint2*>(dig + fg * D + 64 * e + 32 * h + 8 * ft);
-            bfrag[2 * e][h] = __byte_perm(v.x, v.y, 0x6420);      // even channels
-            bfrag[2 * e + 1][h] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
-          }
-        }
+        __syncwarp();  // staging read before the page weights overwrite it
       }
 
       if (ntok > 0) {
@@ -851,7 +867,7 @@ template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
   return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
-         (size_t)kWarps * (C::P_BYTES + 8 * D);  // rings, per-warp weights and digit bytes
+         (size_t)kWarps * 4 * D;  // rings, then per-warp digit staging / page weights
 }
 
 struct OccCache {
