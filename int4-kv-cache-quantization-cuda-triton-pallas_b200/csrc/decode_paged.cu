@@ -851,8 +851,17 @@ __global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, 
 #ifndef I4KV_DECODE_STAGES
 #define I4KV_DECODE_STAGES 2
 #endif
+#ifndef I4KV_DECODE_MAX_CTAS_F32
+#define I4KV_DECODE_MAX_CTAS_F32 0
+#endif
+#ifndef I4KV_DECODE_MAX_CTAS_16
+#define I4KV_DECODE_MAX_CTAS_16 3  // measured: 45.5 us at config 0 vs 46.5 (4) and 53.5 (2)
+#endif
 constexpr int kWarps = I4KV_DECODE_WARPS;    // warps per CTA
 constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
+// CTAs per SM for the grid (0: as many as fit), float32 and 16-bit value pools
+constexpr int kMaxCtasF32 = I4KV_DECODE_MAX_CTAS_F32;
+constexpr int kMaxCtas16 = I4KV_DECODE_MAX_CTAS_16;
 
 // Warps sharing one ring: the largest divisor of kWarps (a power of two) that
 // divides the GQA ratio, so a CTA holds whole groups of query heads.
@@ -929,6 +938,8 @@ cudaError_t decode_grid(int batch, int gs, int* grid_out) {
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   if (per_sm <= 0) return cudaErrorInvalidConfiguration;
+  const int cap = VK == 0 ? kMaxCtasF32 : kMaxCtas16;
+  if (cap > 0 && per_sm > cap) per_sm = cap;
   const int grid = per_sm * sms;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
