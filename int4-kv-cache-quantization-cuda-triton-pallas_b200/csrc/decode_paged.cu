@@ -58,8 +58,6 @@ namespace {
 constexpr int kPage = 16;
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of wall time
-constexpr int kTailMin = 14;  // pages per share below which there are no tail runs
-constexpr int kMaxRuns = 8;   // runs per group (head + claimed tails): bounds the merge list
 
 // Value storage kinds (INT4KV_VALUES_*): 0 float32, 1 float16, 2 bfloat16.
 template <int VK>
@@ -85,10 +83,8 @@ struct Cfg {
 
 // Workspace layout (zero-filled before first use; every completed launch
 // leaves the counters at zero again):
-//   [0, cnt_bytes(S + 2))     per-stream arrival counters, int32 [S = batch*heads],
-//                             then the tail-claim and groups-done counters
-//   [cnt_bytes(S + 2), ...)   partial records, REC_BYTES each: head runs at slot
-//                             (group + stream), tail runs at (groups + S) + (group + stream)
+//   [0, cnt_bytes)            per-stream arrival counters, int32 [batch*heads]
+//   [cnt_bytes, ...)          partial records, slot (warp + stream), REC_BYTES each
 __host__ __device__ inline size_t cnt_bytes(long long streams) {
   return ((size_t)streams * 4 + 127) / 128 * 128;
 }
@@ -355,29 +351,9 @@ paged_decode_kernel(DecodeArgs a) {
   const long long T = (long long)a.vheads * total_pages;  // < 2^31 (checked on the host)
   const long long NW = (long long)gridDim.x * gpc;         // ring groups in the grid
   const long long gw = (long long)blockIdx.x * gpc + gi;
-  const long long SV = (long long)a.batch * a.vheads;      // page streams
-  // Runs. Group w's equal share [wT/NW, (w+1)T/NW) of the page-heads is its
-  // head run; with one warp per ring and at least kTailMin pages in every
-  // share, the last 3/20 of the share (>= 2 pages) is split off as a tail run
-  // with fixed boundaries. A group works its head, then claims tails in order
-  // (one atomic counter) until none are left, so the fast SMs take over the
-  // slow ones' tails; SMs differ by about 10 % in the bandwidth they get.
-  // Records, counters and merges depend only on the run boundaries, never on
-  // which group worked a run: the outputs are deterministic.
-  // Virtual run ids: vr < NW head of group vr, vr >= NW tail of group vr - NW.
-  const bool tails = gs == 1 && T >= (long long)kTailMin * NW;
-  auto run_range = [&](long long vr, int& lo, int& hi) {
-    const long long w = vr < NW ? vr : vr - NW;
-    const int s0 = (int)(w * T / NW), s1 = (int)((w + 1) * T / NW);
-    const int m = s1 - (tails ? (s1 - s0) * 3 / 20 : 0);
-    lo = vr < NW ? s0 : m;
-    hi = vr < NW ? m : s1;
-  };
-  long long vr = gw;  // the run being worked
-  int r_lo, r_hi;
-  run_range(vr, r_lo, r_hi);
-  int len = r_hi - r_lo;
-  if (len <= 0) return;  // with tails every head has >= 12 pages
+  const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
+  const int n = g1 - g0;
+  if (n <= 0) return;
 
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
@@ -386,25 +362,17 @@ paged_decode_kernel(DecodeArgs a) {
   // first 64 bytes between group changes
   uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb + (size_t)warp * 4 * D);
   float* p_tab = reinterpret_cast<float*>(dig);
-  // streams this warp arrived last at, merged after its last run (2 per run)
-  int* pend = reinterpret_cast<int*>(stages + (size_t)WARPS * STAGES * sb + (size_t)WARPS * 4 * D) +
-              warp * 2 * kMaxRuns;
-  int npend = 0;
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
   }
   if (gs == 1) __syncwarp(); else named_bar_sync(1 + gi, gs * 32);
 
-  Desc cur = make_desc(a, s_pfx, r_lo + lane, r_lo, r_hi);
-  Desc nxt = make_desc(a, s_pfx, r_lo + 32 + lane, r_lo, r_hi);
-  int issued = 0;  // pages issued into the ring, over all runs of this group
+  Desc cur = make_desc(a, s_pfx, g0 + lane, g0, g1);
+  Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
   for (int i = 0; i < depth; ++i) {  // prologue: the first `depth` pages (all in chunk 0)
     const Desc d = shfl_desc(cur, i);
-    if (i < len) {
-      if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
-      ++issued;
-    }
+    if (leader && lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
   }
 
   // Logits of the current group: q.k = sum_c qs_c code_c - bias with
@@ -427,49 +395,24 @@ paged_decode_kernel(DecodeArgs a) {
   double m_run = -INFINITY;
   int seg_stream = -1;
   bool aborted = false;
+  int abort_at = 0;
 #pragma unroll
   for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; qv[k] = 0.f; }
 #pragma unroll
   for (int k = 0; k < 2 * C::KT; ++k) { bfrag[k][0] = 0u; bfrag[k][1] = 0u; }
 
   int* counters = reinterpret_cast<int*>(a.ws);
-  int* tail_ctr = counters + streams;  // next tail to claim
-  int* done_ctr = tail_ctr + 1;        // groups finished (the last one resets both)
-  char* recs = a.ws + cnt_bytes(streams + 2);
+  char* recs = a.ws + cnt_bytes(streams);
 
-  // Record of run vr for (virtual) stream s: heads and tails in two regions,
-  // each indexed (w + s), unique because a group's runs cover increasing streams.
-  auto rec_at = [&](long long r, long long s) -> char* {
-    const long long base = r < NW ? r : (NW + SV) + (r - NW);
-    return recs + ((size_t)(base + s) * gs + gj) * C::REC_BYTES;
-  };
-  auto stream_range = [&](int stream, long long& g_lo, long long& g_hi) {
+  // Warps [w_lo, w_hi] whose runs touch `stream`; returns how many of them
+  // hold a non-empty run (those are the stream's contributors).
+  auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
     const int b = stream / a.vheads, h = stream - b * a.vheads;
     const int np = s_pfx[b + 1] - s_pfx[b];
-    g_lo = (long long)a.vheads * s_pfx[b] + (long long)h * np;
-    g_hi = g_lo + np;
-  };
-  // Candidate runs of a stream: c = 0, 1, ... over the shares [w_lo, w_hi]
-  // touching it, heads and (with tails) tails interleaved in page order.
-  auto cand_run = [&](long long w_lo, long long c) -> long long {
-    return tails ? ((c & 1) ? NW + w_lo + (c >> 1) : w_lo + (c >> 1)) : w_lo + c;
-  };
-  auto touches = [&](long long r, long long g_lo, long long g_hi) -> bool {
-    int lo, hi;
-    run_range(r, lo, hi);
-    return lo < hi && lo < g_hi && hi > g_lo;
-  };
-  // Shares [w_lo, w_hi] touching `stream`; returns how many runs of them touch
-  // it (its contributors, each of which writes a record unless it is the only one).
-  auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
-    long long g_lo, g_hi;
-    stream_range(stream, g_lo, g_hi);
-    w_lo = ((g_lo + 1) * NW - 1) / T;
-    w_hi = (g_hi * NW - 1) / T;
-    if (!tails) return (T >= NW) ? (int)(w_hi - w_lo + 1) : (int)(g_hi - g_lo);
-    int cnt = 0;
-    for (long long c = 0; c < 2 * (w_hi - w_lo + 1); ++c) cnt += touches(cand_run(w_lo, c), g_lo, g_hi);
-    return cnt;
+    const long long gs0 = (long long)a.vheads * s_pfx[b] + (long long)h * np, ge = gs0 + np;
+    w_lo = ((gs0 + 1) * NW - 1) / T;
+    w_hi = (ge * NW - 1) / T;
+    return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
   };
 
   // Warp-wide sum of the lanes' denominators (float32 sum minus compensation).
@@ -514,21 +457,17 @@ paged_decode_kernel(DecodeArgs a) {
   // other die); chunks combine online in float64.
   auto merge_stream = [&](int stream, long long w_lo, long long w_hi) {
     constexpr int CH = 32 / DPL;   // records per chunk (registers: CH * DPL floats)
-    const bool all_run = T >= NW;  // then every share in [w_lo, w_hi] is non-empty
-    long long g_lo, g_hi;
-    stream_range(stream, g_lo, g_hi);
-    const long long ncand = (tails ? 2 : 1) * (w_hi - w_lo + 1);
+    const bool all_run = T >= NW;  // then every warp in [w_lo, w_hi] wrote a record
     double M = -INFINITY, L = 0.0, O[DPL];
 #pragma unroll
     for (int k = 0; k < DPL; ++k) O[k] = 0.0;
-    for (long long base = 0; base < ncand; base += CH) {
-      const int cnt = (int)min((long long)CH, ncand - base);
-      const long long rj = cand_run(w_lo, base + lane);
-      const bool okj = lane < cnt && (tails ? touches(rj, g_lo, g_hi)
-                                            : (all_run || (rj * T) / NW != ((rj + 1) * T) / NW));
+    for (long long base = w_lo; base <= w_hi; base += CH) {
+      const int cnt = (int)min((long long)CH, w_hi - base + 1);
+      const long long wj = base + lane;
+      const bool okj = lane < cnt && (all_run || (wj * T) / NW != ((wj + 1) * T) / NW);
       double mj = -INFINITY, lj = 0.0;
       if (okj) {
-        const char* r = rec_at(rj, stream);
+        const char* r = recs + ((size_t)(wj + stream) * gs + gj) * C::REC_BYTES;
         mj = __ldcg(reinterpret_cast<const double*>(r));
         lj = __ldcg(reinterpret_cast<const double*>(r + 8));
       }
@@ -536,8 +475,8 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
       for (int j = 0; j < CH; ++j) {
         if (j < cnt) {
-          load_lane_vec_cg<D>(reinterpret_cast<const float*>(rec_at(cand_run(w_lo, base + j), stream) + 16),
-                              v[j], lane);
+          load_lane_vec_cg<D>(reinterpret_cast<const float*>(
+              recs + ((size_t)(base + j + stream) * gs + gj) * C::REC_BYTES + 16), v[j], lane);
         }
       }
       double cm = mj;
@@ -619,9 +558,10 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
       const double lsum = lane_sum();
-      put_record(rec_at(vr, seg_stream), m_run, lsum, o);
+      put_record(recs + ((size_t)(gw + seg_stream) * gs + gj) * C::REC_BYTES, m_run, lsum, o);
     }
-    if (pub_held) put_record(rec_at(vr, held_stream), held_m, held_l, held_o);
+    if (pub_held)
+      put_record(recs + ((size_t)(gw + held_stream) * gs + gj) * C::REC_BYTES, held_m, held_l, held_o);
     fence_acq_rel_gpu();
     __syncwarp();
     int last = 0;
@@ -639,68 +579,17 @@ paged_decode_kernel(DecodeArgs a) {
     const bool last_cur = __shfl_sync(kFull, last, 1) != 0;
     if (!last_held && !last_cur) return;
     fence_acq_rel_gpu();
-    // merged after the loop: the merge's registers would otherwise stay
-    // allocated across the whole page loop
-    if (lane == 0) {
-      if (last_held) pend[npend] = held_stream;
-      if (last_cur) pend[npend + (last_held ? 1 : 0)] = seg_stream;
-    }
-    npend += (last_held ? 1 : 0) + (last_cur ? 1 : 0);
+    if (last_held) merge_stream(held_stream, lo_h, hi_h);
+    if (last_cur) merge_stream(seg_stream, lo_c, hi_c);
   };
 
-  int st = 0;          // ring slot of the next page to consume
-  uint32_t phase = 0;  // parity of that slot's mbarrier phase
-  int consumed = 0;    // pages consumed, over all runs of this group
-  // The run after this one: -1 not known yet, -2 none left; its first descriptors.
-  long long vr_b = -1;
-  int b_lo = 0, b_hi = 0;
-  Desc bcur = cur;
-  int claim = 0;  // lane 0: the tail index returned by the claim
-  bool claim_sent = false;
-  int nruns = 1;
-  auto claim_next = [&]() {  // after kMaxRuns runs a group claims no more (others take the tails)
-    if (lane == 0) claim = nruns < kMaxRuns ? atomicAdd(tail_ctr, 1) : 0x7fffffff;
-    claim_sent = true;
-  };
-  auto resolve_next = [&]() {
-    if (vr_b != -1) return;
-    const int k = __shfl_sync(kFull, claim, 0);
-    if (k < NW) {
-      vr_b = NW + k;
-      run_range(vr_b, b_lo, b_hi);
-      bcur = make_desc(a, s_pfx, b_lo + lane, b_lo, b_hi);
-    } else {
-      vr_b = -2;
-    }
-  };
-  int i = 0;  // offset in the current run
-  while (true) {
-    if (i == len) {  // the run is done: publish / merge it, then move to the next one
-      end_run();
-      if (!tails) break;
-      if (!claim_sent) claim_next();
-      resolve_next();
-      if (vr_b < 0) break;
-      vr = vr_b;
-      r_lo = b_lo;
-      r_hi = b_hi;
-      len = r_hi - r_lo;
-      cur = bcur;
-      nxt = make_desc(a, s_pfx, r_lo + 32 + lane, r_lo, r_hi);
-      vr_b = -1;
-      claim_sent = false;
-      ++nruns;
-      i = 0;
-      seg_stream = -1;
-      held_stream = -1;
-      continue;
-    }
+  int st = 0;          // ring slot of page i
+  uint32_t phase = 0;  // parity of that slot's mbarrier phase for page i
+  for (int i = 0; i < n; ++i) {
     if (i > 0 && (i & 31) == 0) {
       cur = nxt;
-      nxt = make_desc(a, s_pfx, r_lo + i + 32 + lane, r_lo, r_hi);
+      nxt = make_desc(a, s_pfx, g0 + i + 32 + lane, g0, g1);
     }
-    // claim the next tail two pages before its first page must be issued
-    if (tails && !claim_sent && i + depth + 2 >= len) claim_next();
     char* slot = ring + st * sb;
     const Desc d = shfl_desc(cur, i & 31);
     const int ntok = d.meta & 0xff;
@@ -713,6 +602,7 @@ paged_decode_kernel(DecodeArgs a) {
     if (!ok && gs == 1) {
       set_status(a.status, kStatusWaitTimeout);
       aborted = true;
+      abort_at = i;
       break;
     }
 
@@ -887,63 +777,31 @@ paged_decode_kernel(DecodeArgs a) {
     } else if (named_bar_or(1 + gi, gs * 32, !ok)) {
       if (!ok) set_status(a.status, kStatusWaitTimeout);
       aborted = true;
+      abort_at = i;
       break;
     }
-    const int nx = i + depth;  // the page `depth` positions ahead, in this run or the next
-    if (nx < len) {
+    const int nx = i + depth;
+    if (nx < n) {
       const int src = nx & 31;
       const Desc dn = (nx >> 5) == (i >> 5) ? shfl_desc(cur, src) : shfl_desc(nxt, src);
       if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
-      ++issued;
-    } else if (tails) {
-      resolve_next();
-      const int j = nx - len;  // < depth <= every tail's length
-      if (vr_b >= 0 && j < b_hi - b_lo) {
-        const Desc dn = shfl_desc(bcur, j);
-        if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, dn, slot, &bar[st]);
-        ++issued;
-      }
     }
     if (++st == depth) {
       st = 0;
       phase ^= 1u;
     }
-    ++consumed;
-    ++i;
   }
 
   if (aborted) {
     // The group's leader drains what the ring still has in flight (bounded)
     // before leaving, so no bulk copy lands in shared memory after the CTA
     // has exited.
-    if (leader) {
-      int s2 = st;
-      uint32_t p2 = phase;
-      for (int k = consumed; k < issued; ++k) {
-        (void)mbar_wait_bounded(&bar[s2], p2, kWaitNs);
-        if (++s2 == depth) {
-          s2 = 0;
-          p2 ^= 1u;
-        }
-      }
-    }
+    if (leader)
+      for (int k = abort_at; k < n && k < abort_at + depth; ++k)
+        (void)mbar_wait_bounded(&bar[k % depth], (uint32_t)((k / depth) & 1), kWaitNs);
     return;
   }
-  __syncwarp();
-  for (int k = 0; k < npend; ++k) {
-    const int stream = pend[k];
-    long long lo, hi;
-    (void)contributors_of(stream, lo, hi);
-    merge_stream(stream, lo, hi);
-  }
-  if (tails && lane == 0) {  // the last group out leaves the claim counters at zero
-    fence_acq_rel_gpu();
-    if (atomicAdd(done_ctr, 1) == (int)NW - 1) {
-      fence_acq_rel_gpu();
-      *tail_ctr = 0;
-      *done_ctr = 0;
-    }
-  }
+  end_run();
 }
 
 // Merge per-GPU partial records [parts][streams] of one decode step into
@@ -1018,8 +876,7 @@ template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
   return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
-         (size_t)kWarps * (4 * D + 8 * kMaxRuns);  // rings, per-warp digit staging / page
-                                                     // weights, per-warp merge list
+         (size_t)kWarps * 4 * D;  // rings, then per-warp digit staging / page weights
 }
 
 struct OccCache {
@@ -1101,8 +958,8 @@ cudaError_t ws_size(int batch, int heads, int gs, size_t* out) {
   cudaError_t e = decode_grid<D, VK>(batch, gs, &grid);
   if (e != cudaSuccess) return e;
   const long long streams = (long long)batch * heads;
-  const size_t nrec = 2 * ((size_t)grid * kWarps + (size_t)streams);  // head and tail regions
-  *out = cnt_bytes(streams + 2) + nrec * Cfg<D, kWarps, kStages, VK>::REC_BYTES;
+  const size_t nrec = (size_t)grid * kWarps + (size_t)streams;
+  *out = cnt_bytes(streams) + nrec * Cfg<D, kWarps, kStages, VK>::REC_BYTES;
   return cudaSuccess;
 }
 
@@ -1303,7 +1160,7 @@ cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const
 //   * scratch is the file-scope array below, INT4KV_STATIC_SCRATCH_BYTES per
 //     device; a call whose launch would need more is rejected with
 //     cudaErrorInvalidValue and the bytes it would need in *scratch_needed;
-//   * what must start at zero: the counter region [0, cnt_bytes(streams + 2)) --
+//   * what must start at zero: the counter region [0, cnt_bytes(streams)) --
 //     every call zeroes it on `stream` (cudaMemsetAsync, no allocation) before
 //     the kernel; the partial records need no initial value;
 //   * one scratch per device: calls that overlap in time on the same device
@@ -1355,7 +1212,7 @@ extern "C" cudaError_t int4kv_paged_decode_static_scratch(
   void* scratch = nullptr;
   e = static_scratch_ptr(&scratch);
   if (e != cudaSuccess) return e;
-  const size_t zero_bytes = cnt_bytes((long long)batch * num_q_heads + 2);  // + the claim counters
+  const size_t zero_bytes = cnt_bytes((long long)batch * num_q_heads);
   e = cudaMemsetAsync(scratch, 0, zero_bytes, stream);
   if (e != cudaSuccess) return e;
   return int4kv_paged_decode(query, k_pool, v_pool, sz_pool, block_table, seq_lens, batch,
