@@ -357,10 +357,13 @@ paged_decode_kernel(DecodeArgs a) {
 
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
-  // this warp's digit staging bytes (4 * D: rows of four digits), dig[g * D + c]
+  // this warp's digit staging bytes (4 rows of D + 32: the padding puts the
+  // four rows a round reads in different banks), dig[g * (D + 32) + c]
   // = digit g (mod 4) of channel c; the page's softmax weights reuse its
   // first 64 bytes between group changes
-  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb + (size_t)warp * 4 * D);
+  constexpr int kDigRow = D + 32;
+  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb +
+                                            (size_t)warp * 4 * kDigRow);
   float* p_tab = reinterpret_cast<float*>(dig);
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
@@ -672,7 +675,7 @@ paged_decode_kernel(DecodeArgs a) {
             const int g = 4 * half + g4;
             const int sh = 49 - 7 * g;
             const long long m = g == 0 ? 0xFF : 0x7F;
-            uint8_t* row = dig + g4 * D + lane * DPL;
+            uint8_t* row = dig + g4 * kDigRow + lane * DPL;
             if constexpr (DPL == 2) {
               *reinterpret_cast<uint16_t*>(row) = (uint16_t)(((X[0] >> sh) & m) | (((X[1] >> sh) & m) << 8));
             } else {
@@ -690,7 +693,8 @@ paged_decode_kernel(DecodeArgs a) {
             for (int e = 0; e < C::KT; ++e) {
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
-                const uint2 v = *reinterpret_cast<const uint2*>(dig + (fg & 3) * D + 64 * e + 32 * h + 8 * ft);
+                const uint2 v =
+                    *reinterpret_cast<const uint2*>(dig + (fg & 3) * kDigRow + 64 * e + 32 * h + 8 * ft);
                 bfrag[2 * e][h] = __byte_perm(v.x, v.y, 0x6420);      // even channels
                 bfrag[2 * e + 1][h] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
               }
@@ -876,7 +880,7 @@ template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
   return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
-         (size_t)kWarps * 4 * D;  // rings, then per-warp digit staging / page weights
+         (size_t)kWarps * 4 * (D + 32);  // rings, then per-warp digit staging / page weights
 }
 
 struct OccCache {
