@@ -209,6 +209,9 @@ def cpu_baseline(arrays, streams, bytes_per_stream, seconds_target=2.0):
         pool.close()
     gbs = reps * len(streams) * bytes_per_stream / wall / 1e9
     return {"value": round(gbs, 4), "unit": "GB/s", "cores": pool.procs, "kind": "port",
+            "host_cpu_count": os.cpu_count(), "host_affinity": len(os.sched_getaffinity(0)),
+            "threads": f"{pool.procs} spawn processes x 1 thread "
+                       "(OMP/OPENBLAS/MKL_NUM_THREADS=1 in each)",
             "sample": f"{len(streams)} of the config's (sequence, head) streams x {reps} reps, "
                       f"oracle online softmax per stream (NumPy, 1 BLAS thread per process, "
                       f"{pool.procs} spawn processes), {wall:.2f} s wall",
@@ -492,6 +495,8 @@ def run_reference(args):
         "dtype": "fp32 (NumPy)", "data": "synthetic (seeded, same distributions as ours)",
         "config": workload_config(shape, args.config, 1),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "host_cpu_count": os.cpu_count(),
+                         "host_affinity": len(os.sched_getaffinity(0)),
                          "sample": f"each step = {sample} of the {len(streams)} (sequence, head) "
                                    "streams of one config step, oracle online softmax "
                                    f"(src/flash_decode_ref.py:30-139 restated), {cores} spawn "
