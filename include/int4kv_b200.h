@@ -274,6 +274,17 @@ cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_po
                                          int num_pages, void* partials, void* workspace,
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream);
+/* The same with the value pool stored as `value_dtype` (INT4KV_VALUES_*);
+ * workspace as int4kv_paged_decode_workspace_size_ex. */
+cudaError_t int4kv_paged_decode_partials_ex(const float* query, const uint8_t* k_pool,
+                                            const void* v_pool, int value_dtype,
+                                            const float* sz_pool, const int32_t* block_table,
+                                            const int32_t* seq_lens, int batch, int num_q_heads,
+                                            int num_kv_heads, int head_dim, int page_tokens,
+                                            int group_tokens, int max_pages, int num_pages,
+                                            void* partials, void* workspace,
+                                            size_t workspace_bytes, uint32_t* status,
+                                            cudaStream_t stream);
 
 /* Combine partials [num_parts][streams] records into out [streams, head_dim]
  * float32: out = sum_p acc_p e^(m_p - M) / max(sum_p l_p e^(m_p - M), 1e-10)

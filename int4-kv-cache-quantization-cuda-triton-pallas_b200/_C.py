@@ -393,8 +393,8 @@ def paged_decode_partials(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
     """
     lib = _lib.load()
     num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
-    if v_pool is None or v_pool.dtype != torch.float32:
-        raise RuntimeError("paged_decode_partials needs a float32 v_pool")
+    if v_pool is None:
+        raise RuntimeError("v_pool is required")
     _check_input(query, "query")
     if query.dtype != torch.float32 or query.dim() != 3:
         raise RuntimeError("query must be float32 [batch, heads, head_dim]")
@@ -412,15 +412,16 @@ def paged_decode_partials(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
             out = torch.empty((nbytes,), dtype=torch.uint8, device=query.device)
         elif out.dtype != torch.uint8 or out.numel() != nbytes or not out.is_contiguous():
             raise RuntimeError(f"partials must be contiguous uint8 [{nbytes}]")
-        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device)
+        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device, v_pool.dtype)
         if workspace is None:
             workspace = torch.zeros((need,), dtype=torch.uint8, device=query.device)
         elif workspace.numel() * workspace.element_size() < need:
             raise RuntimeError(f"workspace needs {need} bytes")
-        _lib.check(lib.int4kv_paged_decode_partials(
-            _p(query), _p(k_pool), _p(v_pool), _p(sz_pool), _p(block_table), _p(seq_lens), b, hq,
-            hkv, d, page, group_tokens, max_pages, num_pages, _p(out), _p(workspace),
-            workspace.numel() * workspace.element_size(), _p(status), _stream(query)),
+        _lib.check(lib.int4kv_paged_decode_partials_ex(
+            _p(query), _p(k_pool), _p(v_pool), VALUE_KINDS[v_pool.dtype], _p(sz_pool),
+            _p(block_table), _p(seq_lens), b, hq, hkv, d, page, group_tokens, max_pages,
+            num_pages, _p(out), _p(workspace), workspace.numel() * workspace.element_size(),
+            _p(status), _stream(query)),
             "paged_decode_partials")
     return out
 

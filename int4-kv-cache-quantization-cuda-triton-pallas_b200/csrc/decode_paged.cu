@@ -1112,12 +1112,26 @@ cudaError_t int4kv_paged_decode_partials(const float* query, const uint8_t* k_po
                                          int num_pages, void* partials, void* workspace,
                                          size_t workspace_bytes, uint32_t* status,
                                          cudaStream_t stream) {
+  return int4kv_paged_decode_partials_ex(query, k_pool, v_pool, INT4KV_VALUES_F32, sz_pool,
+                                         block_table, seq_lens, batch, num_q_heads, num_kv_heads,
+                                         head_dim, page_tokens, group_tokens, max_pages, num_pages,
+                                         partials, workspace, workspace_bytes, status, stream);
+}
+
+cudaError_t int4kv_paged_decode_partials_ex(const float* query, const uint8_t* k_pool,
+                                            const void* v_pool, int value_dtype,
+                                            const float* sz_pool, const int32_t* block_table,
+                                            const int32_t* seq_lens, int batch, int num_q_heads,
+                                            int num_kv_heads, int head_dim, int page_tokens,
+                                            int group_tokens, int max_pages, int num_pages,
+                                            void* partials, void* workspace,
+                                            size_t workspace_bytes, uint32_t* status,
+                                            cudaStream_t stream) {
   if (!partials) return cudaErrorInvalidValue;
-  return paged_entry(query, k_pool, v_pool, INT4KV_VALUES_F32, sz_pool, block_table, seq_lens,
-                     batch, num_q_heads,
-                     num_kv_heads, head_dim, page_tokens, group_tokens, max_pages, num_pages,
-                     nullptr, static_cast<char*>(partials), workspace, workspace_bytes, status,
-                     stream, nullptr, nullptr);
+  return paged_entry(query, k_pool, v_pool, value_dtype, sz_pool, block_table, seq_lens, batch,
+                     num_q_heads, num_kv_heads, head_dim, page_tokens, group_tokens, max_pages,
+                     num_pages, nullptr, static_cast<char*>(partials), workspace, workspace_bytes,
+                     status, stream, nullptr, nullptr);
 }
 
 cudaError_t int4kv_merge_partials(const void* partials, int num_parts, int streams, int head_dim,

@@ -301,8 +301,8 @@ class SequenceSplitDecoder:
         dev = cache.device
         self.rec = partial_record_bytes(d)
         self.partials = torch.empty((h * self.rec,), dtype=torch.uint8, device=dev)
-        self.workspace = torch.zeros((_C.paged_decode_workspace_bytes(1, h, h, d, dev),),
-                                     dtype=torch.uint8, device=dev)
+        self.workspace = torch.zeros((_C.paged_decode_workspace_bytes(
+            1, h, h, d, dev, value_dtype=cache.value_dtype),), dtype=torch.uint8, device=dev)
         self._tables = {}
         self.exchange = exchange
         self.peers = None

@@ -96,3 +96,25 @@ def test_values16_full_anchor_config():
     exact = oracle.decode_paged(q.cpu().numpy(), kp, vp, sp, bt, sl, method="f64", streams=streams)
     for b, h in streams:
         assert np.abs(out[b, h] - exact[b, h]).max() <= EXACT_TOL
+
+
+@pytest.mark.parametrize("value_dtype", [torch.float16, torch.bfloat16])
+def test_sequence_split_partials_with_16bit_values(value_dtype):
+    """Partial records of two group-aligned token ranges over 16-bit value pools
+    merge to the whole-sequence decode (the sequence split's per-GPU step)."""
+    heads, d, L = 4, 128, 3000
+    g = torch.Generator(device="cuda").manual_seed(21)
+    k = torch.randn((L, heads, d), generator=g, device="cuda") * 2 + 0.5
+    v = torch.randn((L, heads, d), generator=g, device="cuda")
+    q = torch.randn((1, heads, d), generator=g, device="cuda")
+    whole = P.PagedKVCache(L // 16 + 8, heads, d, device="cuda", seed=1, value_dtype=value_dtype)
+    whole.write_sequences([0], [k], [v])
+    want = whole.decode(q, [0])
+    parts = []
+    for t0, t1 in [(0, 1280), (1280, L)]:
+        c = P.PagedKVCache(L // 16 + 8, heads, d, device="cuda", seed=2, value_dtype=value_dtype)
+        c.write_sequences([0], [k[t0:t1]], [v[t0:t1]])
+        bt, sl = c.block_table([0])
+        parts.append(C.paged_decode_partials(q, c.k_pool, c.v_pool, c.sz_pool, bt, sl))
+    merged = C.merge_partials(torch.stack(parts).contiguous(), heads, d)
+    assert float((merged.view_as(want) - want).abs().max()) <= 2e-6
