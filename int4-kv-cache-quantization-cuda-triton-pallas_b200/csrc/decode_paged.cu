@@ -1,5 +1,6 @@
-// Fused INT4 paged flash-decoding attention for sm_100a (CUDA cores; the op
-// is HBM-bound GEMV work, so no tensor cores).
+// Fused INT4 paged flash-decoding attention for sm_100a. The op is HBM-bound
+// GEMV work; the tensor cores serve only to cut instructions: each page's
+// code x query sums are four int8 MMAs per warp (see Numerics).
 //
 // Semantics: the reference's online softmax (src/flash_decode_ref.py:30-139),
 // run once per (sequence b, query head h) stream over the pages of kv head
@@ -7,27 +8,28 @@
 // 1/sqrt(d)), keys dequantized as code*scale - zp*scale with the scale/zp of the key's
 // 128-token group, output o / max(l, 1e-10); empty streams give exact zeros.
 //
-// The G query streams of a kv head are adjacent in the work order, so the
-// warps running them read the same pages at about the same time (L2 serves
-// the repeats); each query stream still costs a full page pass of work, so a
-// GQA step takes the time of an MHA step with as many heads as queries.
+// Ring groups (GQA): gs = gcd(G, WARPS) warps share one ring of staged pages
+// and serve gs query heads of the same kv head from it, so a kv page crosses
+// HBM once for those gs queries; each warp still does its own query's logits,
+// softmax and P.V on the page (at config-0 sizes that work, not HBM, sets the
+// pace of a GQA step).
 //
-// Work decomposition (stream-K over pages): the page-heads of all streams are
-// laid end to end in (b, h, page) order -- T of them -- and the grid's NW warps
-// each take one contiguous run of ~T/NW pages, so every warp moves the same
-// number of bytes whatever the length distribution. A warp keeps its own
-// online-softmax state per stream segment. A stream covered by one warp is
-// finished by that warp; otherwise each contributing warp writes an
-// (m, l, acc[D]) partial, bumps the stream's counter, and the warp that
+// Work decomposition (stream-K over pages): the page-heads of all page
+// streams (b, kv-head group) are laid end to end -- T of them -- and the
+// grid's NW ring groups each take one contiguous run of ~T/NW pages, so every
+// group moves the same number of bytes whatever the length distribution. A
+// warp keeps its own online-softmax state per stream segment. A stream covered
+// by one run is finished by its warp; otherwise each contributing warp writes
+// an (m, l, acc[D]) partial, bumps the stream's counter, and the warp that
 // arrives last merges the partials and writes the output (counters reset to
 // zero on the way out, so the workspace stays zero-filled between launches).
 //
-// Data movement: each warp owns a ring of STAGES shared-memory slots and lane 0
-// streams its pages into them with 1-D bulk async copies (cp.async.bulk, the
-// TMA engine without a tensor map) completing on per-slot mbarriers: the valid
-// rows of V (fp32) and of packed K, plus the group's scale/zp and the stream's
-// query when they change. Each copy has one destination CTA; the sources are
-// this GPU's own pools.
+// Data movement: each ring group owns STAGES * gs shared-memory slots and one
+// lane streams its pages into them with 1-D bulk async copies (cp.async.bulk,
+// the TMA engine without a tensor map) completing on per-slot mbarriers: the
+// valid rows of V and of packed K, plus the group's scale/zp and the gs
+// queries when they change. Each copy has one destination CTA; the sources
+// are this GPU's own pools.
 //
 // Numerics: with qs_d = q_d*s_d (exact in float64) and c_d the 4-bit code,
 // the logit is sum_d qs_d*c_d - sum_d q_d*zp_d*s_d, i.e. the key dequantized
