@@ -268,6 +268,15 @@ I4KV_F32X2_OP(sub2_rn, "sub.rn.f32x2")
 I4KV_F32X2_OP(mul2_rn, "mul.rn.f32x2")
 #undef I4KV_F32X2_OP
 
+// Paired fused multiply-add, each lane rounded once: (c0, c1) += (a0 b, a1 b)
+// for one scalar b -- exactly fmaf(a0, b, c0), fmaf(a1, b, c1).
+I4KV_DEVINL void fma2_rn(float& c0, float& c1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%0, %1};\n\tfma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
 // Four codes of one row's channel quad (quant_code_rcp for each, in paired
 // arithmetic), nibble-packed as c0 | c1 << 4 | c2 << 8 | c3 << 12. The low
 // byte of the bits of 1.5 * 2^23 + rint(y) is rint(y) itself, so the codes

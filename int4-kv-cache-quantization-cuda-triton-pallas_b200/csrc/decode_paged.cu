@@ -258,33 +258,27 @@ __device__ __forceinline__ void pv_row(const char* vs, float pt, int t, int lane
     const float* row = reinterpret_cast<const float*>(vs) + t * D;
     if constexpr (DPL == 2) {
       const float2 v = *reinterpret_cast<const float2*>(row + 2 * lane);
-      ps[0] = fmaf(pt, v.x, ps[0]);
-      ps[1] = fmaf(pt, v.y, ps[1]);
+      fma2_rn(ps[0], ps[1], v.x, v.y, pt);
     } else {
 #pragma unroll
       for (int v4 = 0; v4 < DPL / 4; ++v4) {
         const float4 v = *reinterpret_cast<const float4*>(row + v4 * 128 + 4 * lane);
-        ps[4 * v4 + 0] = fmaf(pt, v.x, ps[4 * v4 + 0]);
-        ps[4 * v4 + 1] = fmaf(pt, v.y, ps[4 * v4 + 1]);
-        ps[4 * v4 + 2] = fmaf(pt, v.z, ps[4 * v4 + 2]);
-        ps[4 * v4 + 3] = fmaf(pt, v.w, ps[4 * v4 + 3]);
+        fma2_rn(ps[4 * v4 + 0], ps[4 * v4 + 1], v.x, v.y, pt);
+        fma2_rn(ps[4 * v4 + 2], ps[4 * v4 + 3], v.z, v.w, pt);
       }
     }
   } else {
     const uint16_t* row = reinterpret_cast<const uint16_t*>(vs) + t * D;
     if constexpr (DPL == 2) {
       const float2 v = widen2<VK>(*reinterpret_cast<const uint32_t*>(row + 2 * lane));
-      ps[0] = fmaf(pt, v.x, ps[0]);
-      ps[1] = fmaf(pt, v.y, ps[1]);
+      fma2_rn(ps[0], ps[1], v.x, v.y, pt);
     } else {
 #pragma unroll
       for (int v4 = 0; v4 < DPL / 4; ++v4) {
         const uint2 w = *reinterpret_cast<const uint2*>(row + v4 * 128 + 4 * lane);
         const float2 lo = widen2<VK>(w.x), hi = widen2<VK>(w.y);
-        ps[4 * v4 + 0] = fmaf(pt, lo.x, ps[4 * v4 + 0]);
-        ps[4 * v4 + 1] = fmaf(pt, lo.y, ps[4 * v4 + 1]);
-        ps[4 * v4 + 2] = fmaf(pt, hi.x, ps[4 * v4 + 2]);
-        ps[4 * v4 + 3] = fmaf(pt, hi.y, ps[4 * v4 + 3]);
+        fma2_rn(ps[4 * v4 + 0], ps[4 * v4 + 1], lo.x, lo.y, pt);
+        fma2_rn(ps[4 * v4 + 2], ps[4 * v4 + 3], hi.x, hi.y, pt);
       }
     }
   }
