@@ -420,6 +420,8 @@ def run_ours(args):
         "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
         "config": workload_config(shape, args.config, world),
         "decode_us": round(mean_step * 1e3, 2),
+        "step_us_percentiles": {k: round(float(np.percentile(step_ms, q)) * 1e3, 2)
+                                for k, q in (("p10", 10), ("p50", 50), ("p90", 90), ("max", 100))},
         "hbm_frac_of_peak": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
