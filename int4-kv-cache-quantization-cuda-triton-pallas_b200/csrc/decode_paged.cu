@@ -315,7 +315,10 @@ paged_decode_kernel(DecodeArgs a) {
   // (gs = 1 without GQA: one warp, one ring, one query).
   const int gs = a.gs, gpc = WARPS / gs;
   const int gi = warp / gs, gj = warp - gi * gs;
-  const int depth = STAGES * gs;
+  // slots per ring: STAGES pages per warp alone; a ring group keeps gs pages
+  // in flight (its queries share each page, so it needs fewer bytes in flight
+  // and fits more CTAs per SM)
+  const int depth = gs == 1 ? STAGES : gs;
   const int sb = C::Q_OFF + gs * D * 4;  // stage bytes with gs queries
   const bool leader = gj == 0;
   {  // the block table into L2 while the lengths load (first descriptors hit L2)
@@ -358,7 +361,7 @@ paged_decode_kernel(DecodeArgs a) {
   // = digit g (mod 4) of channel c; the page's softmax weights reuse its
   // first 64 bytes between group changes
   constexpr int kDigRow = D + 32;
-  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)WARPS * STAGES * sb +
+  uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)gpc * depth * sb +
                                             (size_t)warp * 4 * kDigRow);
   float* p_tab = reinterpret_cast<float*>(dig);
   if (leader && lane == 0) {
@@ -875,7 +878,8 @@ int ring_group(int num_q_heads, int num_kv_heads) {
 template <int D, int VK>
 size_t dyn_smem(int batch, int gs) {
   using C = Cfg<D, kWarps, kStages, VK>;
-  return 256 + pfx_bytes(batch) + (size_t)kWarps * kStages * (C::Q_OFF + (size_t)gs * D * 4) +
+  const size_t ring_slots = gs == 1 ? (size_t)kWarps * kStages : (size_t)kWarps;  // groups x depth
+  return 256 + pfx_bytes(batch) + ring_slots * (C::Q_OFF + (size_t)gs * D * 4) +
          (size_t)kWarps * 4 * (D + 32);  // rings, then per-warp digit staging / page weights
 }
 
