@@ -77,10 +77,8 @@ struct Cfg {
   static constexpr int SZ_OFF = K_OFF + kPage * D / 2;
   static constexpr int Q_OFF = SZ_OFF + 2 * D * 4;
   static constexpr int STAGE_BYTES = Q_OFF + D * 4;  // one query (gs == 1)
-  static constexpr int P_BYTES = kPage * 4;  // per-warp softmax weights of the current page
-  static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + P_BYTES;
   static constexpr int REC_BYTES = 16 + 4 * D;  // [m f64][l f64][acc D f32]
-  static_assert(STAGE_BYTES % 16 == 0 && WARP_BYTES % 16 == 0, "stage alignment");
+  static_assert(Q_OFF % 16 == 0 && STAGE_BYTES % 16 == 0, "stage alignment");
 };
 
 // Workspace layout (zero-filled before first use; every completed launch
@@ -815,13 +813,13 @@ paged_decode_kernel(DecodeArgs a) {
 template <int D>
 __global__ void __launch_bounds__(256) merge_partials_kernel(const char* parts, int num_parts,
                                                               int streams, float* out) {
-  using C = Cfg<D, 1, 1>;
-  constexpr int DPL = C::DPL;
+  constexpr int DPL = D / 32;
+  constexpr int REC_BYTES = 16 + 4 * D;  // [m f64][l f64][acc D f32]
   const int lane = threadIdx.x & 31;
   const long long s = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (s >= streams) return;
-  const size_t stride = (size_t)streams * C::REC_BYTES;
-  const char* base = parts + (size_t)s * C::REC_BYTES;
+  const size_t stride = (size_t)streams * REC_BYTES;
+  const char* base = parts + (size_t)s * REC_BYTES;
   double M = -INFINITY;
   for (int p = 0; p < num_parts; ++p) M = fmax(M, *reinterpret_cast<const double*>(base + p * stride));
   double L = 0.0, O[DPL];
