@@ -59,7 +59,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=300)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-quantizer", action="store_true")
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl", "fused"],
                     help="sequence split (cfg4_long, N>1): fused peer-memory exchange kernel "
                          "or NCCL all-gather + merge kernel")
     ap.add_argument("--values", default="f32", choices=["f32", "f16", "bf16"],
@@ -533,8 +533,10 @@ def run_reference(args):
 def run_split(args):
     """One long sequence split across the ranks by 128-token groups; a step is
     each rank's partial decode + the exchange of the partial records and their
-    merge: one fused peer-memory kernel (``--exchange p2p``) or one NCCL
-    all-gather + the merge kernel (``--exchange nccl``). Total work is fixed as
+    merge: one fused peer-memory kernel (``--exchange p2p``), one NCCL
+    all-gather + the merge kernel (``--exchange nccl``), or no separate step at
+    all (``--exchange fused``: the decode kernel pushes, waits and merges
+    itself). Total work is fixed as
     N grows (strong scaling)."""
     import datetime
     import importlib
@@ -608,9 +610,14 @@ def run_split(args):
     if dec.peer_status():
         raise RuntimeError(f"peer exchange reported status {dec.peer_status()} in the timed loop")
     total = shape.algorithmic_bytes()
-    step_desc = ("partial decode kernel + fused peer-exchange/merge kernel (NVLink stores, "
-                 "flags, bounded waits; no NCCL)" if args.exchange == "p2p" else
-                 "partial decode kernel + NCCL all-gather + merge kernel")
+    step_desc = {
+        "p2p": "partial decode kernel + fused peer-exchange/merge kernel (NVLink stores, "
+               "flags, bounded waits; no NCCL)",
+        "nccl": "partial decode kernel + NCCL all-gather + merge kernel",
+        "fused": "one kernel: decode, push of each stream's record to every rank over "
+                 "NVLink as its pages finish, bounded wait for the peers' records and "
+                 "their merge (no NCCL)",
+    }[args.exchange]
     peak, peak_kind = measured_peak()
     value = total / (mean * 1e-3) / 1e9
     if rank == 0:
@@ -627,7 +634,7 @@ def run_split(args):
                        "l2": "flushed before every timed step",
                        "parallelism": f"sequence split x{world}"},
             "hbm_frac_of_peak": round(value / world / peak, 4), "peak_source": peak_kind,
-            "gpu_launches": K * 2,
+            "gpu_launches": K * (1 if args.exchange == "fused" else 2),
             "step": "CUDA graph: " + step_desc,
             "parity": {"max_abs_vs_whole_sequence_decode": gate_err},
         }), flush=True)

@@ -323,6 +323,31 @@ cudaError_t int4kv_ipc_handle(const void* dev_ptr, void* handle);
 cudaError_t int4kv_ipc_open(const void* handle, void** dev_ptr);
 cudaError_t int4kv_ipc_close(void* dev_ptr);
 
+/* The sequence split in ONE launch: the paged decode fused with the exchange
+ * over NVLink peer memory. Every stream's GPU-local (m, l, acc) is stored
+ * straight into every rank's exchange buffer the moment it is final (plain
+ * stores through the peer mappings, then a per-stream flag with release
+ * semantics at system scope); each warp, after all of its pushes, waits
+ * (bounded, 2 s; then INT4KV_STATUS_PEER_TIMEOUT and NaN) for the other
+ * ranks' flags of the streams it finished and merges the ranks' records into
+ * out [batch, num_q_heads, head_dim] -- the full attention output, on every
+ * rank. peer_bufs[r] = rank r's buffer as mapped on this GPU (the own one
+ * for r == rank; int4kv_exchange_alloc + int4kv_ipc_open), each
+ * int4kv_paged_decode_split_bytes large, 128-byte aligned, zero-filled once;
+ * world <= INT4KV_EXCHANGE_MAX_RANKS. Every rank launches it once per step
+ * with the same batch and heads. The workspace is that of
+ * int4kv_paged_decode_workspace_size_ex. */
+cudaError_t int4kv_paged_decode_split_bytes(int batch, int num_q_heads, int head_dim,
+                                            size_t* bytes);
+cudaError_t int4kv_paged_decode_split(const float* query, const uint8_t* k_pool,
+                                      const void* v_pool, int value_dtype, const float* sz_pool,
+                                      const int32_t* block_table, const int32_t* seq_lens,
+                                      int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                      int page_tokens, int group_tokens, int max_pages,
+                                      int num_pages, void* const* peer_bufs, int world, int rank,
+                                      float* out, void* workspace, size_t workspace_bytes,
+                                      uint32_t* status, cudaStream_t stream);
+
 /* Scratch capacity of int4kv_paged_decode_static_scratch, per device: a
  * file-scope device array in the library (8 MiB; enough for 8192 streams at
  * head_dim 128). */

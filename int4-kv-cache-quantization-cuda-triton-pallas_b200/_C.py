@@ -542,3 +542,58 @@ def rope(x, positions, cos, sin, out=None, status=None):
         _lib.check(lib.int4kv_rope(_p(x), _p(positions), rows, h, d, _p(cos), _p(sin),
                                    cos.shape[0], _p(out), _p(status), _stream(x)), "rope")
     return out
+
+
+def paged_decode_split_bytes(batch, q_heads, head_dim):
+    """Bytes of one rank's exchange buffer for the fused split decode."""
+    import ctypes
+    n = ctypes.c_size_t(0)
+    _lib.check(_lib.load().int4kv_paged_decode_split_bytes(batch, q_heads, head_dim,
+                                                           ctypes.byref(n)),
+               "paged_decode_split_bytes")
+    return n.value
+
+
+def paged_decode_split(query, k_pool, v_pool, sz_pool, block_table, seq_lens, peer_bufs, rank,
+                       group_tokens=128, out=None, workspace=None, status=None):
+    """The sequence split in one launch (int4kv_paged_decode_split): this rank's
+    token range decoded and merged with every rank's records through the peer
+    exchange buffers ``peer_bufs`` (addresses in rank order, as mapped here).
+    Returns the full attention output [batch, heads, head_dim] float32."""
+    import ctypes
+    lib = _lib.load()
+    num_pages, hkv, page, d = _check_pools(k_pool, v_pool, sz_pool)
+    if v_pool is None:
+        raise RuntimeError("v_pool is required")
+    _check_input(query, "query")
+    if query.dtype != torch.float32 or query.dim() != 3:
+        raise RuntimeError("query must be float32 [batch, heads, head_dim]")
+    b, hq, qd = query.shape
+    if qd != d or hq < hkv or hq % hkv:
+        raise RuntimeError("query must be [batch, G * kv_heads, pool head_dim]")
+    max_pages = _check_table(block_table, b)
+    _check_input(seq_lens, "seq_lens")
+    if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,):
+        raise RuntimeError("seq_lens must be int32 [batch]")
+    if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
+        raise RuntimeError("status must be an int32 tensor")
+    _same_device(query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, workspace, status)
+    world = len(peer_bufs)
+    arr = (ctypes.c_void_p * max(world, 1))(*[int(p) for p in peer_bufs])
+    with torch.cuda.device(query.device):
+        if out is None:
+            out = torch.empty((b, hq, d), dtype=torch.float32, device=query.device)
+        elif out.dtype != torch.float32 or tuple(out.shape) != (b, hq, d) or not out.is_contiguous():
+            raise RuntimeError("out must be contiguous float32 [batch, heads, head_dim]")
+        need = paged_decode_workspace_bytes(b, hq, hkv, d, query.device, v_pool.dtype)
+        if workspace is None:
+            workspace = torch.zeros((need,), dtype=torch.uint8, device=query.device)
+        elif workspace.numel() * workspace.element_size() < need:
+            raise RuntimeError(f"workspace needs {need} bytes")
+        _lib.check(lib.int4kv_paged_decode_split(
+            _p(query), _p(k_pool), _p(v_pool), VALUE_KINDS[v_pool.dtype], _p(sz_pool),
+            _p(block_table), _p(seq_lens), b, hq, hkv, d, page, group_tokens, max_pages,
+            num_pages, arr, world, rank, _p(out), _p(workspace),
+            workspace.numel() * workspace.element_size(), _p(status), _stream(query)),
+            "paged_decode_split")
+    return out

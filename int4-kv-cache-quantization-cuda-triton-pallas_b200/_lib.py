@@ -52,6 +52,10 @@ _PROTOS = {
                                        + [_c_int] * 8 + [_c_void_p, _c_void_p, _c_size_t,
                                                          _c_void_p, _c_void_p],
     "int4kv_merge_partials": [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p],
+    "int4kv_paged_decode_split_bytes": [_c_int, _c_int, _c_int, _c_size_p],
+    "int4kv_paged_decode_split": [_c_void_p, _c_void_p, _c_void_p, _c_int] + [_c_void_p] * 3
+                                 + [_c_int] * 8 + [_c_void_p, _c_int, _c_int]
+                                 + [_c_void_p, _c_void_p, _c_size_t, _c_void_p, _c_void_p],
     "int4kv_exchange_bytes": [_c_int, _c_int, _c_int, _c_size_p],
     "int4kv_exchange_merge": [_c_void_p, _c_void_p] + [_c_int] * 4 + [_c_void_p] * 3,
     "int4kv_exchange_alloc": [_c_int, _c_size_t, ctypes.POINTER(_c_void_p)],

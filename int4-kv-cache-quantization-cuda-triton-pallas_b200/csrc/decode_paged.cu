@@ -58,6 +58,21 @@ using namespace i4kv;
 namespace {
 
 constexpr int kPage = 16;
+constexpr int kXRanks = INT4KV_EXCHANGE_MAX_RANKS;
+constexpr uint64_t kPeerWaitNs = 2000000000ull;  // bounded waits on other GPUs: 2 s
+
+// Exchange buffer of the fused split decode, per rank, S query streams:
+//   step u32 [S]                 steps this rank completed for each stream
+//   flag u32 [2][kXRanks][S]     flag[parity][src][s] = step of rank src
+//   recs     [2][kXRanks][S]     records pushed by rank src for that step
+__host__ __device__ inline size_t x_align(size_t v) { return (v + 127) / 128 * 128; }
+__host__ __device__ inline size_t x_off_flag(long long S) { return x_align((size_t)S * 4); }
+__host__ __device__ inline size_t x_off_recs(long long S) {
+  return x_off_flag(S) + x_align((size_t)2 * kXRanks * S * 4);
+}
+__host__ __device__ inline size_t x_bytes(long long S, int d) {
+  return x_off_recs(S) + (size_t)2 * kXRanks * S * (16 + 4 * (size_t)d);
+}
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of wall time
 
@@ -106,6 +121,11 @@ struct DecodeArgs {
   int group_q;     // multiple: query head h reads kv head h / group_q (GQA)
   int gs;          // warps sharing one ring (query heads served per staged page)
   int vheads;      // heads / gs: the page streams of the work decomposition
+  // Fused sequence-split exchange (xworld > 0): every stream's GPU-local
+  // (m, l, acc) goes to every rank's exchange buffer, and the final output is
+  // the merge of all ranks' records. xbuf[r] = rank r's buffer as mapped here.
+  int xworld, xrank;
+  char* xbuf[kXRanks];
 };
 
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
@@ -292,6 +312,120 @@ __device__ __forceinline__ float exp_neg(double x) {
   return r;
 }
 
+// Fused split exchange, push side: store this GPU's (m, l, acc) of query
+// stream qs into every rank's buffer (plain 16-byte stores through the peer
+// mappings), then raise this rank's flag for qs there (release, system scope).
+// No waiting: a warp pushes everything it owns before it waits on anything.
+template <int D>
+__device__ __forceinline__ void x_push(const DecodeArgs& a, long long S, long long qs, double m,
+                                       double l, const float* o, int lane) {
+  constexpr int REC = 16 + 4 * D;
+  const uint32_t E = reinterpret_cast<const uint32_t*>(a.xbuf[a.xrank])[qs] + 1u;
+  const int par = (int)(E & 1u);
+  for (int r = 0; r < a.xworld; ++r) {
+    char* rec = a.xbuf[r] + x_off_recs(S) + (((size_t)par * kXRanks + a.xrank) * S + qs) * REC;
+    if (lane == 0) {
+      *reinterpret_cast<double*>(rec) = m;
+      *reinterpret_cast<double*>(rec + 8) = l;
+    }
+    store_lane_vec<D>(reinterpret_cast<float*>(rec + 16), o, lane);
+  }
+  fence_acq_rel_sys();
+  __syncwarp();
+  if (lane < a.xworld) {
+    uint32_t* f = reinterpret_cast<uint32_t*>(a.xbuf[lane] + x_off_flag(S)) +
+                  ((size_t)par * kXRanks + a.xrank) * S + qs;
+    st_release_sys(f, E);
+  }
+}
+
+// Fused split exchange, merge side: wait (bounded) for every rank's flag of
+// qs in this rank's buffer, then merge the ranks' records -- the reference's
+// LSE merge (csrc/flash_decode_int4.cu:199-220) across GPUs, in float64 --
+// into the output. A rank that does not arrive within 2 s gives NaN and
+// INT4KV_STATUS_PEER_TIMEOUT instead of a hang. `dead` is the warp's record of
+// an earlier timeout: its later streams give up without waiting again, so a
+// lost peer costs a warp one wait, not one per stream.
+template <int D>
+__device__ __forceinline__ void x_finish(const DecodeArgs& a, long long S, long long qs, int lane,
+                                         bool& dead) {
+  constexpr int REC = 16 + 4 * D;
+  constexpr int DPL = D / 32;
+  char* own = a.xbuf[a.xrank];
+  uint32_t* step = reinterpret_cast<uint32_t*>(own);
+  const uint32_t E = step[qs] + 1u;
+  const int par = (int)(E & 1u);
+  bool ok = true;
+  if (lane < a.xworld) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(own + x_off_flag(S)) +
+                        ((size_t)par * kXRanks + lane) * S + qs;
+    ok = ld_acquire_sys(f) == E;
+    if (!ok && !dead) {
+      const uint64_t t0 = global_ns();
+      while (!(ok = ld_acquire_sys(f) == E)) {
+        if (global_ns() - t0 > kPeerWaitNs) break;
+        __nanosleep(256);
+      }
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  dead = dead || !ok;
+  if (lane == 0) step[qs] = E;
+  float o[DPL];
+  if (!ok) {
+    if (lane == 0) set_status(a.status, kStatusPeerTimeout);
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) o[k] = __int_as_float(0x7fc00000);
+  } else {
+    const char* base = own + x_off_recs(S) + ((size_t)par * kXRanks * S + qs) * REC;
+    const size_t stride = (size_t)S * REC;
+    double M = -INFINITY;
+    for (int r = 0; r < a.xworld; ++r)
+      M = fmax(M, __ldcg(reinterpret_cast<const double*>(base + r * stride)));
+    double L = 0.0, O[DPL];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) O[k] = 0.0;
+    if (M != -INFINITY) {
+      for (int r = 0; r < a.xworld; ++r) {
+        const char* rec = base + r * stride;
+        const double m = __ldcg(reinterpret_cast<const double*>(rec));
+        if (m == -INFINITY) continue;
+        const double e = exp(m - M);
+        L = fma(__ldcg(reinterpret_cast<const double*>(rec + 8)), e, L);
+        float v[DPL];
+        load_lane_vec_cg<D>(reinterpret_cast<const float*>(rec + 16), v, lane);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
+      }
+    }
+    const double den = fmax(L, 1e-10);
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
+  }
+  store_lane_vec<D>(a.out + (size_t)qs * D, o, lane);
+}
+
+// Streams without a page on this GPU (its token range of them is empty) still
+// take part in the exchange: group gw pushes, then finishes, the empty
+// records of streams gw, gw + NW, ...
+template <int D>
+__device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* s_pfx, long long S,
+                                                long long gw, long long NW, int gs, int gj, int lane,
+                                                bool finish, bool& dead) {
+  constexpr int DPL = D / 32;
+  float z[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) z[k] = 0.f;
+  const long long SV = (long long)a.batch * a.vheads;
+  for (long long vs = gw; vs < SV; vs += NW) {
+    const int b = (int)(vs / a.vheads);
+    if (s_pfx[b + 1] != s_pfx[b]) continue;
+    const long long qs = vs * gs + gj;
+    if (finish) x_finish<D>(a, S, qs, lane, dead);
+    else x_push<D>(a, S, qs, -INFINITY, 0.0, z, lane);
+  }
+}
+
 // 16-bit value pools halve the stage size, so four CTAs fit an SM's shared
 // memory; registers are capped to let them all be resident (measured: 6 %
 // faster at 32K context than three CTAs with uncapped registers).
@@ -333,7 +467,7 @@ paged_decode_kernel(DecodeArgs a) {
   for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < streams;
        s += (long long)gridDim.x * blockDim.x) {
     const int b = (int)(s / a.heads);
-    if (s_pfx[b + 1] == s_pfx[b]) {
+    if (s_pfx[b + 1] == s_pfx[b] && a.xworld == 0) {
       float* dst = a.out + (size_t)s * D;
       if (a.part_out) {
         char* rec = a.part_out + (size_t)s * C::REC_BYTES;
@@ -350,7 +484,15 @@ paged_decode_kernel(DecodeArgs a) {
   const long long gw = (long long)blockIdx.x * gpc + gi;
   const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
   const int n = g1 - g0;
-  if (n <= 0) return;
+  const bool xmode = a.xworld > 0;
+  if (n <= 0) {
+    if (xmode) {  // no pages here, but maybe empty streams to exchange
+      bool dead = false;
+      x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, false, dead);
+      x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, true, dead);
+    }
+    return;
+  }
 
   uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
@@ -401,6 +543,7 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
   for (int k = 0; k < 2 * C::KT; ++k) { bfrag[k][0] = 0u; bfrag[k][1] = 0u; }
 
+  int xm0 = -1, xm1 = -1;  // exchange mode: streams this warp merged locally (at most 2)
   int* counters = reinterpret_cast<int*>(a.ws);
   char* recs = a.ws + cnt_bytes(streams);
 
@@ -437,10 +580,11 @@ paged_decode_kernel(DecodeArgs a) {
     const size_t qstream = (size_t)stream * gs + gj;
     const double lsum = lane_sum();
     float o[DPL];
-    if (a.part_out) {
+    if (a.part_out || xmode) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-      put_record(a.part_out + qstream * C::REC_BYTES, m_run, lsum, o);
+      if (xmode) x_push<D>(a, streams, (long long)qstream, m_run, lsum, o, lane);
+      else put_record(a.part_out + qstream * C::REC_BYTES, m_run, lsum, o);
       return;
     }
     const double den = fmax(lsum, 1e-10);
@@ -505,10 +649,15 @@ paged_decode_kernel(DecodeArgs a) {
     }
     const size_t qstream = (size_t)stream * gs + gj;
     float o[DPL];
-    if (a.part_out) {  // partial mode: the merged (M, L, O) of this GPU's share of the stream
+    if (a.part_out || xmode) {  // the merged (M, L, O) of this GPU's share of the stream
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
-      put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
+      if (xmode) {
+        x_push<D>(a, streams, (long long)qstream, M, L, o, lane);
+        (xm0 < 0 ? xm0 : xm1) = stream;  // finished after the warp's last push
+      } else {
+        put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
+      }
       return;
     }
     const double den = fmax(L, 1e-10);
@@ -803,6 +952,24 @@ paged_decode_kernel(DecodeArgs a) {
     return;
   }
   end_run();
+  if (xmode) {
+    // every push of this warp is out; now wait for the other ranks and merge:
+    // the streams it finished alone (the interior of its run), the ones it
+    // merged as the last local arrival, and its share of the empty streams
+    bool dead = false;
+    x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, false, dead);
+    const int v_first = make_desc(a, s_pfx, g0, g0, g1).stream;
+    const int v_last = make_desc(a, s_pfx, g1 - 1, g0, g1).stream;
+    for (int vs = v_first; vs <= v_last; ++vs) {
+      const int b = vs / a.vheads;
+      if (s_pfx[b + 1] == s_pfx[b]) continue;  // no pages here: an empty stream's duty
+      long long lo, hi;
+      if (contributors_of(vs, lo, hi) == 1) x_finish<D>(a, streams, (long long)vs * gs + gj, lane, dead);
+    }
+    if (xm0 >= 0) x_finish<D>(a, streams, (long long)xm0 * gs + gj, lane, dead);
+    if (xm1 >= 0) x_finish<D>(a, streams, (long long)xm1 * gs + gj, lane, dead);
+    x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, true, dead);
+  }
 }
 
 // Merge per-GPU partial records [parts][streams] of one decode step into
@@ -1015,7 +1182,8 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v
                         int page_tokens, int group_tokens, int max_pages, int num_pages,
                         float* out, char* part_out, void* workspace, size_t workspace_bytes,
                         uint32_t* status, cudaStream_t stream, cudaEvent_t ev_before,
-                        cudaEvent_t ev_after) {
+                        cudaEvent_t ev_after, int xworld = 0, int xrank = 0,
+                        void* const* xbufs = nullptr) {
   if (batch <= 0 || batch > kMaxPagedBatch || num_kv_heads <= 0 || num_q_heads < num_kv_heads ||
       num_q_heads % num_kv_heads != 0)
     return cudaErrorInvalidValue;
@@ -1033,6 +1201,16 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v
                part_out, num_kv_heads, num_q_heads / num_kv_heads,
                ring_group(num_q_heads, num_kv_heads), 0};
   a.vheads = num_q_heads / a.gs;
+  if (xworld > 0) {  // fused split exchange: outputs merged over the ranks' records
+    if (xworld > kXRanks || xrank < 0 || xrank >= xworld || !xbufs || part_out || !out)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < xworld; ++r) {
+      if (!xbufs[r] || (reinterpret_cast<uintptr_t>(xbufs[r]) & 127u)) return cudaErrorInvalidValue;
+      a.xbuf[r] = static_cast<char*>(xbufs[r]);
+    }
+    a.xworld = xworld;
+    a.xrank = xrank;
+  }
   switch (head_dim) {
     case 64: return launch_kind<64>(vk, a, workspace_bytes, stream, ev_before, ev_after);
     case 128: return launch_kind<128>(vk, a, workspace_bytes, stream, ev_before, ev_after);
@@ -1146,6 +1324,29 @@ cudaError_t int4kv_merge_partials(const void* partials, int num_parts, int strea
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t int4kv_paged_decode_split_bytes(int batch, int num_q_heads, int head_dim,
+                                            size_t* bytes) {
+  if (!bytes || batch <= 0 || num_q_heads <= 0) return cudaErrorInvalidValue;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return cudaErrorInvalidValue;
+  *bytes = x_bytes((long long)batch * num_q_heads, head_dim);
+  return cudaSuccess;
+}
+
+cudaError_t int4kv_paged_decode_split(const float* query, const uint8_t* k_pool,
+                                      const void* v_pool, int value_dtype, const float* sz_pool,
+                                      const int32_t* block_table, const int32_t* seq_lens,
+                                      int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                      int page_tokens, int group_tokens, int max_pages,
+                                      int num_pages, void* const* peer_bufs, int world, int rank,
+                                      float* out, void* workspace, size_t workspace_bytes,
+                                      uint32_t* status, cudaStream_t stream) {
+  if (world <= 0 || !peer_bufs) return cudaErrorInvalidValue;
+  return paged_entry(query, k_pool, v_pool, value_dtype, sz_pool, block_table, seq_lens, batch,
+                     num_q_heads, num_kv_heads, head_dim, page_tokens, group_tokens, max_pages,
+                     num_pages, out, nullptr, workspace, workspace_bytes, status, stream, nullptr,
+                     nullptr, world, rank, peer_bufs);
 }
 
 cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const float* v_pool,

@@ -20,7 +20,11 @@ Two layouts, both of which keep every KV page on the GPU that owns it:
   ``exchange="p2p"`` the gather and the merge are one kernel instead
   (``PeerExchange``): each rank stores its records straight into every
   rank's buffer over NVLink (CUDA IPC mappings), raises a flag per chunk of
-  streams, waits (bounded) for the peers' flags and merges.
+  streams, waits (bounded) for the peers' flags and merges. With
+  ``exchange="fused"`` the whole step is ONE kernel
+  (``int4kv_paged_decode_split``): the decode itself pushes each stream's
+  GPU-local result to every rank as soon as it is final and merges the
+  ranks' records at the end, so the exchange overlaps the decode.
 
 Failure detection stays on the host: ``PeerMonitor`` has every rank post a
 heartbeat key to the process group's store before each collective step and
@@ -210,6 +214,18 @@ def exchange_layout(streams: int, head_dim: int) -> dict:
             "bytes": off_recs + 2 * EXCHANGE_MAX_RANKS * streams * rec}
 
 
+def split_layout(streams: int, head_dim: int) -> dict:
+    """Byte offsets of one rank's buffer for the fused split decode
+    (``int4kv_paged_decode_split``): ``step u32[S]``, ``flag u32[2][8][S]``,
+    ``recs [2][8][S]`` records, per query stream. Used by tests that stand in
+    for a peer on the host."""
+    off_flag = _align128(streams * 4)
+    off_recs = off_flag + _align128(2 * EXCHANGE_MAX_RANKS * streams * 4)
+    rec = partial_record_bytes(head_dim)
+    return {"off_flag": off_flag, "off_recs": off_recs, "record": rec,
+            "bytes": off_recs + 2 * EXCHANGE_MAX_RANKS * streams * rec}
+
+
 class _DeviceBytes:
     """``__cuda_array_interface__`` of a raw device allocation (uint8)."""
 
@@ -235,7 +251,8 @@ class PeerExchange:
     before unmapping, so no peer is still writing).
     """
 
-    def __init__(self, rank: int, world: int, streams: int, head_dim: int, device, group=None):
+    def __init__(self, rank: int, world: int, streams: int, head_dim: int, device, group=None,
+                 nbytes: Optional[int] = None):
         import torch.distributed as dist
         if not 1 <= world <= EXCHANGE_MAX_RANKS:
             raise ValueError(f"the peer exchange supports 1..{EXCHANGE_MAX_RANKS} ranks")
@@ -243,7 +260,8 @@ class PeerExchange:
         self.streams, self.head_dim = streams, head_dim
         self.device = torch.device(device)
         idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        self.nbytes = _C.exchange_bytes(world, streams, head_dim)
+        # the buffer of the separate exchange kernel, or `nbytes` for another layout
+        self.nbytes = nbytes if nbytes is not None else _C.exchange_bytes(world, streams, head_dim)
         self.own = _C.exchange_alloc(idx, self.nbytes)
         self._opened = []
         handles = [None] * world
@@ -293,8 +311,8 @@ class SequenceSplitDecoder:
 
     def __init__(self, cache, rank: int, world: int, group=None, monitor: Optional[PeerMonitor] = None,
                  exchange: str = "nccl"):
-        if exchange not in ("nccl", "p2p"):
-            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        if exchange not in ("nccl", "p2p", "fused"):
+            raise ValueError("exchange must be 'nccl', 'p2p' or 'fused'")
         self.cache, self.rank, self.world, self.group = cache, rank, world, group
         self.monitor = monitor
         d, h = cache.head_dim, cache.heads
@@ -309,6 +327,10 @@ class SequenceSplitDecoder:
         if exchange == "p2p":
             self.peers = PeerExchange(rank, world, h, d, dev, group)
             self.out = torch.empty((h, d), dtype=torch.float32, device=dev)
+        elif exchange == "fused":  # one launch: decode + exchange + merge
+            self.peers = PeerExchange(rank, world, h, d, dev, group,
+                                      nbytes=_C.paged_decode_split_bytes(1, h, d))
+            self.out = torch.empty((1, h, d), dtype=torch.float32, device=dev)
 
     def refresh(self) -> None:
         """Forget cached block tables (call after the cache's pages change)."""
@@ -324,6 +346,14 @@ class SequenceSplitDecoder:
         return self.partials
 
     def _step(self, query: torch.Tensor, seq_id: int) -> torch.Tensor:
+        if self.exchange == "fused":
+            if seq_id not in self._tables:
+                self._tables[seq_id] = self.cache.block_table([seq_id])
+            bt, sl = self._tables[seq_id]
+            return _C.paged_decode_split(query, self.cache.k_pool, self.cache.v_pool,
+                                         self.cache.sz_pool, bt, sl, self.peers.ptrs, self.rank,
+                                         self.cache.group_tokens, out=self.out,
+                                         workspace=self.workspace, status=self.peers.status)
         parts = self.local_partials(query, seq_id)
         if self.peers is not None:
             return self.peers.merge(parts, self.out).view(1, self.cache.heads, self.cache.head_dim)

@@ -1,12 +1,13 @@
 """Sequence split across GPUs, one process per GPU (run under torchrun).
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 tests/dist_sequence_split.py \
-        [L] [heads] [nccl|p2p]
+        [L] [heads] [nccl|p2p|fused]
 
 Every rank generates the same seeded sequence, keeps its group-aligned token
 range in a paged cache on its own GPU, decodes it into partial records, and
-``SequenceSplitDecoder`` exchanges the records -- one NCCL all-gather, or the
-fused peer-memory exchange kernel (``p2p``) -- and merges them. Each rank checks the merged output against a whole-sequence
+``SequenceSplitDecoder`` exchanges the records -- one NCCL all-gather, the
+peer-memory exchange kernel (``p2p``), or inside the decode kernel itself
+(``fused``) -- and merges them. Each rank checks the merged output against a whole-sequence
 decode on its own GPU; exit status 0 means every rank matched.
 """
 

@@ -141,3 +141,99 @@ def test_peer_exchange_single_rank_decoder():
         assert float((got - want).abs().max()) <= 2e-6
     finally:
         dec.close()
+
+
+# ---------------------------------------------------------------------------
+# the fused split decode: decode + exchange + merge in one launch
+# ---------------------------------------------------------------------------
+
+def _split_caches(L, heads, d, world, seed):
+    P = pkg("paged")
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    k = torch.randn((L, heads, d), generator=g, device="cuda") * 2.0 + 0.5
+    v = torch.randn((L, heads, d), generator=g, device="cuda")
+    caches = []
+    for t0, t1 in par.plan_sequence_split(L, world):
+        c = P.PagedKVCache((t1 - t0 + 15) // 16 + 4, heads, d, device="cuda", seed=t0)
+        c.write_sequences([0], [k[t0:t1]], [v[t0:t1]])
+        caches.append(c)
+    whole = P.PagedKVCache((L + 15) // 16 + 4, heads, d, device="cuda", seed=1)
+    whole.write_sequences([0], [k], [v])
+    return caches, whole, g
+
+
+@pytest.mark.parametrize("world,our,L,heads,d", [(2, 0, 3000, 8, 128), (4, 2, 2000, 4, 64),
+                                                 (8, 7, 700, 4, 128), (3, 1, 5000, 2, 256)])
+def test_fused_split_equals_merge(world, our, L, heads, d):
+    """Rank `our` runs the fused kernel on its token range; the other ranks'
+    records and flags are written into its buffer beforehand. Output = the
+    merge of all ranks' partial records, bit for bit (and the whole-sequence
+    decode to rounding); its own records land in every rank's buffer. With
+    (8, 7, 700) rank 7's range is empty, so only the empty-stream path runs."""
+    caches, whole, g = _split_caches(L, heads, d, world, seed=world + d)
+    lay = par.split_layout(heads, d)
+    n = C.paged_decode_split_bytes(1, heads, d)
+    assert n == lay["bytes"]
+    ptrs = [C.exchange_alloc(torch.cuda.current_device(), n) for _ in range(world)]
+    views = [par.device_bytes(p, n, "cuda") for p in ptrs]
+    rec = lay["record"]
+
+    def recs(buf, parity, src):
+        o = lay["off_recs"] + (parity * par.EXCHANGE_MAX_RANKS + src) * heads * rec
+        return views[buf][o:o + heads * rec]
+
+    def flags(buf, parity, src):
+        o = lay["off_flag"] + (parity * par.EXCHANGE_MAX_RANKS + src) * heads * 4
+        return views[buf][o:o + heads * 4].view(torch.int32)
+
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    try:
+        for step in (1, 2, 3):
+            parity = step & 1
+            q = torch.randn((1, heads, d), generator=g, device="cuda")
+            parts = []
+            for c in caches:
+                bt, sl = c.block_table([0])
+                parts.append(C.paged_decode_partials(q, c.k_pool, c.v_pool, c.sz_pool, bt, sl))
+            for r in range(world):  # the others' pushes, as they would arrive over NVLink
+                if r != our:
+                    recs(our, parity, r).copy_(parts[r])
+                    flags(our, parity, r).fill_(step)
+            me = caches[our]
+            bt, sl = me.block_table([0])
+            # buffer order: rank r's buffer at index r (ours is `our`)
+            out = C.paged_decode_split(q, me.k_pool, me.v_pool, me.sz_pool, bt, sl, ptrs, our,
+                                       status=status)
+            want = C.merge_partials(torch.stack(parts).contiguous(), heads, d).view(1, heads, d)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            assert torch.equal(out, want), float((out - want).abs().max())
+            assert float((out - whole.decode(q, [0])).abs().max()) <= 2e-6
+            for dst in range(world):  # our record and flag reached every rank's buffer
+                assert torch.equal(recs(dst, parity, our), parts[our])
+                assert bool((flags(dst, parity, our) == step).all())
+    finally:
+        torch.cuda.synchronize()
+        for p in ptrs:
+            C.exchange_free(p)
+
+
+def test_fused_split_peer_timeout_is_reported():
+    caches, _, g = _split_caches(1000, 4, 128, 2, seed=3)
+    n = C.paged_decode_split_bytes(1, 4, 128)
+    ptrs = [C.exchange_alloc(torch.cuda.current_device(), n) for _ in range(2)]
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    try:
+        me = caches[0]
+        bt, sl = me.block_table([0])
+        q = torch.randn((1, 4, 128), generator=g, device="cuda")
+        out = C.paged_decode_split(q, me.k_pool, me.v_pool, me.sz_pool, bt, sl, ptrs, 0,
+                                   status=status)  # rank 1 never arrives
+        torch.cuda.synchronize()
+        assert int(status.item()) & PEER_TIMEOUT
+        assert bool(torch.isnan(out).all())
+        assert bool(torch.isfinite(me.decode(q, [0])).all())  # the context is still usable
+    finally:
+        torch.cuda.synchronize()
+        for p in ptrs:
+            C.exchange_free(p)

@@ -141,7 +141,7 @@ def test_batch_head_shards_reassemble():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 or more GPUs")
-@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p", "fused"])
 def test_sequence_split_across_gpus(exchange):
     import os
     import subprocess
@@ -151,6 +151,6 @@ def test_sequence_split_across_gpus(exchange):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300", sys.executable, "-m",
                         "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
-                        "--master-addr", "127.0.0.1", "--master-port", str(29531 + (exchange == "p2p")), script,
+                        "--master-addr", "127.0.0.1", "--master-port", str(29531 + ["nccl", "p2p", "fused"].index(exchange)), script,
                         "32768", "8", exchange], capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
