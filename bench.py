@@ -595,16 +595,22 @@ def run_split(args):
         flush(i)
         dec.replay()
     torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
     dist.barrier()
     torch.cuda.synchronize()
+    t_wall0 = time.perf_counter()
     for i in range(K):
         flush(i)
         ev[i][0].record()
         dec.replay()
         ev[i][1].record()
     torch.cuda.synchronize()
+    t_wall1 = time.perf_counter()
     dist.barrier()
     torch.cuda.synchronize()
+    sampler.mark(t_wall0, t_wall1)
+    sampler.stop()
     mean = sum(a.elapsed_time(b) for a, b in ev) / K
     mean = _all_reduce_max(mean, world)
     if dec.peer_status():
@@ -637,6 +643,7 @@ def run_split(args):
             "gpu_launches": K * (1 if args.exchange == "fused" else 2),
             "step": "CUDA graph: " + step_desc,
             "parity": {"max_abs_vs_whole_sequence_decode": gate_err},
+            "clocks": sampler.summary(),
         }), flush=True)
     dec.close()  # graph (may hold an NCCL call) and peer mappings go before the process group
     torch.cuda.synchronize()
