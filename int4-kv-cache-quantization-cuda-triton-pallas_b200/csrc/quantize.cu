@@ -219,36 +219,48 @@ grouped_quant_kernel(const float* __restrict__ kv, int N, int C, int R, OutConti
 }
 
 // Persistent, TMA-pipelined form of grouped_quant_kernel for the contiguous
-// output (groups of R <= 128 rows, C % 32 == 0). Two CTAs per SM walk tiles
-// (group g, 64-channel slab) t = blockIdx.x, + gridDim.x, ...; the TMA engine
-// moves each tile (R rows x 256 B, one 2-D tensor copy) into a ring of
+// output (groups of R <= 128 rows, C % SLAB == 0). CTAs walk tiles (group g,
+// SLAB-channel slab) t = blockIdx.x, + gridDim.x, ...; the TMA engine moves
+// each tile (R rows x 4 SLAB bytes, one 2-D tensor copy) into a ring of
 // kTmaStages shared-memory stages, so later tiles stream in while the current
-// one is reduced and quantized, and the other CTA's serial phases overlap
-// this one's. Thread (row group q = tid / 16, channel quad c = tid % 16) owns
-// channels [4c, 4c+4) of rows q, q+32, q+64, q+96, held in registers between
-// the min/max pass and the quantize pass; the 16 threads of a row store its
-// 32 code bytes together (one full sector). Thread 0 alone waits on a stage's barrier
-// (bounded) and the CTA learns the outcome through shared memory, so every
-// thread takes the same path; after a timeout the CTA drains its copies
-// (bounded), writes NaN into the scale/zp of every tile it did not finish,
-// and exits.
+// one is reduced and quantized. Thread (row group q = tid / (SLAB/4), channel
+// quad c = tid % (SLAB/4)) owns channels [4c, 4c+4) of rows q, q + 512/(SLAB/4),
+// ..., held in registers between the min/max pass and the quantize pass; the
+// threads of a row store its SLAB/2 code bytes together (whole sectors).
+// Thread 0 alone waits on a stage's barrier (bounded) and the CTA learns the
+// outcome through shared memory, so every thread takes the same path; after a
+// timeout the CTA drains its copies (bounded), writes NaN into the scale/zp
+// of every tile it did not finish, and exits.
+//
+// Two widths. SLAB = 128 (one CTA per SM, 64 KB stages) reads each token row
+// in 512-byte pieces and is used whenever C % 128 == 0; SLAB = 64 (two CTAs
+// per SM, 32 KB stages, 256-byte pieces) serves the other widths. Measured on
+// B200 at 32 heads x d128 (C = 4096, rows 16 KB apart): 459 us (128) vs 508
+// us (64) at 131072 tokens, 123 vs 135 at 32768, 38.6 vs 41.0 at 8192, the
+// same ~20 us at 2048 -- the wider pieces stream better from HBM, though the
+// 64-wide form overlaps one CTA's barriers with the other CTA's streaming.
 constexpr int kTmaStages = 3;
 constexpr int kTmaThreads = 512;
-constexpr int kTmaSlab = 64;                                // channels per tile
-constexpr int kTmaQuads = kTmaSlab / 4;                     // 16 threads per row
-constexpr int kTmaRowGroups = kTmaThreads / kTmaQuads;      // 32
-constexpr int kTmaRowsPerThread = kRegGroupMax / kTmaRowGroups;  // 4
-constexpr int kTileRows = kRegGroupMax;                     // 128 rows x 64 channels = 32 KB
+constexpr int kTileRows = kRegGroupMax;                     // 128
 constexpr int kTmaWarps = kTmaThreads / 32;
 constexpr uint64_t kQuantWaitNs = 2000000000ull;            // 2 s
 
+template <int SLAB>
+struct TmaShape {
+  static constexpr int kQuads = SLAB / 4;                          // threads per row
+  static constexpr int kRowGroups = kTmaThreads / kQuads;
+  static constexpr int kRowsPerThread = kTileRows / kRowGroups;    // 4 (64) or 8 (128)
+  static constexpr int kCtasPerSm = SLAB == 64 ? 2 : 1;
+};
+
+template <int SLAB>
 struct TmaSmem {
-  float stage[kTmaStages][kTileRows * kTmaSlab];
-  float4 s_min[kTmaWarps * kTmaQuads];   // [warp][channel] partials (2 row groups folded)
-  float4 s_max[kTmaWarps * kTmaQuads];
-  float s_lo[kTmaSlab];
-  float s_sc[kTmaSlab];
-  float s_rc[kTmaSlab];
+  float stage[kTmaStages][kTileRows * SLAB];
+  float4 s_min[kTmaWarps * (SLAB / 4)];   // [warp][channel quad] partials (SLAB 64: 2 row groups folded)
+  float4 s_max[kTmaWarps * (SLAB / 4)];
+  float s_lo[SLAB];
+  float s_sc[SLAB];
+  float s_rc[SLAB];
   uint64_t bar[kTmaStages];
   int ok;
 };
@@ -256,29 +268,34 @@ struct TmaSmem {
 // Load tile `tile` into `dst`: one 2-D tensor copy for a full group; the
 // short last group (rows < R) instead takes one 1-D bulk copy per row, so no
 // box ever reaches past the tensor and the byte count is exact.
+template <int SLAB>
 __device__ __forceinline__ void tma_issue_tile(const CUtensorMap* tmap, const float* kv, int N,
                                                int C, int R, int S, long long tile, float* dst,
                                                uint64_t* bar) {
   const int g = (int)(tile / S), slab = (int)(tile - (long long)g * S);
   const int r0 = g * R, rows = min(R, N - r0);
   fence_proxy_async_smem();
-  mbar_arrive_expect_tx(bar, (uint32_t)(rows * kTmaSlab * 4));
+  mbar_arrive_expect_tx(bar, (uint32_t)(rows * SLAB * 4));
   if (rows == R) {
-    tma_load_2d(dst, tmap, slab * kTmaSlab, r0, bar);
+    tma_load_2d(dst, tmap, slab * SLAB, r0, bar);
   } else {
     for (int r = 0; r < rows; ++r)
-      bulk_g2s(dst + r * kTmaSlab, kv + (size_t)(r0 + r) * C + slab * kTmaSlab, kTmaSlab * 4, bar);
+      bulk_g2s(dst + r * SLAB, kv + (size_t)(r0 + r) * C + slab * SLAB, SLAB * 4, bar);
   }
 }
 
-__global__ void __launch_bounds__(kTmaThreads, 2)
+template <int SLAB>
+__global__ void __launch_bounds__(kTmaThreads, TmaShape<SLAB>::kCtasPerSm)
 grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ kv,
                          int N, int C, int R, OutContig oc) {
   extern __shared__ __align__(128) char smem_raw[];
-  TmaSmem& sm = *reinterpret_cast<TmaSmem*>(smem_raw);
+  using Sh = TmaShape<SLAB>;
+  constexpr int kTmaSlab = SLAB, kTmaQuads = Sh::kQuads, kTmaRowGroups = Sh::kRowGroups,
+                kTmaRowsPerThread = Sh::kRowsPerThread;
+  TmaSmem<SLAB>& sm = *reinterpret_cast<TmaSmem<SLAB>*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int cq = tid % kTmaQuads, rg = tid / kTmaQuads;
-  const int S = C / kTmaSlab;  // C % 64 == 0 (launcher)
+  const int S = C / kTmaSlab;  // C % kTmaSlab == 0 (launcher)
   const long long total = (long long)((N + R - 1) / R) * S;
   const long long first = blockIdx.x, step = gridDim.x;
   if (first >= total) return;
@@ -287,7 +304,7 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     fence_barrier_init();
     for (int i = 0; i < kTmaStages; ++i) {
       const long long t = first + i * step;
-      if (t < total) tma_issue_tile(&tmap, kv, N, C, R, S, t, sm.stage[i], &sm.bar[i]);
+      if (t < total) tma_issue_tile<SLAB>(&tmap, kv, N, C, R, S, t, sm.stage[i], &sm.bar[i]);
     }
   }
   __syncthreads();
@@ -323,19 +340,29 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
 
     float4 vals[kTmaRowsPerThread];
     float4 mn, mx;
-    if (rows == kTileRows) {  // full tile: three-input min / max over the 4 rows
-      static_assert(kTmaRowsPerThread == 4, "min3/max3 pairing");
+    if (rows == kTileRows) {  // full tile: three-input min / max over the thread's rows
 #pragma unroll
       for (int k = 0; k < kTmaRowsPerThread; ++k)
         vals[k] = reinterpret_cast<const float4*>(tile + (rg + k * kTmaRowGroups) * kTmaSlab)[cq];
-      mn.x = fmin3f(fmin3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, INFINITY);
-      mn.y = fmin3f(fmin3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, INFINITY);
-      mn.z = fmin3f(fmin3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, INFINITY);
-      mn.w = fmin3f(fmin3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, INFINITY);
-      mx.x = fmax3f(fmax3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, -INFINITY);
-      mx.y = fmax3f(fmax3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, -INFINITY);
-      mx.z = fmax3f(fmax3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, -INFINITY);
-      mx.w = fmax3f(fmax3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, -INFINITY);
+      if constexpr (kTmaRowsPerThread == 4) {
+        mn.x = fmin3f(fmin3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, INFINITY);
+        mn.y = fmin3f(fmin3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, INFINITY);
+        mn.z = fmin3f(fmin3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, INFINITY);
+        mn.w = fmin3f(fmin3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, INFINITY);
+        mx.x = fmax3f(fmax3f(vals[0].x, vals[1].x, vals[2].x), vals[3].x, -INFINITY);
+        mx.y = fmax3f(fmax3f(vals[0].y, vals[1].y, vals[2].y), vals[3].y, -INFINITY);
+        mx.z = fmax3f(fmax3f(vals[0].z, vals[1].z, vals[2].z), vals[3].z, -INFINITY);
+        mx.w = fmax3f(fmax3f(vals[0].w, vals[1].w, vals[2].w), vals[3].w, -INFINITY);
+      } else {
+        static_assert(kTmaRowsPerThread == 8, "min3/max3 chains for 4 or 8 rows");
+#define I4KV_CHAIN3(f3, f2, c) \
+  f2(f3(f3(f3(vals[0].c, vals[1].c, vals[2].c), vals[3].c, vals[4].c), vals[5].c, vals[6].c), vals[7].c)
+        mn.x = I4KV_CHAIN3(fmin3f, fminf, x); mn.y = I4KV_CHAIN3(fmin3f, fminf, y);
+        mn.z = I4KV_CHAIN3(fmin3f, fminf, z); mn.w = I4KV_CHAIN3(fmin3f, fminf, w);
+        mx.x = I4KV_CHAIN3(fmax3f, fmaxf, x); mx.y = I4KV_CHAIN3(fmax3f, fmaxf, y);
+        mx.z = I4KV_CHAIN3(fmax3f, fmaxf, z); mx.w = I4KV_CHAIN3(fmax3f, fmaxf, w);
+#undef I4KV_CHAIN3
+      }
     } else {
       mn = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
       mx = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
@@ -349,7 +376,7 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
       }
     }
     // fold the warp's two row groups (lanes l and l ^ 16 hold the same quad)
-    {
+    if constexpr (kTmaQuads == 16) {
       float4 o;
       o.x = __shfl_xor_sync(0xffffffffu, mn.x, 16); o.y = __shfl_xor_sync(0xffffffffu, mn.y, 16);
       o.z = __shfl_xor_sync(0xffffffffu, mn.z, 16); o.w = __shfl_xor_sync(0xffffffffu, mn.w, 16);
@@ -365,7 +392,7 @@ grouped_quant_tma_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     }
     __syncthreads();  // stage st fully read: refill it; partial min/max visible
     if (tid == 0 && t + kTmaStages * step < total)
-      tma_issue_tile(&tmap, kv, N, C, R, S, t + kTmaStages * step, sm.stage[st], &sm.bar[st]);
+      tma_issue_tile<SLAB>(&tmap, kv, N, C, R, S, t + kTmaStages * step, sm.stage[st], &sm.bar[st]);
     if (tid < kTmaSlab) {
       // consecutive threads read consecutive channels of each warp's partials
       const float* pmin = reinterpret_cast<const float*>(sm.s_min);
@@ -734,8 +761,11 @@ cudaError_t tma_quant_setup(int* sms_out) {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lk(mu);
   if (!sms[dev]) {
-    e = cudaFuncSetAttribute(grouped_quant_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(TmaSmem));
+    e = cudaFuncSetAttribute(grouped_quant_tma_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TmaSmem<64>));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(grouped_quant_tma_kernel<128>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TmaSmem<128>));
     if (e != cudaSuccess) return e;
     int n = 0;
     e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -818,14 +848,21 @@ cudaError_t int4kv_quantize_grouped(const float* kv, int num_tokens, int num_hea
   cudaError_t e = cudaSuccess;
   int sms = 0;
   CUtensorMap tmap;
-  if (group_tokens <= kRegGroupMax && C % kTmaSlab == 0 && aligned16(packed_out) &&
+  // 128-channel slabs (512-byte row pieces) wherever the width allows
+  const int slab = C % 128 == 0 ? 128 : 64;
+  if (group_tokens <= kRegGroupMax && C % slab == 0 && aligned16(packed_out) &&
       (e = tma_quant_setup(&sms)) == cudaSuccess &&
-      (e = encode_rows_map(&tmap, kv, num_tokens, (int)C, kTmaSlab, group_tokens)) == cudaSuccess) {
-    const long long tiles = (long long)groups * (C / kTmaSlab);
-    const long long slots = 2LL * sms;  // two CTAs per SM
+      (e = encode_rows_map(&tmap, kv, num_tokens, (int)C, slab, group_tokens)) == cudaSuccess) {
+    const long long tiles = (long long)groups * (C / slab);
+    const long long slots = (long long)sms * (slab == 64 ? TmaShape<64>::kCtasPerSm
+                                                         : TmaShape<128>::kCtasPerSm);
     const unsigned pgrid = (unsigned)(tiles < slots ? tiles : slots);
-    grouped_quant_tma_kernel<<<pgrid, kTmaThreads, sizeof(TmaSmem), stream>>>(
-        tmap, kv, num_tokens, (int)C, group_tokens, oc);
+    if (slab == 128)
+      grouped_quant_tma_kernel<128><<<pgrid, kTmaThreads, sizeof(TmaSmem<128>), stream>>>(
+          tmap, kv, num_tokens, (int)C, group_tokens, oc);
+    else
+      grouped_quant_tma_kernel<64><<<pgrid, kTmaThreads, sizeof(TmaSmem<64>), stream>>>(
+          tmap, kv, num_tokens, (int)C, group_tokens, oc);
   } else if (e != cudaSuccess) {
     return e;
   } else if (group_tokens <= kRegGroupMax) {

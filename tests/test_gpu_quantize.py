@@ -79,8 +79,12 @@ def test_grouped_golden(name):
 
 @pytest.mark.parametrize("n,h,d,group", [(1, 1, 4, 128), (129, 2, 64, 128), (300, 3, 128, 128),
                                          (4096, 32, 128, 128), (1000, 8, 64, 16),
-                                         (777, 4, 128, 200), (256, 2, 256, 64)])
+                                         (777, 4, 128, 200), (256, 2, 256, 64),
+                                         (500, 3, 64, 128), (4000, 1, 64, 32)])
 def test_grouped_matches_oracle(n, h, d, group):
+    """Every kernel form: 128-channel TMA slabs (C % 128 == 0), 64-channel
+    slabs (C = 192, 64), the register kernel (C = 4) and the two-pass kernel
+    (groups > 128); full and short last groups."""
     kv = W.np_anchor_keys(np.random.default_rng(n + d), n, h, d)
     q, s, z = oracle.quantize_grouped(kv, group)
     assert_same(ops.quantize_int4_grouped(kv, group), (oracle.pack_int4(q), s, z))
