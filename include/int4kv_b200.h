@@ -336,7 +336,13 @@ cudaError_t int4kv_ipc_close(void* dev_ptr);
  * int4kv_paged_decode_split_bytes large, 128-byte aligned, zero-filled once;
  * world <= INT4KV_EXCHANGE_MAX_RANKS. Every rank launches it once per step
  * with the same batch and heads. The workspace is that of
- * int4kv_paged_decode_workspace_size_ex. */
+ * int4kv_paged_decode_workspace_size_ex. The grid is one resident wave, and
+ * a warp only ever waits for other GPUs' pushes, all of which precede any
+ * wait: launch it where no other kernel holds SMs of the GPU (a concurrent
+ * kernel on every rank can keep some CTAs from starting while the resident
+ * ones wait for them across GPUs; the step then ends in the bounded wait with
+ * INT4KV_STATUS_PEER_TIMEOUT instead of hanging). After a timeout the ranks'
+ * step counters differ: free and re-create the buffers before the next step. */
 cudaError_t int4kv_paged_decode_split_bytes(int batch, int num_q_heads, int head_dim,
                                             size_t* bytes);
 cudaError_t int4kv_paged_decode_split(const float* query, const uint8_t* k_pool,
