@@ -371,7 +371,9 @@ class SequenceSplitDecoder:
     graph = None
 
     def capture(self, query: torch.Tensor, seq_id: int = 0, warmup: int = 2) -> torch.Tensor:
-        """Record one step (partial decode -> all-gather -> merge) as a CUDA graph.
+        """Record one step as a CUDA graph (partial decode -> all-gather -> merge
+        with NCCL; partial decode -> exchange kernel with p2p; the one split
+        decode kernel with fused).
 
         ``query`` becomes the graph's input buffer: copy each new query into it
         and call ``replay()``, which returns the (static) output tensor. Every

@@ -121,3 +121,34 @@ def test_rope_entry_points_reject_bad_arguments(lib):
                                         p, n, 8, n, n, 0, n, n) == CUDA_ERROR_INVALID_VALUE
     assert lib.int4kv_cache_append_rope(p, n, p, p, p, 1, 1, 2, 64, 128, 16, p, 4, 4, p, n, 0, p,
                                         p, p, 8, p, n, 2, n, n) == CUDA_ERROR_INVALID_VALUE
+
+
+def test_split_decode_layout_and_argument_checks(lib):
+    """int4kv_paged_decode_split_bytes matches the documented buffer layout
+    (the offsets tests use to stand in for peers), and the split decode
+    rejects a bad world / rank / peer buffer before touching the device."""
+    par = pkg("parallel")
+    for batch, heads, d in [(1, 32, 128), (1, 8, 64), (4, 6, 256), (2, 1, 128)]:
+        size = ctypes.c_size_t(0)
+        assert lib.int4kv_paged_decode_split_bytes(batch, heads, d, ctypes.byref(size)) == 0
+        assert size.value == par.split_layout(batch * heads, d)["bytes"]
+        assert par.split_layout(batch * heads, d)["off_recs"] % 128 == 0
+    size = ctypes.c_size_t(0)
+    assert lib.int4kv_paged_decode_split_bytes(1, 8, 96, ctypes.byref(size)) == CUDA_ERROR_INVALID_VALUE
+    assert lib.int4kv_paged_decode_split_bytes(0, 8, 128, ctypes.byref(size)) == CUDA_ERROR_INVALID_VALUE
+    p, n = ctypes.c_void_p(1 << 20), None
+
+    def call(bufs, world, rank):
+        return lib.int4kv_paged_decode_split(p, p, p, 0, p, p, p, 1, 8, 8, 128, 16, 128, 4, 4,
+                                             bufs, world, rank, p, p, 1 << 20, n, n)
+
+    two = (ctypes.c_void_p * 9)(*([1 << 20] * 9))
+    assert call(two, 9, 0) == CUDA_ERROR_INVALID_VALUE      # more than 8 ranks
+    assert call(two, 2, 2) == CUDA_ERROR_INVALID_VALUE      # rank outside the world
+    assert call(two, 2, -1) == CUDA_ERROR_INVALID_VALUE
+    assert call(two, 0, 0) == CUDA_ERROR_INVALID_VALUE      # no ranks
+    assert call(n, 2, 0) == CUDA_ERROR_INVALID_VALUE        # no buffer list
+    odd = (ctypes.c_void_p * 2)(1 << 20, (1 << 20) + 64)
+    assert call(odd, 2, 0) == CUDA_ERROR_INVALID_VALUE      # a peer buffer not 128-byte aligned
+    empty = (ctypes.c_void_p * 2)(1 << 20, 0)
+    assert call(empty, 2, 1) == CUDA_ERROR_INVALID_VALUE    # a missing peer buffer
