@@ -369,6 +369,9 @@ __device__ __forceinline__ void x_finish(const DecodeArgs& a, long long S, long 
     }
   }
   ok = __all_sync(0xffffffffu, ok);
+  // lane r acquired rank r's flag; the warp barrier orders those acquires
+  // before every lane's reads of every rank's record
+  __syncwarp();
   dead = dead || !ok;
   if (lane == 0) step[qs] = E;
   float o[DPL];
