@@ -303,7 +303,7 @@ __device__ __forceinline__ void pv_row(const char* vs, float pt, int t, int lane
 }
 
 // e^x for x <= 0 given in float64: 2^(x*log2(e)) with the hardware base-2
-// exponential (relative error ~2^-22, far inside the kernel's 1e-6 budget);
+// exponential (relative error ~2^-22, far inside the kernel's 1e-6 tolerance);
 // x = -inf gives exactly 0.
 __device__ __forceinline__ float exp_neg(double x) {
   const float y = (float)(x * 1.4426950408889634);
