@@ -84,6 +84,20 @@ def test_plan_rejects_bad_arguments():
         par.plan_sequence_split(100, 2, group_tokens=20)
 
 
+def test_split_decoder_and_exchange_reject_bad_modes():
+    """Checked on the host before any device work: the exchange mode names
+    and the exchange's rank limit."""
+    class _Cache:  # what the constructor reads before it allocates
+        head_dim, heads, device = 128, 8, "cpu"
+    with pytest.raises(ValueError, match="exchange must be"):
+        par.SequenceSplitDecoder(_Cache(), 0, 2, exchange="allgather")
+    with pytest.raises(ValueError, match="1..8 ranks"):
+        par.PeerExchange(0, 9, 8, 128, "cpu")
+    lay = par.split_layout(8, 128)
+    assert lay["off_flag"] % 128 == 0 and lay["off_recs"] % 128 == 0
+    assert lay["bytes"] == lay["off_recs"] + 2 * par.EXCHANGE_MAX_RANKS * 8 * lay["record"]
+
+
 # ---------------- merge arithmetic (oracle restatement) ----------------
 
 def _split_problem(L, heads=4, d=64, world=3, seed=0):
