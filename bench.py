@@ -64,6 +64,12 @@ def parse():
                          "or NCCL all-gather + merge kernel")
     ap.add_argument("--values", default="f32", choices=["f32", "f16", "bf16"],
                     help="value-pool storage type (keys are INT4 either way)")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="skip the config 2 / config 3 sweep and the reference-API records (N=1)")
+    ap.add_argument("--no-split", action="store_true",
+                    help="skip the sequence-split leg of a multi-GPU run")
+    ap.add_argument("--no-seed-check", action="store_true",
+                    help="skip re-timing rank 0's problem on every rank (N>1)")
     return ap.parse_args()
 
 
@@ -118,7 +124,7 @@ def workload_config(shape, name, world):
 class ClockSampler:
     """NVML sampling of SM clock and throttle reasons in a background thread."""
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.002):
         self.samples = []
         self.ok = False
         self._stop = threading.Event()
@@ -175,8 +181,10 @@ class ClockSampler:
         use = inside if len(inside) >= 3 else self.samples
         reasons = sorted({r for s in use for r in s[2]} - {"gpu_idle"})
         return {"sm_mhz": statistics.median(s[1] for s in use), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(use),
-                "window": "timed region" if use is inside else "warmup + timed region"}
+                "reasons": reasons, "samples": len(use), "period_ms": round(self.period * 1e3, 1),
+                "window": (self.window if use is inside else "warmup + timed loops")}
+
+    window = "timed region"
 
 
 def _all_reduce_max(x, world):
@@ -216,6 +224,204 @@ def cpu_baseline(arrays, streams, bytes_per_stream, seconds_target=2.0):
                       f"oracle online softmax per stream (NumPy, 1 BLAS thread per process, "
                       f"{pool.procs} spawn processes), {wall:.2f} s wall",
             "ms_per_stream": round(1e3 * wall / (reps * len(streams)) * pool.procs, 3)}, outs
+
+
+def stream_gate(torch, out, query, cache, bt, sl, streams, group_q=1):
+    """Max |gpu - float64 arbiter| over (sequence, kv head) streams, each copied
+    off the device on its own (no host copy of a whole pool)."""
+    import oracle
+    o, q = out.cpu().numpy(), query.cpu().numpy()
+    bt_h, sl_h = bt.cpu().numpy(), sl.cpu().numpy()
+    G, err = group_q, 0.0
+    for b, h in streams:
+        n = int(sl_h[b])
+        got = o[b, h * G:(h + 1) * G]
+        if n == 0:
+            err = max(err, float(np.abs(got).max()))
+            continue
+        pages = torch.as_tensor(bt_h[b, :(n + 15) // 16].astype(np.int64), device=out.device)
+        ex = oracle.stream_f64(q[b, h * G:(h + 1) * G], cache.k_pool[pages, h].cpu().numpy(),
+                               cache.v_pool[pages, h].float().cpu().numpy(),
+                               cache.sz_pool[pages, h].cpu().numpy(), n)
+        err = max(err, float(np.abs(got - ex).max()))
+    return err
+
+
+def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, seed=0):
+    """CUDA-event time of the decode kernel alone (events recorded by the C ABI
+    around the launch) on a built problem, L2 flushed before every launch,
+    behind a float64 gate on `gate_streams` seeded streams."""
+    import ctypes
+    cache, query = prob["cache"], prob["query"]
+    ids = list(range(shape.batch))
+    bt, sl = cache.block_table(ids)
+    hq, h, d = shape.query_heads, shape.heads, shape.head_dim
+    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, hq, h, d, value_dtype=vdtype)
+    ws = torch.zeros((ws_bytes,), dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(query)
+    stream = torch.cuda.current_stream()
+    vk = C.VALUE_KINDS[vdtype]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    for a, b in ev:
+        a.record()
+        b.record()
+
+    def launch(e0=None, e1=None):
+        rc = lib.int4kv_paged_decode_ex(
+            query.data_ptr(), cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), vk,
+            cache.sz_pool.data_ptr(), bt.data_ptr(), sl.data_ptr(), shape.batch, hq, h, d, 16,
+            shape.group_tokens, bt.shape[1], cache.num_pages, out.data_ptr(), ws.data_ptr(),
+            ws_bytes, None, stream.cuda_stream, e0, e1)
+        if rc:
+            raise RuntimeError(f"decode launch failed: cudaError {rc}")
+
+    launch()
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(seed)
+    streams = sorted({(int(b), int(x)) for b, x in zip(rng.integers(0, shape.batch, gate_streams),
+                                                       rng.integers(0, h, gate_streams))})
+    gate = stream_gate(torch, out, query, cache, bt, sl, streams, hq // h)
+    if not (torch.isfinite(out).all() and gate <= 1e-6):
+        raise RuntimeError(f"decode failed its correctness gate (max err {gate}); not timing")
+    for i in range(3):
+        flush(i)
+        launch()
+    for i, (a, b) in enumerate(ev):
+        flush(i)
+        launch(ctypes.c_void_p(a.cuda_event), ctypes.c_void_p(b.cuda_event))
+    torch.cuda.synchronize()
+    us = [a.elapsed_time(b) * 1e3 for a, b in ev]
+    return {"kernel_us": round(sum(us) / K, 2), "kernel_us_p50": round(float(np.median(us)), 2),
+            "gate_streams": len(streams), "max_abs_vs_f64_arbiter": gate}
+
+
+def sweep_records(torch, lib, C, W, K, flush, peak):
+    """The other decode configurations of the benchmark definition on this GPU:
+    config 2's context sweep and config 3's ragged batch (d64, d128)."""
+    recs = {}
+    for name in ("cfg2_512", "cfg2_8192", "cfg2_32768", "cfg3_d64", "cfg3_d128"):
+        shape = W.config_shape(name)
+        prob = W.torch_build_cache(shape, seed=7)
+        r = decode_timing(torch, lib, C, shape, prob, torch.float32, K, flush, seed=1)
+        nbytes = shape.algorithmic_bytes()
+        r.update({"algorithmic_bytes": nbytes,
+                  "gbs": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9, 1),
+                  "frac": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9 / peak, 4)})
+        recs[name] = r
+        del prob
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return recs
+
+
+def reference_api_records(torch, lib, flush):
+    """The reference's own two launchers, through their drop-in C signatures, at
+    the shapes its published H100 numbers are quoted on:
+    cu_flash_decode_int4 at b8 x h32 x d128 x s2048 (one shared stream of
+    256-row pages, one code per byte, float32 values;
+    results/three_backend_attention_h100.json:187 of the reference, 0.400 ms)
+    and cu_quantize_int4 at 32768 x 128 (results/three_backend_quantize_h100.json:237,
+    0.150 ms). Inputs as the reference's benchmark builds them
+    (benchmarks/bench_three_backend.py:113-129): randn query, keys and values,
+    keys quantized per block."""
+    import oracle
+    stream = torch.cuda.current_stream().cuda_stream
+    rng = np.random.RandomState(1234)
+    B, H, D, bs, L = 8, 32, 128, 256, 2048
+    nb = L // bs
+    query = rng.randn(B, H, D).astype(np.float32)
+    kq, ks, kz, vv = [], [], [], []
+    for _ in range(nb):
+        k = rng.randn(bs, D).astype(np.float32)
+        vv.append(rng.randn(bs, D).astype(np.float32))
+        q_, s_, z_ = oracle.quantize_int4(k)
+        kq.append(q_), ks.append(s_), kz.append(z_)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    tq, tk, ts, tz, tv = dev(query), dev(np.stack(kq)), dev(np.stack(ks)), dev(np.stack(kz)), dev(np.stack(vv))
+    tl = torch.full((nb,), bs, dtype=torch.int32, device="cuda")
+    out = torch.empty((B, H, D), device="cuda")
+
+    def attn():
+        rc = lib.cu_flash_decode_int4(tq.data_ptr(), tk.data_ptr(), ts.data_ptr(), tz.data_ptr(),
+                                      tv.data_ptr(), tl.data_ptr(), B, H, D, nb, bs,
+                                      out.data_ptr(), stream)
+        if rc:
+            raise RuntimeError(f"cu_flash_decode_int4 failed: cudaError {rc}")
+
+    attn()
+    torch.cuda.synchronize()
+    pages = list(zip(kq, ks, kz))
+    gate = float(np.abs(out.cpu().numpy() - oracle.attention_f64(query, pages, vv)).max())
+    ref32 = float(np.abs(out.cpu().numpy() - oracle.online_softmax(query, pages, vv)[0]).max())
+    if not gate <= 1e-6:
+        raise RuntimeError(f"cu_flash_decode_int4 failed its gate ({gate}); not timing")
+
+    rows, ch = 32768, 128
+    kv = torch.from_numpy(np.random.RandomState(4321).randn(rows, ch).astype(np.float32)).cuda()
+    q_out = torch.empty((rows, ch), dtype=torch.uint8, device="cuda")
+    s_out = torch.empty((ch,), device="cuda")
+    z_out = torch.empty((ch,), device="cuda")
+
+    def quant():
+        rc = lib.cu_quantize_int4(kv.data_ptr(), rows, ch, q_out.data_ptr(), s_out.data_ptr(),
+                                  z_out.data_ptr(), stream)
+        if rc:
+            raise RuntimeError(f"cu_quantize_int4 failed: cudaError {rc}")
+
+    quant()
+    torch.cuda.synchronize()
+    q_r, s_r, z_r = oracle.quantize_int4(kv.cpu().numpy())
+    exact = (np.array_equal(q_out.cpu().numpy(), q_r)
+             and np.array_equal(s_out.cpu().numpy().view(np.uint32), s_r.view(np.uint32))
+             and np.array_equal(z_out.cpu().numpy().view(np.uint32), z_r.view(np.uint32)))
+    if not exact:
+        raise RuntimeError("cu_quantize_int4 is not bit-exact with the oracle; not timing")
+
+    def timed(fn, n, flushed):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        for i in range(3):
+            fn()
+        for i, (a, b) in enumerate(ev):
+            if flushed:
+                flush(i)
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return round(sum(a.elapsed_time(b) for a, b in ev) / n * 1e3, 2)
+
+    a_warm, a_cold = timed(attn, 50, False), timed(attn, 50, True)
+    q_warm, q_cold = timed(quant, 50, False), timed(quant, 50, True)
+    return {
+        "cu_flash_decode_int4": {
+            "shape": "b8 x h32 x d128, one shared stream of 2048 tokens in 8 pages of 256 rows, "
+                     "1-byte codes, float32 values",
+            "us_back_to_back": a_warm, "us_l2_flushed": a_cold,
+            "reference_h100_us": 400.0,
+            "speedup_vs_reference_h100": round(400.0 / a_warm, 2),
+            "max_abs_vs_f64_arbiter": gate, "max_abs_vs_oracle_fp32": ref32},
+        "cu_quantize_int4": {
+            "shape": "32768 rows x 128 channels, group = all rows, 1-byte codes",
+            "us_back_to_back": q_warm, "us_l2_flushed": q_cold,
+            "gbs_l2_flushed": round((rows * ch * 5 + 8 * ch) / (q_cold * 1e-6) / 1e9, 1),
+            "reference_h100_us": 150.0,
+            "speedup_vs_reference_h100": round(150.0 / q_warm, 2), "bit_exact": exact},
+        "timing": "CUDA events around each C-ABI call; the reference's numbers are "
+                  "back-to-back launches on device-resident inputs (src/_prepared.py:1-18)",
+    }
+
+
+def gather_per_rank(torch, vals, world):
+    """[[rank 0 values], [rank 1 values], ...] on every rank (one all-gather)."""
+    if world == 1:
+        return [list(vals)]
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    outs = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(outs, t)
+    return [o.tolist() for o in outs]
 
 
 # --------------------------------------------------------------------------
@@ -328,7 +534,6 @@ def run_ours(args):
     torch.cuda.synchronize()
     _barrier(world)
     torch.cuda.synchronize()
-    sampler.mark(t_wall0, t_wall1)
     kern_ms = [e[1].elapsed_time(e[2]) for e in ev]
     mean_step = _all_reduce_max(sum(step_ms) / K, world)
     mean_kern = _all_reduce_max(sum(kern_ms) / K, world)
@@ -371,6 +576,9 @@ def run_ours(args):
         if rc:
             raise RuntimeError(f"decode launch failed: cudaError {rc}")
     torch.cuda.synchronize()
+    t_wall1 = time.perf_counter()
+    sampler.window = "timed loops (step, kernel-only, end-to-end)"
+    sampler.mark(t_wall0, t_wall1)
     _barrier(world)
     e2e_ms = _all_reduce_max(sum(a.elapsed_time(b) for a, b in ee) / KE, world)
     if not torch.equal(out_host, out.cpu()):
@@ -397,6 +605,48 @@ def run_ours(args):
             del kv
     sampler.stop()
 
+    # ---- per-rank view of the weak-scaling step (N > 1) ----
+    seed = 7 + 1000 * rank
+    per_rank = None
+    if world > 1:
+        stats = gather_per_rank(torch, [sum(step_ms) / K * 1e3, sum(kern_ms) / K * 1e3, seed],
+                                world)
+        per_rank = {"step_us": [round(x[0], 2) for x in stats],
+                    "kernel_us": [round(x[1], 2) for x in stats],
+                    "seed": [int(x[2]) for x in stats]}
+        # every rank decodes rank 0's problem (seed 7) once more: separates the
+        # block table / data of each rank from the GPU it runs on
+        if not args.no_seed_check:
+            prob0 = W.torch_build_cache(shape, seed=7, value_dtype=vdtype)
+            r0 = decode_timing(torch, lib, C, shape, prob0, vdtype, K, flush, seed=rank)
+            del prob0
+            torch.cuda.empty_cache()
+            same = gather_per_rank(torch, [r0["kernel_us"]], world)
+            per_rank["kernel_us_rank0_problem"] = [round(x[0], 2) for x in same]
+
+    # ---- the sequence split of config 4's long sequence over the same ranks ----
+    seq_split = None
+    if world > 1 and args.config == "cfg0" and not args.no_split:
+        import torch.distributed as dist
+        P = importlib.import_module(PKG + ".paged")
+        par = importlib.import_module(PKG + ".parallel")
+        env = split_setup(torch, P, par, W, "cfg4_long", rank, world)
+        seq_split = {"workload": "cfg4_long: one sequence of 131072 tokens x 32 heads x d128 "
+                                 f"split across {world} GPUs by 128-token groups (strong scaling)",
+                     "algorithmic_bytes": env["shape"].algorithmic_bytes(),
+                     "steps": K, "warmup": Wm}
+        for mode in ("nccl", "p2p", "fused"):
+            seq_split[mode] = split_mode(torch, dist, par, env, mode, rank, world, K, Wm, flush)
+        del env
+        torch.cuda.empty_cache()
+
+    # ---- the other decode configs and the reference's own launchers (N == 1) ----
+    peak, peak_kind = measured_peak()
+    sweep = ref_api = None
+    if world == 1 and not args.no_sweep:
+        sweep = sweep_records(torch, lib, C, W, K, flush, peak)
+        ref_api = reference_api_records(torch, lib, flush)
+
     # ---- CPU baseline: the oracle on a bounded sample (rank 0, N == 1) ----
     bytes_step = shape.algorithmic_bytes()
     cpu = None
@@ -407,7 +657,6 @@ def run_ours(args):
         cpu["max_abs_gpu_vs_oracle_fp32"] = float(max(np.abs(o_host[b, hh] - o).max()
                                                       for (b, hh), o in outs.items()))
 
-    peak, peak_kind = measured_peak()
     total_bytes = bytes_step * world
     value = total_bytes / (mean_step * 1e-3) / 1e9
     achieved = bytes_step / (mean_kern * 1e-3) / 1e9
@@ -428,6 +677,9 @@ def run_ours(args):
                      "kernel": f"paged_decode_kernel<{d},4,2> (decode + fused combine)",
                      "kernel_us": round(mean_kern * 1e3, 2),
                      "algorithmic_bytes_per_launch": bytes_step,
+                     "traffic_source": ("profiles/paged_decode_cfg0.md: static, from one ncu "
+                                        "capture of this kernel at this config (not this run)")
+                     if traffic is not None else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
                      "measured" else "fallback 6.65 TB/s"},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -442,6 +694,14 @@ def run_ours(args):
         "parity": {"gate_streams": len(gate_streams), "max_abs_vs_f64_arbiter": gate_err},
         "quantizer": quant,
     }
+    if per_rank is not None:
+        result["per_rank"] = per_rank
+    if seq_split is not None:
+        result["seq_split"] = seq_split
+    if sweep is not None:
+        result["sweep"] = sweep
+    if ref_api is not None:
+        result["reference_api"] = ref_api
     if cpu is not None:
         result["cpu_baseline"] = cpu
     if rank == 0:
@@ -530,14 +790,111 @@ def run_reference(args):
 # our arm, sequence split (cfg4_long under torchrun): strong scaling
 # --------------------------------------------------------------------------
 
+SPLIT_DESC = {
+    "p2p": "partial decode kernel + fused peer-exchange/merge kernel (NVLink stores, "
+           "flags, bounded waits; no NCCL)",
+    "nccl": "partial decode kernel + NCCL all-gather + merge kernel",
+    "fused": "one kernel: decode, push of each stream's record to every rank over "
+             "NVLink as its pages finish, bounded wait for the peers' records and "
+             "their merge (no NCCL)",
+}
+
+
+def split_setup(torch, P, par, W, name, rank, world):
+    """One long sequence (config `name`, e.g. cfg4_long = 1 x 131072 tokens x 32
+    heads) drawn identically on every rank; each rank keeps its 128-token-group
+    aligned token range in its own cache. Rank 0 also decodes the whole
+    sequence on its own GPU: the gate every split mode is checked against."""
+    shape = W.config_shape(name)
+    L, h, d = shape.seq_lens[0], shape.heads, shape.head_dim
+    g = torch.Generator(device="cuda").manual_seed(7)
+    sc = torch.rand((h, d), generator=g, device="cuda") * 2.5 + 0.5
+    off = torch.randn((h, d), generator=g, device="cuda") * 2.0
+    t0, t1 = par.plan_sequence_split(L, world)[rank]
+    keys = torch.randn((L, h, d), generator=g, device="cuda") * sc + off
+    vals = torch.randn((L, h, d), generator=g, device="cuda")
+    query = torch.randn((1, h, d), generator=g, device="cuda")
+    cache = P.PagedKVCache((t1 - t0 + 15) // 16 + 8, h, d, device="cuda", seed=rank)
+    cache.write_sequences([0], [keys[t0:t1]], [vals[t0:t1]])
+    whole_out = None
+    if rank == 0:
+        whole = P.PagedKVCache((L + 15) // 16 + 8, h, d, device="cuda", seed=99)
+        whole.write_sequences([0], [keys], [vals])
+        whole_out = whole.decode(query, [0]).clone()
+        del whole
+    del keys, vals
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"shape": shape, "cache": cache, "query": query, "whole_out": whole_out,
+            "range": (t0, t1)}
+
+
+def split_mode(torch, dist, par, env, exchange, rank, world, K, Wm, flush, sampler=None):
+    """Time one exchange mode of the sequence split: gate against the whole-
+    sequence decode (rank 0), the step captured as one CUDA graph, K replays
+    with L2 flushed before each, max over ranks. Every rank takes the same
+    collective steps whatever the outcome, so a failed gate is reported, not
+    raised half-way."""
+    cache, query = env["cache"], env["query"]
+    store = dist.distributed_c10d._get_default_store()
+    dec = par.SequenceSplitDecoder(
+        cache, rank, world, exchange=exchange,
+        monitor=par.PeerMonitor(store, rank, world, timeout=60.0, prefix=f"i4kv_split_{exchange}"))
+    try:
+        out = dec.decode(query).clone()
+        gate = torch.zeros((1,), device="cuda", dtype=torch.float64)
+        if rank == 0:
+            gate[0] = (out - env["whole_out"]).abs().max().double()
+        dist.all_reduce(gate, op=dist.ReduceOp.MAX)
+        gate_err = float(gate.item())
+        st = torch.tensor([float(dec.peer_status())], device="cuda", dtype=torch.float64)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        dec.monitor = None  # host liveness checks stay out of the timed loop
+        dec.capture(query)
+        graph_out = dec.replay()
+        torch.cuda.synchronize()
+        gerr = float((graph_out - out).abs().max())
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(K)]
+        for i in range(Wm):
+            flush(i)
+            dec.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(K):
+            flush(i)
+            ev[i][0].record()
+            dec.replay()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        dist.barrier()
+        if sampler is not None:
+            sampler.mark(t0, t1)
+        us = [a.elapsed_time(b) * 1e3 for a, b in ev]
+        mean = _all_reduce_max(sum(us) / K, world)
+        st2 = torch.tensor([float(dec.peer_status())], device="cuda", dtype=torch.float64)
+        dist.all_reduce(st2, op=dist.ReduceOp.MAX)
+        per_rank = [r[0] for r in gather_per_rank(torch, [sum(us) / K], world)]
+    finally:
+        dec.close()  # graph (may hold an NCCL call) and peer mappings go before the process group
+        torch.cuda.synchronize()
+    ok = gate_err <= 2e-6 and gerr == 0.0 and int(st.item()) == 0 and int(st2.item()) == 0
+    return {"us_per_step": round(mean, 2), "us_per_step_per_rank": [round(x, 2) for x in per_rank],
+            "max_abs_vs_whole_sequence_decode": gate_err, "graph_replay_vs_eager": gerr,
+            "peer_status": int(max(st.item(), st2.item())), "gate_ok": ok,
+            "launches_per_step": 1 if exchange == "fused" else 2, "step": SPLIT_DESC[exchange]}
+
+
 def run_split(args):
     """One long sequence split across the ranks by 128-token groups; a step is
     each rank's partial decode + the exchange of the partial records and their
     merge: one fused peer-memory kernel (``--exchange p2p``), one NCCL
     all-gather + the merge kernel (``--exchange nccl``), or no separate step at
     all (``--exchange fused``: the decode kernel pushes, waits and merges
-    itself). Total work is fixed as
-    N grows (strong scaling)."""
+    itself). Total work is fixed as N grows (strong scaling)."""
     import datetime
     import importlib
     import torch
@@ -550,102 +907,42 @@ def run_split(args):
     W = importlib.import_module(PKG + ".workloads")
     P = importlib.import_module(PKG + ".paged")
     par = importlib.import_module(PKG + ".parallel")
-    shape = W.config_shape(args.config)
-    L, h, d = shape.seq_lens[0], shape.heads, shape.head_dim
-    g = torch.Generator(device="cuda").manual_seed(7)
-    sc = torch.rand((h, d), generator=g, device="cuda") * 2.5 + 0.5
-    off = torch.randn((h, d), generator=g, device="cuda") * 2.0
-    t0, t1 = par.plan_sequence_split(L, world)[rank]
-    # every rank draws the same sequence; it keeps only its own token range
-    keys = torch.randn((L, h, d), generator=g, device="cuda") * sc + off
-    vals = torch.randn((L, h, d), generator=g, device="cuda")
-    query = torch.randn((1, h, d), generator=g, device="cuda")
-    cache = P.PagedKVCache((t1 - t0 + 15) // 16 + 8, h, d, device="cuda", seed=rank)
-    cache.write_sequences([0], [keys[t0:t1]], [vals[t0:t1]])
-    store = dist.distributed_c10d._get_default_store()
-    dec = par.SequenceSplitDecoder(cache, rank, world,
-                                   monitor=par.PeerMonitor(store, rank, world, timeout=60.0),
-                                   exchange=args.exchange)
-    out = dec.decode(query).clone()  # correctness gate: against a whole-sequence decode on rank 0
-    gate = torch.zeros((1,), device="cuda")
-    if rank == 0:
-        whole = P.PagedKVCache((L + 15) // 16 + 8, h, d, device="cuda", seed=99)
-        whole.write_sequences([0], [keys], [vals])
-        gate[0] = (out - whole.decode(query, [0])).abs().max()
-        del whole
-    del keys, vals
-    dist.all_reduce(gate, op=dist.ReduceOp.MAX)
-    gate_err = float(gate.item())
-    if dec.peer_status():
-        raise RuntimeError(f"peer exchange reported status {dec.peer_status()}")
-    if not gate_err <= 2e-6:
-        raise RuntimeError(f"sequence-split decode failed its gate (max err {gate_err})")
-    dec.monitor = None  # host liveness checks stay out of the timed loop
-    dec.capture(query)  # the step as one CUDA graph: no host gaps between its parts
-    graph_out = dec.replay()
-    torch.cuda.synchronize()
-    gerr = float((graph_out - out).abs().max())
-    if gerr != 0.0:
-        raise RuntimeError(f"graph replay differs from the eager step by {gerr}")
+    env = split_setup(torch, P, par, W, args.config, rank, world)
     flush = L2Flush(torch)
-    K, Wm = args.steps, args.warmup
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(K)]
-    for i in range(Wm):
-        flush(i)
-        dec.replay()
-    torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
-    dist.barrier()
-    torch.cuda.synchronize()
-    t_wall0 = time.perf_counter()
-    for i in range(K):
-        flush(i)
-        ev[i][0].record()
-        dec.replay()
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    t_wall1 = time.perf_counter()
-    dist.barrier()
-    torch.cuda.synchronize()
-    sampler.mark(t_wall0, t_wall1)
+    rec = split_mode(torch, dist, par, env, args.exchange, rank, world, args.steps, args.warmup,
+                     flush, sampler)
     sampler.stop()
-    mean = sum(a.elapsed_time(b) for a, b in ev) / K
-    mean = _all_reduce_max(mean, world)
-    if dec.peer_status():
-        raise RuntimeError(f"peer exchange reported status {dec.peer_status()} in the timed loop")
-    total = shape.algorithmic_bytes()
-    step_desc = {
-        "p2p": "partial decode kernel + fused peer-exchange/merge kernel (NVLink stores, "
-               "flags, bounded waits; no NCCL)",
-        "nccl": "partial decode kernel + NCCL all-gather + merge kernel",
-        "fused": "one kernel: decode, push of each stream's record to every rank over "
-                 "NVLink as its pages finish, bounded wait for the peers' records and "
-                 "their merge (no NCCL)",
-    }[args.exchange]
+    if not rec["gate_ok"]:
+        raise RuntimeError(f"sequence split failed its gate: {rec}")
+    shape = env["shape"]
+    L, h, d = shape.seq_lens[0], shape.heads, shape.head_dim
+    mean = rec["us_per_step"] * 1e-3
     peak, peak_kind = measured_peak()
+    total = shape.algorithmic_bytes()
     value = total / (mean * 1e-3) / 1e9
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
-            "steps": K, "warmup": Wm, "ms_per_step": round(mean, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (exact integer logits, fp64 recombination), int4 keys",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32 (exact integer logits, fp64 recombination), int4 keys",
             "data": "synthetic (seeded, config-0 distributions)",
             "config": {"workload": f"{args.config}: one sequence of {L} tokens x {h} heads x d{d}, "
                                    f"split across {world} GPUs by 128-token groups; step = "
-                                   + step_desc,
+                                   + SPLIT_DESC[args.exchange],
                        "exchange": args.exchange,
                        "global_batch": 1, "seq_len": L, "heads": h, "head_dim": d,
                        "l2": "flushed before every timed step",
                        "parallelism": f"sequence split x{world}"},
             "hbm_frac_of_peak": round(value / world / peak, 4), "peak_source": peak_kind,
-            "gpu_launches": K * (1 if args.exchange == "fused" else 2),
-            "step": "CUDA graph: " + step_desc,
-            "parity": {"max_abs_vs_whole_sequence_decode": gate_err},
+            "gpu_launches": args.steps * rec["launches_per_step"],
+            "step": "CUDA graph: " + SPLIT_DESC[args.exchange],
+            "parity": {"max_abs_vs_whole_sequence_decode": rec["max_abs_vs_whole_sequence_decode"]},
+            "split": rec,
             "clocks": sampler.summary(),
         }), flush=True)
-    dec.close()  # graph (may hold an NCCL call) and peer mappings go before the process group
     torch.cuda.synchronize()
     dist.destroy_process_group()
 

@@ -5,8 +5,11 @@
  *   - plain device pointers, int sizes and a cudaStream_t; no torch types;
  *   - every launcher returns cudaErrorInvalidValue for bad sizes / null or
  *     misaligned pointers, otherwise the launch's cudaGetLastError();
- *   - launchers are stateless and re-entrant (safe on concurrent streams) and
- *     never allocate: scratch space is passed in by the caller.
+ *   - launchers never allocate and keep no state between calls (safe on
+ *     concurrent streams): scratch space is passed in by the caller. Two
+ *     documented exceptions: int4kv_exchange_alloc allocates the peer-exchange
+ *     buffer (its whole purpose), and int4kv_paged_decode_static_scratch uses a
+ *     library-owned device array shared by every call on a device.
  *
  * Numerical contract: quantizer bins, scales and zero-points are bit-identical
  * to the reference's NumPy oracle (src/quantize_int4_ref.py:51-75: IEEE float32,
@@ -355,8 +358,11 @@ cudaError_t int4kv_paged_decode_split(const float* query, const uint8_t* k_pool,
                                       uint32_t* status, cudaStream_t stream);
 
 /* Scratch capacity of int4kv_paged_decode_static_scratch, per device: a
- * file-scope device array in the library (8 MiB; enough for 8192 streams at
- * head_dim 128). */
+ * file-scope device array in the library, 8 MiB. That holds about 14,000
+ * (sequence, query head) streams at head_dim 128; the exact limit depends on
+ * the launch grid, because the scratch holds one record per resident warp as
+ * well as one per stream -- *scratch_needed, or
+ * int4kv_paged_decode_workspace_size, gives the exact bytes for a shape. */
 #define INT4KV_STATIC_SCRATCH_BYTES (8u << 20)
 
 /* int4kv_paged_decode without a workspace argument, for callers that cannot
@@ -373,7 +379,11 @@ cudaError_t int4kv_paged_decode_split(const float* query, const uint8_t* k_pool,
  * them. The first call on a device (and the first per head_dim and batch
  * size class) performs set-up -- it resolves the array's device address and
  * sets the kernel's shared-memory attribute -- and should precede any stream
- * capture. Other arguments, checks and results as int4kv_paged_decode. */
+ * capture. The array's device address is resolved once per device and kept
+ * for the life of the process: cudaDeviceReset (or destroying the device's
+ * primary context) after the first call is not supported. Value pools are
+ * float32 only (the 16-bit pools of int4kv_paged_decode_ex are not accepted
+ * here). Other arguments, checks and results as int4kv_paged_decode. */
 cudaError_t int4kv_paged_decode_static_scratch(const float* query, const uint8_t* k_pool,
                                                const float* v_pool, const float* sz_pool,
                                                const int32_t* block_table,

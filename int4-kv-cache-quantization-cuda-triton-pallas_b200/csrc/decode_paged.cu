@@ -429,9 +429,10 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
   }
 }
 
-// 16-bit value pools halve the stage size, so four CTAs fit an SM's shared
-// memory; registers are capped to let them all be resident (measured: 6 %
-// faster at 32K context than three CTAs with uncapped registers).
+// 16-bit value pools halve the stage size, so up to four CTAs fit an SM's
+// shared memory; registers are capped at 128 so that four could be resident,
+// but the grid launches three per SM (I4KV_DECODE_MAX_CTAS_16: measured 45.5
+// us at config 0 against 46.5 with four and 53.5 with two).
 template <int D, int WARPS, int STAGES, int VK>
 __global__ void __launch_bounds__(WARPS * 32, VK == 0 ? 1 : 4)
 paged_decode_kernel(DecodeArgs a) {
@@ -1398,7 +1399,10 @@ cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const
 //   * set-up: the first call on a device resolves the array's device address
 //     (cudaGetSymbolAddress, with that device current) and the first call per
 //     (head_dim, batch size class) sets the kernel's shared-memory attribute;
-//     make those first calls before any stream capture begins.
+//     make those first calls before any stream capture begins. The address is
+//     kept for the life of the process, so cudaDeviceReset (or destroying the
+//     device's primary context) after the first call is not supported;
+//   * float32 value pools only.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_static_scratch[INT4KV_STATIC_SCRATCH_BYTES];
 

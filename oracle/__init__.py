@@ -33,5 +33,6 @@ from .attention import (  # noqa: F401
     attention_exact_f32_keys,
     paged_stream_pages,
     decode_paged,
+    stream_f64,
 )
 from .rope import apply_rope, rope_table_f32  # noqa: F401

@@ -167,6 +167,33 @@ def decode_paged_state(query, k_pool, v_pool, sz_pool, block_table, seq_lens,
     return m, l, acc
 
 
+def stream_f64(query, k_pages, v_pages, sz_pages, n_tok, page=16, group_pages=8):
+    """Float64 arbiter for ONE stream whose pages are stored in order, vectorised.
+
+    The same evaluation as ``attention_f64`` (tests/test_pallas_flash_decode.py:53-78
+    of the reference): every valid row concatenated, keys dequantized in
+    float64 as ``kq*s - zp*s``, one softmax. Pages: k_pages [P, page, D/2]
+    packed codes, v_pages [P, page, D], sz_pages [P, 2, D] with the group's
+    scale/zp stored at its first page (page index multiple of ``group_pages``).
+    query [G, D] -> out [G, D] float64. Used where the per-page form is too
+    slow (streams of 10^5 tokens); tests pin the two against each other.
+    """
+    q64 = np.asarray(query, np.float64)
+    if n_tok == 0:
+        return np.zeros(q64.shape, np.float64)
+    d = q64.shape[-1]
+    npg = (n_tok + page - 1) // page
+    codes = unpack_int4(np.asarray(k_pages[:npg]), d).astype(np.float64)  # [P, page, D]
+    grp = (np.arange(npg) // group_pages) * group_pages
+    s64 = np.asarray(sz_pages, np.float64)[grp, 0][:, None, :]
+    z64 = np.asarray(sz_pages, np.float64)[grp, 1][:, None, :]
+    k = (codes * s64 - z64 * s64).reshape(npg * page, d)[:n_tok]
+    v = np.asarray(v_pages[:npg], np.float64).reshape(npg * page, d)[:n_tok]
+    logits = q64 @ k.T
+    p = np.exp(logits - logits.max(axis=-1, keepdims=True))
+    return (p @ v) / p.sum(axis=-1, keepdims=True)
+
+
 _METHODS = {
     "oracle": lambda q, pg, v: online_softmax(q, pg, v)[0],
     "f64": attention_f64,

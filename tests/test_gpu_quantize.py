@@ -99,9 +99,29 @@ def test_grouped_half_even_ties():
     assert codes[:9].tolist() == [0, 15, 0, 2, 2, 4, 4, 14, 14]
 
 
+def torch_quantize_grouped(kv, group):
+    """The oracle's grouped quantizer (oracle.quantize_grouped, restating
+    src/quantize_int4_ref.py:51-75 per 128-token group and head) written with
+    torch operations on the device, for full groups: exact min/max, IEEE
+    float32 subtraction and tensor / tensor division (no reciprocal), round half
+    to even (torch.round), clamp, then the nibble packing of src/int4_pack.py
+    (even channel -> low nibble). Returns (packed, scale, zp)."""
+    n, h, d = kv.shape
+    blk = kv.view(n // group, group, h, d)
+    lo, hi = blk.amin(dim=1, keepdim=True), blk.amax(dim=1, keepdim=True)
+    scale = torch.clamp(hi - lo, min=1e-8) / torch.full_like(lo, 15.0)
+    zp = -lo / scale
+    codes = torch.clamp(torch.round((blk - lo) / scale), 0, 15).to(torch.uint8).view(n, h, d)
+    packed = codes[..., 0::2] | (codes[..., 1::2] << 4)
+    return packed, scale.view(n // group, h, d), zp.view(n // group, h, d)
+
+
 @pytest.mark.parametrize("n_tokens", [2048, 8192, 32768, 131072])
 def test_grouped_baseline_sizes(n_tokens):
-    """benchmark config 1: [N, 32, 128], 128-token groups."""
+    """benchmark config 1: [N, 32, 128], 128-token groups. Every code, scale and
+    zero-point of the whole output is compared bit for bit with the torch
+    restatement of the oracle, which is itself checked bit for bit against the
+    oracle on a seeded sample of (group, head) slices."""
     h, d, group = 32, 128, 128
     g = torch.Generator(device="cuda").manual_seed(n_tokens)
     sc = torch.rand((h, d), generator=g, device="cuda") * 2.5 + 0.5
@@ -121,10 +141,16 @@ def test_grouped_baseline_sizes(n_tokens):
     deq = (codes.view(G, group, h, d) * scale[:, None] - zp[:, None] * scale[:, None])
     err = (deq - blk).abs()
     assert bool((err <= scale[:, None] * 0.5001 + 1e-6).all())
-    # exact comparison of a seeded sample of (group, head) slices against the oracle
+    # every byte of the output against the torch restatement of the oracle
+    t_packed, t_scale, t_zp = torch_quantize_grouped(kv, group)
+    assert torch.equal(packed, t_packed), int((packed != t_packed).sum())
+    assert torch.equal(scale.view(torch.int32), t_scale.view(torch.int32))
+    assert torch.equal(zp.view(torch.int32), t_zp.view(torch.int32))
+    # the restatement (and so the GPU output) against the oracle itself on a
+    # seeded sample of (group, head) slices
     rng = np.random.default_rng(n_tokens)
     kv_h = kv.cpu().numpy()
-    pk_h, sc_h, zp_h = packed.cpu().numpy(), scale.cpu().numpy(), zp.cpu().numpy()
+    pk_h, sc_h, zp_h = t_packed.cpu().numpy(), t_scale.cpu().numpy(), t_zp.cpu().numpy()
     for gi, hi_ in zip(rng.integers(0, G, 16), rng.integers(0, h, 16)):
         q_r, s_r, z_r = oracle.quantize_int4(kv_h[gi * group:(gi + 1) * group, hi_, :])
         np.testing.assert_array_equal(pk_h[gi * group:(gi + 1) * group, hi_], oracle.pack_int4(q_r))

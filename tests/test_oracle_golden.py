@@ -95,3 +95,21 @@ def test_arbiters_agree_with_oracle_on_small_cases():
     ex = oracle.attention_exact_f32_keys(query, pages, v, lens)
     assert np.abs(ref - f64).max() < 1e-5
     assert np.abs(ref - ex).max() < 1e-5
+
+
+@pytest.mark.parametrize("n_tok,gq", [(1, 1), (16, 2), (130, 1), (2048, 4), (3001, 1)])
+def test_stream_f64_equals_per_page_arbiter(n_tok, gq):
+    """The vectorised one-stream float64 arbiter evaluates the same mathematics
+    as the per-page ``attention_f64`` (partial pages and groups included)."""
+    from helpers import oracle_build_pools, pkg
+    W = pkg("workloads")
+    prob = W.np_paged_problem(1, 1, 128, [n_tok], pool_pages=(n_tok + 15) // 16 + 3, seed=n_tok)
+    prob["query"] = np.repeat(prob["query"], gq, axis=1) * np.linspace(0.5, 1.5, gq)[None, :, None]
+    prob["query"] = prob["query"].astype(np.float32)
+    k_pool, v_pool, sz_pool = oracle_build_pools(prob)
+    bt, sl = prob["block_table"], prob["seq_lens"]
+    per_page = oracle.decode_paged(prob["query"], k_pool, v_pool, sz_pool, bt, sl, method="f64")
+    pages = bt[0, :(n_tok + 15) // 16]
+    vec = oracle.stream_f64(prob["query"][0], k_pool[pages, 0], v_pool[pages, 0],
+                            sz_pool[pages, 0], n_tok)
+    np.testing.assert_allclose(vec, per_page[0], rtol=0, atol=1e-12)

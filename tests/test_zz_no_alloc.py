@@ -34,8 +34,9 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def _problem(batch, heads, d, lens, seed):
-    shape = W.DecodeShape(batch, heads, d, lens, pool_pages=sum((n + 15) // 16 for n in lens) + 16)
+def _problem(batch, heads, d, lens, seed, q_heads=None):
+    shape = W.DecodeShape(batch, heads, d, lens, pool_pages=sum((n + 15) // 16 for n in lens) + 16,
+                          q_heads=q_heads)
     prob = W.torch_build_cache(shape, seed=seed)
     cache = prob["cache"]
     bt, sl = cache.block_table(list(range(batch)))
@@ -44,14 +45,18 @@ def _problem(batch, heads, d, lens, seed):
 
 def _args(shape, query, cache, bt, sl):
     return (_p(query), _p(cache.k_pool), _p(cache.v_pool), _p(cache.sz_pool), _p(bt), _p(sl),
-            shape.batch, shape.heads, shape.heads, shape.head_dim, 16, shape.group_tokens,
+            shape.batch, shape.query_heads, shape.heads, shape.head_dim, 16, shape.group_tokens,
             bt.shape[1], cache.num_pages)
+
+
+def _workspace_bytes(shape):
+    return C.paged_decode_workspace_bytes(shape.batch, shape.query_heads, shape.heads,
+                                          shape.head_dim)
 
 
 def _existing(lib, shape, query, cache, bt, sl):
     out = torch.full_like(query, float("nan"))
-    ws_bytes = C.paged_decode_workspace_bytes(shape.batch, shape.heads, shape.heads,
-                                              shape.head_dim)
+    ws_bytes = _workspace_bytes(shape)
     ws = torch.zeros((ws_bytes,), dtype=torch.uint8, device=query.device)
     stream = torch.cuda.current_stream().cuda_stream
     rc = lib.int4kv_paged_decode(*_args(shape, query, cache, bt, sl), _p(out), _p(ws), ws_bytes,
@@ -72,18 +77,22 @@ def _static(lib, shape, query, cache, bt, sl):
     assert rc == 0, f"int4kv_paged_decode_static_scratch: cudaError {rc}"
     torch.cuda.synchronize()
     assert int(status.item()) == 0
+    # a call that fits reports exactly the workspace the existing entry point asks for
+    assert need.value == _workspace_bytes(shape)
     assert 0 < need.value <= STATIC_SCRATCH_BYTES
     return out
 
 
-@pytest.mark.parametrize("batch,heads,d,lens", [
-    (8, 32, 128, [2048] * 8),                     # config-0 shape
-    (5, 4, 128, [300, 0, 4096, 17, 1]),           # ragged, with an empty sequence
-    (3, 8, 64, [129, 2000, 16]),
+@pytest.mark.parametrize("batch,heads,d,lens,q_heads", [
+    (8, 32, 128, [2048] * 8, None),               # config-0 shape
+    (5, 4, 128, [300, 0, 4096, 17, 1], None),     # ragged, with an empty sequence
+    (3, 8, 64, [129, 2000, 16], None),
+    (4, 8, 128, [1500, 0, 2048, 77], 32),         # grouped-query: 32 query heads over 8 kv heads
 ])
-def test_static_scratch_matches_existing_entry_point(batch, heads, d, lens):
+def test_static_scratch_matches_existing_entry_point(batch, heads, d, lens, q_heads):
     lib = _lib()
-    shape, query, cache, bt, sl = _problem(batch, heads, d, lens, seed=batch * 100 + d)
+    shape, query, cache, bt, sl = _problem(batch, heads, d, lens, seed=batch * 100 + d,
+                                           q_heads=q_heads)
     ref = _existing(lib, shape, query, cache, bt, sl).cpu().numpy()
     first = _static(lib, shape, query, cache, bt, sl).cpu().numpy()
     second = _static(lib, shape, query, cache, bt, sl).cpu().numpy()  # two calls in a row
@@ -119,3 +128,9 @@ def test_static_scratch_rejects_launches_beyond_its_capacity():
     assert rc == CUDA_ERROR_INVALID_VALUE
     assert need.value > STATIC_SCRATCH_BYTES
     assert bool((out == 7.0).all()), "a refused call must not launch"
+    # the refused call left the scratch usable: the next call that fits matches
+    # the existing entry point
+    shape, query, cache, bt, sl = _problem(3, 4, 128, [600, 33, 0], seed=5)
+    ref = _existing(lib, shape, query, cache, bt, sl).cpu().numpy()
+    got = _static(lib, shape, query, cache, bt, sl).cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=0, atol=TOL)
