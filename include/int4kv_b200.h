@@ -65,15 +65,21 @@ cudaError_t cu_quantize_int4(const float* kv, int num_rows, int num_channels, ui
  * page stream: k_q[num_blocks, block_size, head_dim] uint8 (one code per byte),
  * k_scale/k_zp[num_blocks, head_dim], value[num_blocks, block_size, head_dim]
  * float32, block_lens[num_blocks] valid rows per page (clamped to
- * [0, block_size] on the device). head_dim in [1, 256]. No softmax scale. */
+ * [0, block_size] on the device). head_dim in [1, 256]. No softmax scale.
+ * One launch: query tiles x stream ranges, the ranges of a query tile merged
+ * through distributed shared memory (no scratch); logits exact on the tensor
+ * cores (integer codes x fixed-point digits of q * scale). */
 cudaError_t cu_flash_decode_int4(const float* query, const uint8_t* k_q, const float* k_scale,
                                  const float* k_zp, const float* value, const int* block_lens,
                                  int batch_size, int num_heads, int head_dim, int num_blocks,
                                  int block_size, float* output, cudaStream_t stream);
 
-/* Same contract as cu_flash_decode_int4, with the page stream split across
- * CTAs (split-KV) for parallelism: `workspace` of at least
- * int4kv_dense_decode_workspace_size() bytes, 16-byte aligned. */
+/* Same contract and kernel as cu_flash_decode_int4 (kept for callers written
+ * against an earlier form that took a split-KV workspace). cu_flash_decode_int4
+ * already splits the page stream across the CTAs of a thread-block cluster and
+ * merges the partial softmax states in distributed shared memory, so
+ * int4kv_dense_decode_workspace_size reports 16 bytes and the workspace
+ * argument is not used. */
 cudaError_t int4kv_dense_decode_workspace_size(int batch_size, int num_heads, int head_dim,
                                                int num_blocks, int block_size, size_t* bytes);
 cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const float* k_scale,

@@ -211,6 +211,18 @@ I4KV_DEVINL uint32_t ordered_key(float f) {  // monotone float -> uint32 map
   uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+I4KV_DEVINL float from_ordered_key(uint32_t k) {  // inverse of ordered_key
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Programmatic dependent launch (sm_90+): a kernel launched with the
+// programmatic-serialization attribute may start while its predecessor on the
+// stream is still running; grid_dependency_wait() blocks the calling thread
+// until the predecessor grid has completed and its memory is visible (a no-op
+// without the attribute), and allow_dependent_launch() lets the next kernel be
+// scheduled once every CTA of this grid has called it or exited.
+I4KV_DEVINL void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+I4KV_DEVINL void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // The reference's per-channel parameters (src/quantize_int4_ref.py:65-70):
 // range = max(max - min, 1e-8); scale = range / 15; zp = -min / scale.
@@ -240,6 +252,27 @@ I4KV_DEVINL uint32_t quant_code_rcp(float x, float mn, float scale, float rcp) {
   // 0 <= y <= 15 * (1 + 3 * 2^-24) for x in [mn, max], so rint(y) is already
   // in [0, 15]: the mask only keeps the nibble (and maps a NaN input to 0).
   return static_cast<uint32_t>(__float_as_int(t) - 0x4B400000) & 15u;
+}
+
+// e^x for x <= 0 given in float64: 2^(x*log2(e)) with the hardware base-2
+// exponential (relative error ~2^-22, far inside the decode's 1e-6 tolerance);
+// x = -inf gives exactly 0.
+I4KV_DEVINL float exp_neg(double x) {
+  const float y = (float)(x * 1.4426950408889634);
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
+  return r;
+}
+
+// sum = sum*r + x with a running compensation term c (Kahan): the rescale
+// applies to both, the addition captures its own rounding error in c.
+I4KV_DEVINL void kahan_rescale_add(float& sum, float& c, float r, float x) {
+  sum *= r;
+  c *= r;
+  const float y = __fsub_rn(x, c);
+  const float t = __fadd_rn(sum, y);
+  c = __fsub_rn(__fsub_rn(t, sum), y);
+  sum = t;
 }
 
 // Three-input float32 min / max (sm_100), with fminf / fmaxf semantics.
@@ -278,10 +311,10 @@ I4KV_DEVINL void fma2_rn(float& c0, float& c1, float a0, float a1, float b) {
 }
 
 // Four codes of one row's channel quad (quant_code_rcp for each, in paired
-// arithmetic), nibble-packed as c0 | c1 << 4 | c2 << 8 | c3 << 12. The low
-// byte of the bits of 1.5 * 2^23 + rint(y) is rint(y) itself, so the codes
-// are gathered with byte permutes.
-I4KV_DEVINL uint32_t pack4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
+// arithmetic), one per byte: c0 | c1 << 8 | c2 << 16 | c3 << 24. The low byte
+// of the bits of 1.5 * 2^23 + rint(y) is rint(y) itself, so the codes are
+// gathered with byte permutes.
+I4KV_DEVINL uint32_t codes4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
   constexpr float kMagic = 12582912.0f;
   constexpr float kNearHalf = 0.49999237060546875f;  // 0.5 - 2^-17
   float a0, a1, a2, a3, y0, y1, y2, y3, t0, t1, t2, t3, r0, r1, r2, r3, d0, d1, d2, d3;
@@ -301,11 +334,16 @@ I4KV_DEVINL uint32_t pack4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
     if (fabsf(d2) >= kNearHalf) t2 = __fadd_rn(__fdiv_rn(a2, sc.z), kMagic);
     if (fabsf(d3) >= kNearHalf) t3 = __fadd_rn(__fdiv_rn(a3, sc.w), kMagic);
   }
-  const uint32_t x = __byte_perm(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040),
-                                 __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040),
-                                 0x5410);                       // bytes c0, c1, c2, c3
-  const uint32_t y = x | (x >> 4);                              // c0|c1<<4, ., c2|c3<<4, .
-  return __byte_perm(y, 0u, 0x4420);                            // [c0|c1<<4][c2|c3<<4]
+  return __byte_perm(__byte_perm(__float_as_uint(t0), __float_as_uint(t1), 0x0040),
+                     __byte_perm(__float_as_uint(t2), __float_as_uint(t3), 0x0040),
+                     0x5410);  // bytes c0, c1, c2, c3 (each already in [0, 15])
+}
+
+// The same four codes nibble-packed: c0 | c1 << 4 | c2 << 8 | c3 << 12.
+I4KV_DEVINL uint32_t pack4_rcp(float4 v, float4 mn, float4 sc, float4 rc) {
+  const uint32_t x = codes4_rcp(v, mn, sc, rc);  // bytes c0, c1, c2, c3
+  const uint32_t y = x | (x >> 4);                // c0|c1<<4, ., c2|c3<<4, .
+  return __byte_perm(y, 0u, 0x4420);              // [c0|c1<<4][c2|c3<<4]
 }
 
 // q = clip(round_half_even((x - min) / scale), 0, 15)  (src/quantize_int4_ref.py:74-75)

@@ -1,268 +1,559 @@
-// Generic INT4 flash-decode over ONE shared page stream (the reference's
-// cu_flash_decode_int4 contract, csrc/flash_decode_int4.cu:104-284):
-// every query of [batch, heads] attends to the same list of pages, each page
-// [block_size, head_dim] with one code per byte, its own per-channel
-// scale/zp and a valid-row count. Any head_dim in [1, 256], any page size.
+// INT4 flash-decode over ONE shared page stream (the reference's
+// cu_flash_decode_int4 contract, csrc/flash_decode_int4.cu:104-284): every
+// query of [batch, heads] attends to the same list of pages, each page
+// [block_size, head_dim] with one code per byte (or two, in the vLLM-style
+// block cache), its own per-channel scale / zero-point and a valid-row count.
+// Any head_dim in [1, 256], any page size. No softmax scale.
 //
-// B200 mapping (CUDA cores):
-//   * A CTA serves a tile of QT queries, so every key/value byte it reads feeds
-//     QT dot products (the shared-stream case is all-queries-one-stream).
-//   * Logits: one thread per key row, QT dot products in float64 as
-//     sum_d (q_d*s_d)*c_d - sum_d q_d*zp_d*s_d (exact dequantization, the
-//     reference's float64 arbiter); no cross-lane reduction per token.
-//   * Softmax: per-warp online state over 32-row tiles; P.V with lanes over
-//     head_dim (coalesced value rows).
-//   * Split-KV: the page list can be cut into `splits` contiguous ranges, one
-//     CTA each, merged by a combine kernel. The drop-in entry point has no
-//     workspace argument and runs with one split.
+// With all queries on one stream the work is attention-shaped, not GEMV-shaped:
+// every staged key / value byte serves a tile of queries. B200 mapping:
+//
+//   * Grid: query tiles x S stream ranges; the S CTAs of one query tile form a
+//     thread-block cluster (S <= 8). Each CTA runs an online softmax over its
+//     contiguous range of 16-row page tiles; the S partial (m, l, acc) states
+//     are merged through distributed shared memory at the end -- split-KV with
+//     no workspace and no second launch.
+//   * Staging: 64-row chunks of keys and values, double-buffered in shared
+//     memory with 16-byte asynchronous copies (cp.async) into padded rows.
+//   * Logits on the tensor cores, exactly: q_d * s_d (exact in float64) is put
+//     in fixed point against the query's largest magnitude 2^E and split into
+//     eight base-128 digits; one mma.m16n8k32 (u8 codes x s8 digits, int32
+//     sums) per digit and 32 channels gives a 16-token x 8-query tile of
+//     code x digit sums, recombined in float64 with weights 2^(E-7-7j). The
+//     key is thereby dequantized as c*s - zp*s without rounding; the bias
+//     sum_d q_d zp_d s_d is a float64 sum.
+//   * Softmax: float64 running max per query, float32 weights (ex2 of the
+//     float64 difference), Kahan-compensated float32 sums.
+//   * P.V in float32 FMAs: each thread owns 2 queries x 4 channels.
+//   * QT x DP = 2048 (queries per CTA x padded head dim): 16 queries at d128;
+//     eight warps, and under 114 KB of shared memory up to d128 so that two
+//     CTAs share an SM.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "../../include/int4kv_b200.h"
 
+namespace cg = cooperative_groups;
 using namespace i4kv;
 
 namespace {
 
-constexpr int kQT = 4;        // queries per CTA
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
+constexpr int kChunk = 64;     // staged rows per chunk: four 16-row MMA tiles
+constexpr int kDig = 8;        // base-128 digits of the fixed-point q * s
+constexpr int kMaxSplit = 8;   // cluster size (portable limit)
 constexpr int kMaxD = 256;
-constexpr int kDPL = kMaxD / 32;
 constexpr uint32_t kFull = 0xffffffffu;
 
 struct DenseArgs {
-  const float* q;
-  const uint8_t* kq;
-  const float* ks;
-  const float* kz;
-  const void* v;
-  const int* lens;
-  int nq, D, nb, bs, splits;
-  float* out;       // final output (splits == 1)
-  char* ws;         // partial records (splits > 1)
-  const int* ids;   // nullable: page pg of the stream is block ids[pg] of the storage
-  int num_blocks;   // storage blocks (ids outside [0, num_blocks) are skipped)
+  const float* q;      // [nq, D]
+  const uint8_t* kq;   // [num_blocks, bs, RB]: RB = D (one code per byte) or ceil(D/2)
+  const float* ks;     // [num_blocks, D]
+  const float* kz;     // [num_blocks, D]
+  const void* v;       // [num_blocks, bs, D] of the value type
+  const int* lens;     // [num_blocks] valid rows per block (clamped to [0, bs])
+  const int* ids;      // nullable: stream page pi is storage block ids[pi]
+  int nq, D, np, bs, num_blocks;  // np: pages in the stream
+  float* out;          // [nq, D]
 };
 
-// Code of dim d in a key row: one code per byte, or two per byte (low
-// nibble = even dim) in the packed storage of the vLLM-style block cache.
-template <bool PACKED>
-__device__ __forceinline__ double key_code(const uint8_t* krow, int d) {
-  if constexpr (PACKED) {
-    return (double)((krow[d >> 1] >> ((d & 1) << 2)) & 15);
-  } else {
-    return (double)krow[d];
-  }
+template <int DP, bool PACKED, int VK>
+struct DCfg {
+  static constexpr int QT = 2048 / DP;                     // queries per CTA
+  static constexpr int NOCT = QT / 8;                      // 8-query MMA column blocks
+  static constexpr int KK = DP / 32;                       // 32-position k-steps of a digit row
+  static constexpr int VB = VK == 0 ? 4 : 2;               // stored value bytes
+  // Staged key rows and digit rows are padded by 16 bytes: a row stride of
+  // 4 x (odd) words puts the eight rows an ldmatrix / B-operand load touches
+  // on distinct banks.
+  static constexpr int KROW = (PACKED ? DP / 2 : DP) + 16;
+  static constexpr int DROW = DP + 16;
+  static constexpr int QP = QT / 2;                        // P.V: query pairs
+  static constexpr int DG = DP / 4;                        // P.V: channel groups of 4
+  static_assert(QP * DG == kThreads, "P.V: one (2 queries x 4 channels) block per thread");
+  static constexpr int PROW = kChunk + 1;                  // weights [QT][PROW]: conflict-free
+  // shared-memory layout (bytes); the chunk's weights overwrite its logits
+  static constexpr size_t OFF_DIG = 0;                                    // u8 [kDig][QT][DROW]
+  static constexpr size_t OFF_K = OFF_DIG + (size_t)kDig * QT * DROW;     // u8 [2][kChunk][KROW]
+  static constexpr size_t OFF_V = OFF_K + (size_t)2 * kChunk * KROW;      // [2][kChunk][DP] values
+  static constexpr size_t OFF_LG = OFF_V + (size_t)2 * kChunk * DP * VB;  // double [QT][kChunk]
+  static constexpr size_t OFF_P = OFF_LG;                                 // float [QT][PROW]
+  static_assert((size_t)QT * PROW * 4 <= (size_t)QT * kChunk * 8, "weights fit over the logits");
+  static constexpr size_t OFF_BIAS = OFF_LG + (size_t)QT * kChunk * 8;    // double [QT]
+  static constexpr size_t OFF_M = OFF_BIAS + (size_t)QT * 8;              // double [QT]
+  static constexpr size_t OFF_W = OFF_M + (size_t)QT * 8;                 // double [QT][kMaxSplit]
+  static constexpr size_t OFF_L = OFF_W + (size_t)QT * kMaxSplit * 8;     // float [QT] (l), [QT] (c)
+  static constexpr size_t OFF_E = OFF_L + (size_t)QT * 8;                 // int [QT]
+  static constexpr size_t OFF_CORR = OFF_E + (size_t)QT * 4;              // float [QT]
+  static constexpr size_t OFF_LL = OFF_CORR + (size_t)QT * 4;             // double [QT] (merged L)
+  static constexpr size_t SMEM = OFF_LL + (size_t)QT * 8;
+  // the merge reuses the value stages for acc [QT][DP] float
+  static_assert((size_t)QT * DP * 4 <= (size_t)2 * kChunk * DP * VB, "acc fits the value stages");
+  static_assert(OFF_DIG % 16 == 0 && OFF_K % 16 == 0 && OFF_V % 16 == 0 && OFF_LG % 16 == 0 &&
+                    OFF_P % 16 == 0,
+                "alignment");
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <int VK>
-__device__ __forceinline__ float value_at(const void* vrow, int d) {
+__device__ __forceinline__ float4 load_v4(const char* p) {
   if constexpr (VK == 0) {
-    return static_cast<const float*>(vrow)[d];
-  } else if constexpr (VK == 1) {
-    return __half2float(static_cast<const __half*>(vrow)[d]);
+    return *reinterpret_cast<const float4*>(p);
   } else {
-    return __bfloat162float(static_cast<const __nv_bfloat16*>(vrow)[d]);
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    if constexpr (VK == 1) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+      return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+      return make_float4(a.x, a.y, b.x, b.y);
+    }
   }
 }
 
-// Partial record: [m f64][l f32][pad][acc D f32], padded to a multiple of 16
-// bytes so every record (and its double) stays aligned for any head_dim.
-__host__ __device__ inline size_t dense_rec_bytes(int D) { return 16 + 16 * (((size_t)D + 3) / 4); }
+// One chunk of the CTA's range: rows [row0, row0 + rows) of stream page pi
+// (storage block pg), rows > 0.
+struct Chunk {
+  int pi, pg, row0, rows;
+};
 
-template <bool PACKED, int VK>
+// The next non-empty chunk at or after tile `cur` (tiles of 16 rows, tpp per
+// page) and before `end`; advances `cur` past it. Uniform across the CTA.
+__device__ __forceinline__ bool next_chunk(const DenseArgs& a, int tpp, long long& cur,
+                                           long long end, Chunk& c) {
+  while (cur < end) {
+    const int pi = (int)(cur / tpp);
+    const int i = (int)(cur - (long long)pi * tpp);
+    const int nt = (int)min((long long)min(4, tpp - i), end - cur);
+    cur += nt;
+    const int pg = a.ids ? __ldg(a.ids + pi) : pi;
+    if (pg < 0 || pg >= a.num_blocks) continue;  // unknown block id: skipped, never read
+    const int len = min(max(__ldg(a.lens + pg), 0), a.bs);
+    const int row0 = 16 * i;
+    const int rows = min(16 * nt, len - row0);
+    if (rows <= 0) continue;
+    c = Chunk{pi, pg, row0, rows};
+    return true;
+  }
+  return false;
+}
+
+// Stage the codes and values of chunk c into buffer `buf` (asynchronous when
+// every row starts on a 16-byte boundary, else plain loads).
+template <int DP, bool PACKED, int VK>
+__device__ __forceinline__ void load_chunk(const DenseArgs& a, const Chunk& c, char* smem, int buf,
+                                           bool aligned) {
+  using Cf = DCfg<DP, PACKED, VK>;
+  const int RB = PACKED ? (a.D + 1) / 2 : a.D;
+  uint8_t* sk = reinterpret_cast<uint8_t*>(smem + Cf::OFF_K) + (size_t)buf * kChunk * Cf::KROW;
+  char* sv = smem + Cf::OFF_V + (size_t)buf * kChunk * DP * Cf::VB;
+  const uint8_t* gk = a.kq + ((size_t)c.pg * a.bs + c.row0) * RB;
+  const char* gv = static_cast<const char*>(a.v) + ((size_t)c.pg * a.bs + c.row0) * a.D * Cf::VB;
+  const int vrow = a.D * Cf::VB;
+  if (aligned) {
+    const int kp = RB / 16, vp = vrow / 16;
+    for (int i = threadIdx.x; i < c.rows * kp; i += kThreads) {
+      const int r = i / kp, j = i - r * kp;
+      cp_async16(sk + r * Cf::KROW + 16 * j, gk + (size_t)r * RB + 16 * j);
+    }
+    for (int i = threadIdx.x; i < c.rows * vp; i += kThreads) {
+      const int r = i / vp, j = i - r * vp;
+      cp_async16(sv + (size_t)r * DP * Cf::VB + 16 * j, gv + (size_t)r * vrow + 16 * j);
+    }
+  } else {
+    for (int i = threadIdx.x; i < c.rows * RB; i += kThreads) {
+      const int r = i / RB, j = i - r * RB;
+      sk[r * Cf::KROW + j] = __ldg(gk + (size_t)r * RB + j);
+    }
+    for (int i = threadIdx.x; i < c.rows * a.D; i += kThreads) {
+      const int r = i / a.D, d = i - r * a.D;
+      if constexpr (Cf::VB == 4) {
+        reinterpret_cast<float*>(sv)[(size_t)r * DP + d] =
+            __ldg(reinterpret_cast<const float*>(gv) + (size_t)r * a.D + d);
+      } else {
+        reinterpret_cast<uint16_t*>(sv)[(size_t)r * DP + d] =
+            __ldg(reinterpret_cast<const unsigned short*>(gv) + (size_t)r * a.D + d);
+      }
+    }
+  }
+}
+
+// Position of channel d in a digit row: d itself for one code per byte; for
+// packed codes the even channels of each 64-channel block come first, then the
+// odd ones (the low / high nibbles of the block's 32 key bytes).
+template <bool PACKED>
+__device__ __forceinline__ int dig_pos(int d) {
+  if constexpr (PACKED) return (d & ~63) | ((d & 1) << 5) | ((d & 63) >> 1);
+  else return d;
+}
+
+// Fixed-point digits and bias of the CTA's queries (q0 ..) against page pg's
+// scales: each thread takes 8 channels of one query.
+template <int DP, bool PACKED, int VK>
+__device__ __forceinline__ void page_digits(const DenseArgs& a, int q0, int pg, char* smem) {
+  using Cf = DCfg<DP, PACKED, VK>;
+  constexpr int TPQ = kThreads / Cf::QT;  // threads per query (a power of two <= 32)
+  static_assert(TPQ * 8 == DP, "8 channels per thread");
+  uint8_t* sdig = reinterpret_cast<uint8_t*>(smem + Cf::OFF_DIG);
+  const int q = threadIdx.x / TPQ;
+  const int d0 = (threadIdx.x % TPQ) * 8;
+  const bool qok = q0 + q < a.nq;
+  const float* qrow = a.q + (size_t)(q0 + q) * a.D;
+  double qs[8];
+  double amax = 0.0, bsum = 0.0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int d = d0 + k;
+    double x = 0.0;
+    if (qok && d < a.D) {
+      const double qd = (double)__ldg(qrow + d);
+      const double sd = (double)__ldg(a.ks + (size_t)pg * a.D + d);
+      x = qd * sd;  // exact: a product of two float32 values
+      bsum = fma(qd, (double)__ldg(a.kz + (size_t)pg * a.D + d) * sd, bsum);
+    }
+    qs[k] = x;
+    amax = fmax(amax, fabs(x));
+  }
+  int bexp = amax > 0.0 ? ((__double2hiint(amax) >> 20) & 0x7FF) : 0;
+#pragma unroll
+  for (int o = TPQ / 2; o > 0; o >>= 1) {
+    bexp = max(bexp, __shfl_xor_sync(kFull, bexp, o));
+    bsum += __shfl_xor_sync(kFull, bsum, o);
+  }
+  // |q*s| < 2^E; float32 products lie in [2^-298, 2^256], so every power of
+  // two used here and in the recombination is a normal double
+  const int E = bexp > 0 ? bexp - 1022 : 0;
+  if (threadIdx.x % TPQ == 0) {
+    reinterpret_cast<double*>(smem + Cf::OFF_BIAS)[q] = bsum;
+    reinterpret_cast<int*>(smem + Cf::OFF_E)[q] = E;
+  }
+  const double scale = __hiloint2double((1023 + 56 - E) << 20, 0);
+  long long X[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) X[k] = __double2ll_rn(qs[k] * scale);  // |X| < 2^56
+#pragma unroll
+  for (int j = 0; j < kDig; ++j) {  // digit j: bits [49 - 7j, 56 - 7j) of X, the top one signed
+    const int sh = 49 - 7 * j;
+    const long long m = j == 0 ? 0xFF : 0x7F;
+    uint8_t* row = sdig + ((size_t)j * Cf::QT + q) * Cf::DROW;
+    const uint32_t w0 = (uint32_t)(((X[0] >> sh) & m) | (((X[1] >> sh) & m) << 8) |
+                                   (((X[2] >> sh) & m) << 16) | (((X[3] >> sh) & m) << 24));
+    const uint32_t w1 = (uint32_t)(((X[4] >> sh) & m) | (((X[5] >> sh) & m) << 8) |
+                                   (((X[6] >> sh) & m) << 16) | (((X[7] >> sh) & m) << 24));
+    if constexpr (PACKED) {
+      // even channels d0, d0+2, .., d0+6 and the odd ones: 4 bytes each
+      *reinterpret_cast<uint32_t*>(row + dig_pos<true>(d0)) = __byte_perm(w0, w1, 0x6420);
+      *reinterpret_cast<uint32_t*>(row + dig_pos<true>(d0 + 1)) = __byte_perm(w0, w1, 0x7531);
+    } else {
+      *reinterpret_cast<uint2*>(row + d0) = make_uint2(w0, w1);
+    }
+  }
+}
+
+template <int DP, bool PACKED, int VK>
 __global__ void __launch_bounds__(kThreads)
-dense_decode_kernel(DenseArgs a) {
-  __shared__ float s_q[kQT][kMaxD];
-  __shared__ double s_qs[kQT][kMaxD];   // q_d * s_d of the current page (exact)
-  __shared__ double s_bias[kQT];        // sum_d q_d * zp_d * s_d of the current page
-  __shared__ double s_m[kWarps][kQT];
-  __shared__ float s_l[kWarps][kQT];
-  __shared__ float s_acc[kWarps][kQT][kMaxD];
-
+shared_stream_decode_kernel(DenseArgs a) {
+  using Cf = DCfg<DP, PACKED, VK>;
+  constexpr int QT = Cf::QT;
+  extern __shared__ __align__(128) char smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  const int q0 = (blockIdx.x / S) * QT;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int q0 = blockIdx.x * kQT;
-  const int nqt = min(kQT, a.nq - q0);
-  const int D = a.D;
-  const int split = blockIdx.y;
-  const int pb = (int)((long long)split * a.nb / a.splits);
-  const int pe = (int)((long long)(split + 1) * a.nb / a.splits);
+  const int g = lane >> 2, t = lane & 3;
 
-  for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
-    const int qi = i / D, d = i - qi * D;
-    s_q[qi][d] = qi < nqt ? a.q[(size_t)(q0 + qi) * D + d] : 0.f;
+  double* s_lg = reinterpret_cast<double*>(smem + Cf::OFF_LG);
+  float* s_p = reinterpret_cast<float*>(smem + Cf::OFF_P);
+  double* s_bias = reinterpret_cast<double*>(smem + Cf::OFF_BIAS);
+  double* s_m = reinterpret_cast<double*>(smem + Cf::OFF_M);
+  float* s_l = reinterpret_cast<float*>(smem + Cf::OFF_L);
+  float* s_lc = s_l + QT;
+  int* s_E = reinterpret_cast<int*>(smem + Cf::OFF_E);
+  float* s_corr = reinterpret_cast<float*>(smem + Cf::OFF_CORR);
+  const uint8_t* sdig = reinterpret_cast<const uint8_t*>(smem + Cf::OFF_DIG);
+
+  for (int i = threadIdx.x; i < QT; i += kThreads) {
+    s_m[i] = -INFINITY;
+    s_l[i] = 0.f;
+    s_lc[i] = 0.f;
   }
 
-  double m_w[kQT];
-  float l_lane[kQT];
-  float acc[kQT][kDPL];
-#pragma unroll
-  for (int qi = 0; qi < kQT; ++qi) {
-    m_w[qi] = -INFINITY;
-    l_lane[qi] = 0.f;
-#pragma unroll
-    for (int k = 0; k < kDPL; ++k) acc[qi][k] = 0.f;
-  }
+  // this CTA's contiguous range of 16-row tiles of the stream
+  const int tpp = (a.bs + 15) / 16;
+  const long long total = (long long)a.np * tpp;
+  long long cur = total * rank / S;
+  const long long end = total * (rank + 1) / S;
+  const int RB = PACKED ? (a.D + 1) / 2 : a.D;
+  const bool aligned = (RB % 16 == 0) && ((a.D * Cf::VB) % 16 == 0) &&
+                       ((reinterpret_cast<uintptr_t>(a.kq) | reinterpret_cast<uintptr_t>(a.v)) & 15u) == 0;
 
-  const int row_bytes = PACKED ? (D + 1) / 2 : D;
-  constexpr int VB = VK == 0 ? 4 : 2;
-  for (int pi = pb; pi < pe; ++pi) {
-    const int pg = a.ids ? a.ids[pi] : pi;  // storage block of the stream's page pi
-    if (pg < 0 || pg >= a.num_blocks) continue;  // uniform across the CTA
-    __syncthreads();  // previous page's folded constants no longer in use
-    for (int i = threadIdx.x; i < kQT * D; i += kThreads) {
-      const int qi = i / D, d = i - qi * D;
-      s_qs[qi][d] = (double)s_q[qi][d] * (double)a.ks[(size_t)pg * D + d];
-    }
-    if (warp < kQT) {  // warp qi reduces sum_d q_d * zp_d * s_d for query qi
-      double b = 0.0;
-      for (int d = lane; d < D; d += 32)
-        b = fma((double)s_q[warp][d],
-                (double)a.kz[(size_t)pg * D + d] * (double)a.ks[(size_t)pg * D + d], b);
+  // P.V ownership: queries 2qp, 2qp+1 x channels 4dg .. 4dg+3
+  const int qp = threadIdx.x % Cf::QP, dg = threadIdx.x / Cf::QP;
+  float acc[2][4], acc_c[2][4];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) b += __shfl_xor_sync(kFull, b, o);
-      if (lane == 0) s_bias[warp] = b;
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f, acc_c[i][j] = 0.f;
+
+  Chunk c{}, nc{};
+  bool have = next_chunk(a, tpp, cur, end, c);
+  if (have) {
+    load_chunk<DP, PACKED, VK>(a, c, smem, 0, aligned);
+    cp_async_commit();
+  }
+  int dig_pg = -1;
+  int buf = 0;
+  __syncthreads();  // running state initialised
+  while (have) {
+    const bool more = next_chunk(a, tpp, cur, end, nc);
+    if (more) load_chunk<DP, PACKED, VK>(a, nc, smem, buf ^ 1, aligned);
+    cp_async_commit();
+    if (c.pg != dig_pg) {  // new page: its scales into the query digits
+      page_digits<DP, PACKED, VK>(a, q0, c.pg, smem);
+      dig_pg = c.pg;
     }
+    cp_async_wait<1>();  // this chunk's copies (the next chunk's may still fly)
     __syncthreads();
-    const int blen = min(max(a.lens[pg], 0), a.bs);  // defence in depth, as the reference
-    const uint8_t* kpage = a.kq + (size_t)pg * a.bs * row_bytes;
-    const char* vpage = static_cast<const char*>(a.v) + (size_t)pg * a.bs * D * VB;
-    for (int r0 = warp * 32; r0 < blen; r0 += kThreads) {
-      const int r = r0 + lane;
-      const bool valid = r < blen;
-      double lg[kQT];
+
+    // ---- logits: units (8-query block o, 16-row tile ti), one per warp at d128 ----
+    const uint8_t* sk = reinterpret_cast<const uint8_t*>(smem + Cf::OFF_K) + (size_t)buf * kChunk * Cf::KROW;
+    for (int u = warp; u < Cf::NOCT * 4; u += kWarps) {
+      const int o = u >> 2, ti = u & 3;
+      if (16 * ti >= c.rows) continue;  // warp-uniform
+      uint32_t A[Cf::KK][4];
+      const uint8_t* rowp = sk + (16 * ti + (lane & 7) + 8 * ((lane >> 3) & 1)) * Cf::KROW + 16 * (lane >> 4);
+      if constexpr (PACKED) {
 #pragma unroll
-      for (int qi = 0; qi < kQT; ++qi) lg[qi] = 0.0;
-      if (valid) {
-        const uint8_t* krow = kpage + (size_t)r * row_bytes;
-        for (int d = 0; d < D; ++d) {
-          const double code = key_code<PACKED>(krow, d);
+        for (int e = 0; e < Cf::KK / 2; ++e) {
+          uint32_t r[4];
+          ldmatrix_x4(r, rowp + 32 * e);
 #pragma unroll
-          for (int qi = 0; qi < kQT; ++qi) lg[qi] = fma(s_qs[qi][d], code, lg[qi]);
-        }
-#pragma unroll
-        for (int qi = 0; qi < kQT; ++qi) lg[qi] -= s_bias[qi];
-      }
-      const int nrow = min(32, blen - r0);
-#pragma unroll
-      for (int qi = 0; qi < kQT; ++qi) {
-        double l = valid ? lg[qi] : -INFINITY;
-        double mx = l;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(kFull, mx, o));
-        const double m_new = fmax(m_w[qi], mx);
-        const float corr = expf((float)(m_w[qi] - m_new));
-        const float p = expf((float)(l - m_new));
-        l_lane[qi] = l_lane[qi] * corr + p;
-        m_w[qi] = m_new;
-#pragma unroll
-        for (int k = 0; k < kDPL; ++k) acc[qi][k] *= corr;
-        lg[qi] = p;  // reuse as this lane's probability
-      }
-      for (int j = 0; j < nrow; ++j) {
-        const char* vrow = vpage + (size_t)(r0 + j) * D * VB;
-        float pj[kQT];
-#pragma unroll
-        for (int qi = 0; qi < kQT; ++qi) pj[qi] = __shfl_sync(kFull, (float)lg[qi], j);
-#pragma unroll
-        for (int k = 0; k < kDPL; ++k) {
-          const int d = lane + 32 * k;
-          if (d < D) {
-            const float vv = value_at<VK>(vrow, d);
-#pragma unroll
-            for (int qi = 0; qi < kQT; ++qi) acc[qi][k] = fmaf(pj[qi], vv, acc[qi][k]);
+          for (int k = 0; k < 4; ++k) {
+            A[2 * e][k] = r[k] & 0x0F0F0F0Fu;
+            A[2 * e + 1][k] = (r[k] >> 4) & 0x0F0F0F0Fu;
           }
         }
+      } else {
+#pragma unroll
+        for (int e = 0; e < Cf::KK; ++e) ldmatrix_x4(A[e], rowp + 32 * e);
+      }
+      // eight independent accumulator chains, one per digit
+      int cs[kDig][4];
+#pragma unroll
+      for (int j = 0; j < kDig; ++j) cs[j][0] = cs[j][1] = cs[j][2] = cs[j][3] = 0;
+      const uint8_t* dcol = sdig + (size_t)(8 * o + g) * Cf::DROW + 4 * t;
+#pragma unroll
+      for (int kk = 0; kk < Cf::KK; ++kk) {
+#pragma unroll
+        for (int j = 0; j < kDig; ++j) {
+          const uint8_t* drow = dcol + (size_t)j * QT * Cf::DROW + 32 * kk;
+          mma_u8s8_16832(cs[j], A[kk], *reinterpret_cast<const uint32_t*>(drow),
+                         *reinterpret_cast<const uint32_t*>(drow + 16));
+        }
+      }
+      const int qa = 8 * o + 2 * t, qb = qa + 1;
+      double wa = __hiloint2double((1023 + s_E[qa] - 7) << 20, 0);
+      double wb = __hiloint2double((1023 + s_E[qb] - 7) << 20, 0);
+      double lg[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+      for (int j = 0; j < kDig; ++j) {
+        lg[0] = fma((double)cs[j][0], wa, lg[0]);
+        lg[1] = fma((double)cs[j][1], wb, lg[1]);
+        lg[2] = fma((double)cs[j][2], wa, lg[2]);
+        lg[3] = fma((double)cs[j][3], wb, lg[3]);
+        wa *= 0.0078125;  // 2^-7: the next digit's weight (exact)
+        wb *= 0.0078125;
+      }
+      const int r0 = 16 * ti + g, r1 = r0 + 8;
+      s_lg[qa * kChunk + r0] = r0 < c.rows ? lg[0] - s_bias[qa] : -INFINITY;
+      s_lg[qb * kChunk + r0] = r0 < c.rows ? lg[1] - s_bias[qb] : -INFINITY;
+      s_lg[qa * kChunk + r1] = r1 < c.rows ? lg[2] - s_bias[qa] : -INFINITY;
+      s_lg[qb * kChunk + r1] = r1 < c.rows ? lg[3] - s_bias[qb] : -INFINITY;
+    }
+    __syncthreads();
+
+    // ---- online softmax over the chunk: lane covers rows lane, lane + 32 ----
+    constexpr int QW = (QT + kWarps - 1) / kWarps;  // queries per warp
+    double xs[QW][2];
+#pragma unroll
+    for (int k = 0; k < QW; ++k) {
+      const int qi = warp + k * kWarps;
+      xs[k][0] = (qi < QT && lane < c.rows) ? s_lg[qi * kChunk + lane] : -INFINITY;
+      xs[k][1] = (qi < QT && lane + 32 < c.rows) ? s_lg[qi * kChunk + lane + 32] : -INFINITY;
+    }
+    __syncthreads();  // the weights overwrite the logits
+#pragma unroll
+    for (int k = 0; k < QW; ++k) {
+      const int qi = warp + k * kWarps;
+      if (qi >= QT) break;
+      double mx = fmax(xs[k][0], xs[k][1]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmax(mx, __shfl_xor_sync(kFull, mx, off));
+      const double m_old = s_m[qi];
+      const double m_new = fmax(m_old, mx);
+      float p0 = 0.f, p1 = 0.f, corr = 1.f;
+      if (m_new != -INFINITY) {
+        p0 = exp_neg(xs[k][0] - m_new);
+        p1 = exp_neg(xs[k][1] - m_new);
+        corr = exp_neg(m_old - m_new);  // 0 for the first live chunk (m_old = -inf)
+      }
+      s_p[qi * Cf::PROW + lane] = p0;
+      s_p[qi * Cf::PROW + lane + 32] = p1;
+      float ps = p0 + p1;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(kFull, ps, off);
+      if (lane == 0) {
+        float l = s_l[qi], lc = s_lc[qi];
+        kahan_rescale_add(l, lc, corr, ps);
+        s_l[qi] = l;
+        s_lc[qi] = lc;
+        s_m[qi] = m_new;
+        s_corr[qi] = corr;
       }
     }
-  }
+    __syncthreads();
 
-  // merge the warps' states
+    // ---- P.V: this thread's 2 queries x 4 channels ----
+    {
+      const char* vp = smem + Cf::OFF_V + (size_t)buf * kChunk * DP * Cf::VB + (size_t)(4 * dg) * Cf::VB;
+      const float* pa = s_p + (2 * qp) * Cf::PROW;
+      const float* pb = pa + Cf::PROW;
+      float ch[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+      for (int r = 0; r < c.rows; ++r) {
+        const float4 v4 = load_v4<VK>(vp + (size_t)r * DP * Cf::VB);
+        const float x = pa[r], y = pb[r];
+        ch[0][0] = fmaf(x, v4.x, ch[0][0]); ch[0][1] = fmaf(x, v4.y, ch[0][1]);
+        ch[0][2] = fmaf(x, v4.z, ch[0][2]); ch[0][3] = fmaf(x, v4.w, ch[0][3]);
+        ch[1][0] = fmaf(y, v4.x, ch[1][0]); ch[1][1] = fmaf(y, v4.y, ch[1][1]);
+        ch[1][2] = fmaf(y, v4.z, ch[1][2]); ch[1][3] = fmaf(y, v4.w, ch[1][3]);
+      }
+      const float ca = s_corr[2 * qp], cb = s_corr[2 * qp + 1];
 #pragma unroll
-  for (int qi = 0; qi < kQT; ++qi) {
-    float l = l_lane[qi];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(kFull, l, o);
-    if (lane == 0) {
-      s_m[warp][qi] = m_w[qi];
-      s_l[warp][qi] = l;
+      for (int j = 0; j < 4; ++j) {
+        kahan_rescale_add(acc[0][j], acc_c[0][j], ca, ch[0][j]);
+        kahan_rescale_add(acc[1][j], acc_c[1][j], cb, ch[1][j]);
+      }
     }
+    __syncthreads();  // the stage, digits and weights are free for the next chunk
+    c = nc;
+    have = more;
+    buf ^= 1;
+  }
+  cp_async_wait<0>();
+
+  // ---- merge the cluster's S partial states through distributed shared memory ----
+  float* s_acc = reinterpret_cast<float*>(smem + Cf::OFF_V);  // [QT][DP], over the value stages
+  __syncthreads();
 #pragma unroll
-    for (int k = 0; k < kDPL; ++k) {
-      const int d = lane + 32 * k;
-      if (d < D) s_acc[warp][qi][d] = acc[qi][k];
+  for (int i = 0; i < 2; ++i)
+    *reinterpret_cast<float4*>(s_acc + (2 * qp + i) * DP + 4 * dg) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  cluster.sync();  // every rank's (m, l, acc) is final and visible
+  double* s_w = reinterpret_cast<double*>(smem + Cf::OFF_W);
+  double* s_L = reinterpret_cast<double*>(smem + Cf::OFF_LL);
+  for (int qi = threadIdx.x; qi < QT; qi += kThreads) {
+    double M = -INFINITY;
+    for (int r = 0; r < S; ++r) M = fmax(M, cluster.map_shared_rank(s_m, r)[qi]);
+    double L = 0.0;
+    for (int r = 0; r < S; ++r) {
+      const double mr = cluster.map_shared_rank(s_m, r)[qi];
+      const double w = mr == -INFINITY ? 0.0 : exp(mr - M);
+      s_w[qi * kMaxSplit + r] = w;
+      L = fma((double)cluster.map_shared_rank(s_l, r)[qi], w, L);
     }
+    s_L[qi] = L;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < nqt * D; i += kThreads) {
-    const int qi = i / D, d = i - qi * D;
-    double M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmax(M, s_m[w][qi]);
-    float L = 0.f, o = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        if (s_m[w][qi] == -INFINITY) continue;
-        const float e = expf((float)(s_m[w][qi] - M));
-        L = fmaf(s_l[w][qi], e, L);
-        o = fmaf(s_acc[w][qi][d], e, o);
-      }
-    }
-    if (a.splits == 1) {
-      a.out[(size_t)(q0 + qi) * D + d] = __fdiv_rn(o, fmaxf(L, 1e-10f));
-    } else {
-      char* rec = a.ws + ((size_t)(q0 + qi) * a.splits + split) * dense_rec_bytes(D);
-      if (d == 0) {
-        *reinterpret_cast<double*>(rec) = M;
-        *reinterpret_cast<float*>(rec + 8) = L;
-      }
-      reinterpret_cast<float*>(rec + 16)[d] = o;
-    }
+  const int per = (QT * DP + S - 1) / S;  // (query, channel) outputs this rank finishes
+  for (int i = threadIdx.x; i < per; i += kThreads) {
+    const int idx = rank * per + i;
+    if (idx >= QT * DP) break;
+    const int qi = idx / DP, d = idx - qi * DP;
+    if (q0 + qi >= a.nq || d >= a.D) continue;
+    double o = 0.0;
+    for (int r = 0; r < S; ++r)
+      o = fma((double)cluster.map_shared_rank(s_acc, r)[qi * DP + d], s_w[qi * kMaxSplit + r], o);
+    a.out[(size_t)(q0 + qi) * a.D + d] = (float)(o / fmax(s_L[qi], 1e-10));
   }
+  cluster.sync();  // peers finished reading this CTA's shared memory
 }
 
-__global__ void __launch_bounds__(128)
-dense_combine_kernel(const char* __restrict__ ws, int nq, int D, int splits, float* __restrict__ out) {
-  const int qi = blockIdx.x;
-  if (qi >= nq) return;
-  const size_t rb = dense_rec_bytes(D);
-  const char* base = ws + (size_t)qi * splits * rb;
-  double M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmax(M, *reinterpret_cast<const double*>(base + s * rb));
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float L = 0.f, o = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < splits; ++s) {
-        const char* rec = base + s * rb;
-        const double m = *reinterpret_cast<const double*>(rec);
-        if (m == -INFINITY) continue;
-        const float e = expf((float)(m - M));
-        L = fmaf(*reinterpret_cast<const float*>(rec + 8), e, L);
-        o = fmaf(reinterpret_cast<const float*>(rec + 16)[d], e, o);
-      }
-    }
-    out[(size_t)qi * D + d] = __fdiv_rn(o, fmaxf(L, 1e-10f));
-  }
-}
-
-int choose_splits(int nq, int nb) {
+template <int DP, bool PACKED, int VK>
+cudaError_t launch_shared(const DenseArgs& a, cudaStream_t stream) {
+  using Cf = DCfg<DP, PACKED, VK>;
+  static std::mutex mu;
+  static bool attr_done[64] = {};
   int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int tiles = (nq + kQT - 1) / kQT;
-  int splits = (2 * sms + tiles - 1) / tiles;
-  if (splits > nb) splits = nb;
-  if (splits > 64) splits = 64;
-  return splits < 1 ? 1 : splits;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  auto kern = shared_stream_decode_kernel<DP, PACKED, VK>;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!attr_done[dev]) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM);
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = true;
+    }
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int qtiles = (a.nq + Cf::QT - 1) / Cf::QT;
+  const long long tiles = (long long)a.np * ((a.bs + 15) / 16);
+  // enough stream ranges to give the GPU about two CTAs per SM, at most one
+  // cluster of 8 per query tile and no more ranges than 16-row tiles
+  int S = (2 * sms + qtiles - 1) / qtiles;
+  S = (int)max(1LL, min((long long)min(S, kMaxSplit), tiles));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(qtiles * S), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cf::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <bool PACKED, int VK>
+cudaError_t dispatch_dp(const DenseArgs& a, cudaStream_t stream) {
+  const int dp = PACKED ? ((a.D + 63) / 64) * 64 : ((a.D + 31) / 32) * 32;
+  if constexpr (!PACKED) {
+    if (dp <= 32) return launch_shared<32, PACKED, VK>(a, stream);
+  }
+  if (dp <= 64) return launch_shared<64, PACKED, VK>(a, stream);
+  if (dp <= 128) return launch_shared<128, PACKED, VK>(a, stream);
+  return launch_shared<256, PACKED, VK>(a, stream);
 }
 
 cudaError_t check(const float* query, const uint8_t* k_q, const float* k_scale, const float* k_zp,
-                  const float* value, const int* block_lens, int batch_size, int num_heads,
+                  const void* value, const int* block_lens, int batch_size, int num_heads,
                   int head_dim, int num_blocks, int block_size, const float* output) {
   if (head_dim <= 0 || head_dim > kMaxD) return cudaErrorInvalidValue;
   if (batch_size <= 0 || num_heads <= 0 || num_blocks < 0 || block_size < 0) return cudaErrorInvalidValue;
@@ -270,6 +561,19 @@ cudaError_t check(const float* query, const uint8_t* k_q, const float* k_scale, 
   if (!query || !output) return cudaErrorInvalidValue;
   if (num_blocks > 0 && (!k_q || !k_scale || !k_zp || !value || !block_lens)) return cudaErrorInvalidValue;
   return cudaSuccess;
+}
+
+cudaError_t run(const DenseArgs& a, bool packed, int value_dtype, cudaStream_t stream) {
+  if (a.np == 0 || a.bs == 0) {  // an empty stream: every output is 0 (reference: o / max(0, 1e-10))
+    const cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)a.nq * a.D * sizeof(float), stream);
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
+  if (!packed) return dispatch_dp<false, 0>(a, stream);
+  switch (value_dtype) {
+    case INT4KV_VALUES_F32: return dispatch_dp<true, 0>(a, stream);
+    case INT4KV_VALUES_F16: return dispatch_dp<true, 1>(a, stream);
+    default: return dispatch_dp<true, 2>(a, stream);
+  }
 }
 
 }  // namespace
@@ -283,11 +587,9 @@ cudaError_t cu_flash_decode_int4(const float* query, const uint8_t* k_q, const f
   cudaError_t e = check(query, k_q, k_scale, k_zp, value, block_lens, batch_size, num_heads,
                         head_dim, num_blocks, block_size, output);
   if (e != cudaSuccess) return e;
-  const int nq = batch_size * num_heads;
-  DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
-              1, output, nullptr, nullptr, num_blocks};
-  dense_decode_kernel<false, 0><<<dim3((nq + kQT - 1) / kQT, 1), kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  const DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nullptr, batch_size * num_heads,
+                    head_dim, num_blocks, block_size, num_blocks, output};
+  return run(a, false, INT4KV_VALUES_F32, stream);
 }
 
 cudaError_t int4kv_dense_decode_workspace_size(int batch_size, int num_heads, int head_dim,
@@ -295,9 +597,7 @@ cudaError_t int4kv_dense_decode_workspace_size(int batch_size, int num_heads, in
   if (!bytes || head_dim <= 0 || head_dim > kMaxD || batch_size <= 0 || num_heads <= 0 ||
       num_blocks < 0 || block_size < 0)
     return cudaErrorInvalidValue;
-  const int nq = batch_size * num_heads;
-  const int splits = choose_splits(nq, num_blocks);
-  *bytes = splits > 1 ? (size_t)nq * splits * dense_rec_bytes(head_dim) : 16;
+  *bytes = 16;  // the split-KV merge runs in distributed shared memory: no workspace
   return cudaSuccess;
 }
 
@@ -306,24 +606,10 @@ cudaError_t int4kv_dense_decode(const float* query, const uint8_t* k_q, const fl
                                 int batch_size, int num_heads, int head_dim, int num_blocks,
                                 int block_size, float* output, void* workspace,
                                 size_t workspace_bytes, cudaStream_t stream) {
-  cudaError_t e = check(query, k_q, k_scale, k_zp, value, block_lens, batch_size, num_heads,
-                        head_dim, num_blocks, block_size, output);
-  if (e != cudaSuccess) return e;
-  const int nq = batch_size * num_heads;
-  const int splits = choose_splits(nq, num_blocks);
-  if (splits > 1) {
-    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
-        workspace_bytes < (size_t)nq * splits * dense_rec_bytes(head_dim))
-      return cudaErrorInvalidValue;
-  }
-  DenseArgs a{query, k_q, k_scale, k_zp, value, block_lens, nq, head_dim, num_blocks, block_size,
-              splits, output, static_cast<char*>(workspace), nullptr, num_blocks};
-  dense_decode_kernel<false, 0><<<dim3((nq + kQT - 1) / kQT, splits), kThreads, 0, stream>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess || splits == 1) return e;
-  dense_combine_kernel<<<nq, 128, 0, stream>>>(static_cast<const char*>(workspace), nq, head_dim,
-                                               splits, output);
-  return cudaGetLastError();
+  (void)workspace;
+  (void)workspace_bytes;
+  return cu_flash_decode_int4(query, k_q, k_scale, k_zp, value, block_lens, batch_size, num_heads,
+                              head_dim, num_blocks, block_size, output, stream);
 }
 
 cudaError_t int4kv_block_decode(const float* query, const uint8_t* k_packed, const float* k_scale,
@@ -332,34 +618,18 @@ cudaError_t int4kv_block_decode(const float* query, const uint8_t* k_packed, con
                                 int num_listed, int num_blocks, int batch_size, int num_heads,
                                 int head_dim, int block_size, float* output, void* workspace,
                                 size_t workspace_bytes, cudaStream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   if ((!block_ids && num_listed > 0) || num_blocks < 0) return cudaErrorInvalidValue;
-  cudaError_t e = check(query, k_packed, k_scale, k_zp, static_cast<const float*>(value),
-                        block_lens, batch_size, num_heads, head_dim, num_listed, block_size,
-                        output);
+  cudaError_t e = check(query, k_packed, k_scale, k_zp, value, block_lens, batch_size, num_heads,
+                        head_dim, num_listed, block_size, output);
   if (e != cudaSuccess) return e;
   if (value_dtype != INT4KV_VALUES_F32 && value_dtype != INT4KV_VALUES_F16 &&
       value_dtype != INT4KV_VALUES_BF16)
     return cudaErrorInvalidValue;
-  const int nq = batch_size * num_heads;
-  const int splits = choose_splits(nq, num_listed);
-  if (splits > 1) {
-    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
-        workspace_bytes < (size_t)nq * splits * dense_rec_bytes(head_dim))
-      return cudaErrorInvalidValue;
-  }
-  DenseArgs a{query, k_packed, k_scale, k_zp, value, block_lens, nq, head_dim, num_listed,
-              block_size, splits, output, static_cast<char*>(workspace), block_ids, num_blocks};
-  const dim3 grid((nq + kQT - 1) / kQT, splits);
-  switch (value_dtype) {
-    case INT4KV_VALUES_F32: dense_decode_kernel<true, 0><<<grid, kThreads, 0, stream>>>(a); break;
-    case INT4KV_VALUES_F16: dense_decode_kernel<true, 1><<<grid, kThreads, 0, stream>>>(a); break;
-    default: dense_decode_kernel<true, 2><<<grid, kThreads, 0, stream>>>(a); break;
-  }
-  e = cudaGetLastError();
-  if (e != cudaSuccess || splits == 1) return e;
-  dense_combine_kernel<<<nq, 128, 0, stream>>>(static_cast<const char*>(workspace), nq, head_dim,
-                                               splits, output);
-  return cudaGetLastError();
+  const DenseArgs a{query, k_packed, k_scale, k_zp, value, block_lens, block_ids,
+                    batch_size * num_heads, head_dim, num_listed, block_size, num_blocks, output};
+  return run(a, true, value_dtype, stream);
 }
 
 const char* int4kv_build_info(void) {

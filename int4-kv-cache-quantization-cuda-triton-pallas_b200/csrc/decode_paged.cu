@@ -245,16 +245,6 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
     bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * D, (uint32_t)a.gs * D * 4, bar);
 }
 
-// sum = sum*r + x with a running compensation term c (Kahan): the rescale
-// applies to both, the addition captures its own rounding error in c.
-__device__ __forceinline__ void kahan_rescale_add(float& sum, float& c, float r, float x) {
-  sum *= r;
-  c *= r;
-  const float y = __fsub_rn(x, c);
-  const float t = __fadd_rn(sum, y);
-  c = __fsub_rn(__fsub_rn(t, sum), y);
-  sum = t;
-}
 
 // Two 16-bit stored values (one 32-bit word, low half first) widened to
 // float32 exactly.
@@ -302,15 +292,6 @@ __device__ __forceinline__ void pv_row(const char* vs, float pt, int t, int lane
   }
 }
 
-// e^x for x <= 0 given in float64: 2^(x*log2(e)) with the hardware base-2
-// exponential (relative error ~2^-22, far inside the kernel's 1e-6 tolerance);
-// x = -inf gives exactly 0.
-__device__ __forceinline__ float exp_neg(double x) {
-  const float y = (float)(x * 1.4426950408889634);
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
 
 // Fused split exchange, push side: store this GPU's (m, l, acc) of query
 // stream qs into every rank's buffer (plain 16-byte stores through the peer

@@ -17,11 +17,14 @@
 //                            into their pages by the same CTA.
 //   grouped_quant_loop_kernel -- same contract for groups longer than 128 rows
 //                            (two passes; the second pass re-reads from L2).
-//   legacy_quant_kernel   -- the reference's cu_quantize_int4 contract: one group
-//                            = all rows, one value per byte. A thread-block cluster
-//                            splits the rows; partial min/max meet in distributed
-//                            shared memory, so no global scratch is needed.
-#include <cooperative_groups.h>
+//   legacy_*_kernel       -- the reference's cu_quantize_int4 contract: one group
+//                            = all rows, one value per byte. Four launches chained
+//                            by programmatic dependent launch, no scratch beyond the
+//                            outputs: the scale / zp outputs first hold the running
+//                            per-channel max / min as order-preserving integer keys
+//                            (atomic max / min from every row chunk), then the
+//                            codes are written from them, then they are replaced by
+//                            the final scale / zp.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -34,7 +37,6 @@
 #include "common.cuh"
 #include "../../include/int4kv_b200.h"
 
-namespace cg = cooperative_groups;
 using namespace i4kv;
 
 namespace {
@@ -669,84 +671,199 @@ grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, Out
 }
 
 // Reference contract (csrc/flash_decode_int4.cu:27-83 of the reference): one
-// group = all rows, one code per byte. Grid: x = 32-channel slabs, y = cluster
-// of `cl` CTAs splitting the rows. Partial min/max are exchanged through
-// distributed shared memory.
-constexpr int kLegacyWarps = 8;
-__global__ void __launch_bounds__(kLegacyWarps * 32)
-legacy_quant_kernel(const float* __restrict__ kv, int rows, int C, uint8_t* __restrict__ q_out,
-                    float* __restrict__ scale_out, float* __restrict__ zp_out) {
-  __shared__ float s_wmin[kLegacyWarps][32];
-  __shared__ float s_wmax[kLegacyWarps][32];
-  __shared__ float s_pmin[32];
-  __shared__ float s_pmax[32];
-  __shared__ float s_lo[32];
-  __shared__ float s_sc[32];
-  __shared__ float s_rc[32];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int cl = static_cast<int>(cluster.num_blocks());
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int c = blockIdx.x * 32 + lane;
-  const bool ok = c < C;
-  const int chunk = (rows + cl - 1) / cl;
-  const int rb = rank * chunk;
-  const int re = min(rows, rb + chunk);
+// group = all rows, one code per byte. The min / max over all rows is a
+// reduction across the whole grid, and the reference's launcher takes no
+// scratch buffer, so it is split at the one point where every CTA must have
+// contributed: kernel boundaries, whose launch gaps programmatic dependent
+// launch hides. Each CTA owns a chunk of rows of one 128-channel tile; a warp
+// reads whole 512-byte row pieces (float4 per lane) when the rows allow it.
+//   1. legacy_keys_init   : scale_out / zp_out <- the keys of -inf / +inf
+//   2. legacy_minmax      : per-CTA min / max of its chunk, then one atomicMax /
+//                           atomicMin of the order-preserving key per channel
+//   3. legacy_codes       : codes of the chunk from the final min / max (the
+//                           chunk is read again, from L2 when it fits there)
+//   4. legacy_params      : scale_out / zp_out <- scale, zp of each channel
+// Steps 2-4 call grid_dependency_wait() before they touch what the step before
+// wrote, so starting early never changes a result.
+constexpr int kLegWarps = 8;
+constexpr int kLegTile = 128;  // channels per CTA (32 lanes x 4)
 
-  float lo = INFINITY, hi = -INFINITY;
-  if (ok) {
-    int r = rb + warp;
-    for (; r + 3 * kLegacyWarps < re; r += 4 * kLegacyWarps) {
-      const float a = __ldg(kv + (size_t)r * C + c);
-      const float b = __ldg(kv + (size_t)(r + kLegacyWarps) * C + c);
-      const float d = __ldg(kv + (size_t)(r + 2 * kLegacyWarps) * C + c);
-      const float e = __ldg(kv + (size_t)(r + 3 * kLegacyWarps) * C + c);
-      lo = fminf(fminf(lo, a), fminf(b, fminf(d, e)));
-      hi = fmaxf(fmaxf(hi, a), fmaxf(b, fmaxf(d, e)));
+__global__ void __launch_bounds__(256)
+legacy_keys_init(float* __restrict__ scale_out, float* __restrict__ zp_out, int C) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < C) {
+    reinterpret_cast<uint32_t*>(scale_out)[c] = 0u;           // below the key of any float
+    reinterpret_cast<uint32_t*>(zp_out)[c] = 0xffffffffu;     // above the key of any float
+  }
+  allow_dependent_launch();
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kLegWarps * 32)
+legacy_minmax(const float* __restrict__ kv, int rows, int C, int chunk,
+              float* __restrict__ scale_out, float* __restrict__ zp_out) {
+  __shared__ float s_lo[kLegWarps][kLegTile];
+  __shared__ float s_hi[kLegWarps][kLegTile];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.y * kLegTile;
+  const int r0 = blockIdx.x * chunk;
+  const int r1 = min(rows, r0 + chunk);
+  float lo[4], hi[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) lo[k] = INFINITY, hi[k] = -INFINITY;
+  if constexpr (VEC) {
+    const int c = c0 + 4 * lane;
+    if (c < C) {
+      const float* p = kv + (size_t)r0 * C + c;
+      int r = r0 + warp;
+      for (; r + kLegWarps < r1; r += 2 * kLegWarps) {  // two rows in flight per warp
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0) * C));
+        const float4 b =
+            __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0 + kLegWarps) * C));
+        lo[0] = fmin3f(lo[0], a.x, b.x); hi[0] = fmax3f(hi[0], a.x, b.x);
+        lo[1] = fmin3f(lo[1], a.y, b.y); hi[1] = fmax3f(hi[1], a.y, b.y);
+        lo[2] = fmin3f(lo[2], a.z, b.z); hi[2] = fmax3f(hi[2], a.z, b.z);
+        lo[3] = fmin3f(lo[3], a.w, b.w); hi[3] = fmax3f(hi[3], a.w, b.w);
+      }
+      if (r < r1) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0) * C));
+        lo[0] = fminf(lo[0], a.x); hi[0] = fmaxf(hi[0], a.x);
+        lo[1] = fminf(lo[1], a.y); hi[1] = fmaxf(hi[1], a.y);
+        lo[2] = fminf(lo[2], a.z); hi[2] = fmaxf(hi[2], a.z);
+        lo[3] = fminf(lo[3], a.w); hi[3] = fmaxf(hi[3], a.w);
+      }
     }
-    for (; r < re; r += kLegacyWarps) {
-      const float a = __ldg(kv + (size_t)r * C + c);
-      lo = fminf(lo, a);
-      hi = fmaxf(hi, a);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      s_lo[warp][4 * lane + k] = lo[k];
+      s_hi[warp][4 * lane + k] = hi[k];
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + lane + 32 * k;
+      if (c < C) {
+        for (int r = r0 + warp; r < r1; r += kLegWarps) {
+          const float a = __ldg(kv + (size_t)r * C + c);
+          lo[k] = fminf(lo[k], a);
+          hi[k] = fmaxf(hi[k], a);
+        }
+      }
+      s_lo[warp][lane + 32 * k] = lo[k];
+      s_hi[warp][lane + 32 * k] = hi[k];
     }
   }
-  s_wmin[warp][lane] = lo;
-  s_wmax[warp][lane] = hi;
+  allow_dependent_launch();
   __syncthreads();
-  if (warp == 0) {
-    for (int w = 1; w < kLegacyWarps; ++w) {
-      lo = fminf(lo, s_wmin[w][lane]);
-      hi = fmaxf(hi, s_wmax[w][lane]);
+  const int t = threadIdx.x;
+  if (t < kLegTile && c0 + t < C) {
+    float l = s_lo[0][t], h = s_hi[0][t];
+#pragma unroll
+    for (int w = 1; w < kLegWarps; ++w) {
+      l = fminf(l, s_lo[w][t]);
+      h = fmaxf(h, s_hi[w][t]);
     }
-    s_pmin[lane] = lo;
-    s_pmax[lane] = hi;
+    grid_dependency_wait();  // the keys were initialised by the previous launch
+    if (h >= l) {            // a chunk with no rows (or only NaN) leaves the keys alone
+      atomicMax(reinterpret_cast<unsigned int*>(scale_out) + c0 + t, ordered_key(h));
+      atomicMin(reinterpret_cast<unsigned int*>(zp_out) + c0 + t, ordered_key(l));
+    }
   }
-  cluster.sync();
-  if (warp == 0) {
-    float glo = INFINITY, ghi = -INFINITY;
-    for (int k = 0; k < cl; ++k) {
-      const float* pmin = cluster.map_shared_rank(s_pmin, k);
-      const float* pmax = cluster.map_shared_rank(s_pmax, k);
-      glo = fminf(glo, pmin[lane]);
-      ghi = fmaxf(ghi, pmax[lane]);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kLegWarps * 32)
+legacy_codes(const float* __restrict__ kv, int rows, int C, int chunk,
+             const float* __restrict__ max_keys, const float* __restrict__ min_keys,
+             uint8_t* __restrict__ q_out) {
+  __shared__ __align__(16) float s_mn[kLegTile];
+  __shared__ __align__(16) float s_sc[kLegTile];
+  __shared__ __align__(16) float s_rc[kLegTile];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.y * kLegTile;
+  const int r0 = blockIdx.x * chunk;
+  const int r1 = min(rows, r0 + chunk);
+  const int t = threadIdx.x;
+  grid_dependency_wait();  // every chunk's min / max has landed in the keys
+  if (t < kLegTile) {
+    float mn = 0.f, sc = 1.f;
+    if (c0 + t < C) {
+      mn = from_ordered_key(reinterpret_cast<const uint32_t*>(min_keys)[c0 + t]);
+      const float mx = from_ordered_key(reinterpret_cast<const uint32_t*>(max_keys)[c0 + t]);
+      float zp;
+      channel_params(mn, mx, &sc, &zp);
     }
+    s_mn[t] = mn;
+    s_sc[t] = sc;
+    s_rc[t] = __frcp_rn(sc);
+  }
+  __syncthreads();
+  allow_dependent_launch();
+  if constexpr (VEC) {
+    const int c = c0 + 4 * lane;
+    if (c >= C) return;
+    const float4 mn = reinterpret_cast<const float4*>(s_mn)[lane];
+    const float4 sc = reinterpret_cast<const float4*>(s_sc)[lane];
+    const float4 rc = reinterpret_cast<const float4*>(s_rc)[lane];
+    for (int r = r0 + warp; r < r1; r += kLegWarps) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(kv + (size_t)r * C + c));
+      *reinterpret_cast<uint32_t*>(q_out + (size_t)r * C + c) = codes4_rcp(v, mn, sc, rc);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + lane + 32 * k;
+      if (c >= C) continue;
+      const float mn = s_mn[lane + 32 * k], sc = s_sc[lane + 32 * k], rc = s_rc[lane + 32 * k];
+      for (int r = r0 + warp; r < r1; r += kLegWarps)
+        q_out[(size_t)r * C + c] =
+            static_cast<uint8_t>(quant_code_rcp(__ldg(kv + (size_t)r * C + c), mn, sc, rc));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256)
+legacy_params(float* __restrict__ scale_out, float* __restrict__ zp_out, int C) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  grid_dependency_wait();  // every CTA of the codes step has read the keys
+  if (c < C) {
+    const float mx = from_ordered_key(reinterpret_cast<const uint32_t*>(scale_out)[c]);
+    const float mn = from_ordered_key(reinterpret_cast<const uint32_t*>(zp_out)[c]);
     float s, z;
-    channel_params(glo, ghi, &s, &z);
-    s_lo[lane] = glo;
-    s_sc[lane] = s;
-    s_rc[lane] = __frcp_rn(s);
-    if (rank == 0 && ok) {
-      scale_out[c] = s;
-      zp_out[c] = z;
-    }
+    channel_params(mn, mx, &s, &z);
+    scale_out[c] = s;
+    zp_out[c] = z;
   }
-  cluster.sync();  // peers are done reading this CTA's partials; s_lo/s_sc visible
-  if (!ok) return;
-  const float mn = s_lo[lane], sc = s_sc[lane], rc = s_rc[lane];
-  for (int r = rb + warp; r < re; r += kLegacyWarps) {
-    q_out[(size_t)r * C + c] =
-        static_cast<uint8_t>(quant_code_rcp(__ldg(kv + (size_t)r * C + c), mn, sc, rc));
-  }
+}
+
+int device_sms() {
+  static std::mutex mu;
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms[dev] = 148;
+  return sms[dev];
+}
+
+// Launch `kern` with the programmatic-serialization attribute: it may begin
+// while the previous kernel on `stream` is still running (it waits for that
+// kernel's results with grid_dependency_wait()).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -813,22 +930,34 @@ cudaError_t cu_quantize_int4(const float* kv, int num_rows, int num_channels, ui
                              float* scale_out, float* zp_out, cudaStream_t stream) {
   if (num_rows <= 0 || num_channels <= 0) return cudaErrorInvalidValue;
   if (!kv || !q_out || !scale_out || !zp_out) return cudaErrorInvalidValue;
-  const int cl = num_rows >= 8 * 256 ? 8 : (num_rows + 255) / 256;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((num_channels + 31) / 32, cl, 1);
-  cfg.blockDim = dim3(kLegacyWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = cl;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, legacy_quant_kernel, kv, num_rows, num_channels, q_out,
-                                       scale_out, zp_out);
-  if (err != cudaSuccess) return err;
+  const int C = num_channels;
+  const int tiles = (C + kLegTile - 1) / kLegTile;
+  // about two CTAs per SM in all; at least 8 rows (one per warp) per chunk
+  int chunks = (2 * device_sms() + tiles - 1) / tiles;
+  chunks = min(chunks, (num_rows + kLegWarps - 1) / kLegWarps);
+  chunks = max(chunks, 1);
+  const int chunk = (num_rows + chunks - 1) / chunks;
+  chunks = (num_rows + chunk - 1) / chunk;
+  const bool vec = C % 4 == 0 && aligned16(kv) && (reinterpret_cast<uintptr_t>(q_out) & 3u) == 0;
+  const dim3 grid(chunks, tiles), block(kLegWarps * 32);
+  const dim3 pgrid((C + 255) / 256), pblock(256);
+  legacy_keys_init<<<pgrid, pblock, 0, stream>>>(scale_out, zp_out, C);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = vec ? launch_pdl(legacy_minmax<true>, grid, block, stream, kv, num_rows, C, chunk,
+                       scale_out, zp_out)
+          : launch_pdl(legacy_minmax<false>, grid, block, stream, kv, num_rows, C, chunk,
+                       scale_out, zp_out);
+  if (e != cudaSuccess) return e;
+  e = vec ? launch_pdl(legacy_codes<true>, grid, block, stream, kv, num_rows, C, chunk,
+                       static_cast<const float*>(scale_out), static_cast<const float*>(zp_out),
+                       q_out)
+          : launch_pdl(legacy_codes<false>, grid, block, stream, kv, num_rows, C, chunk,
+                       static_cast<const float*>(scale_out), static_cast<const float*>(zp_out),
+                       q_out);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(legacy_params, pgrid, pblock, stream, scale_out, zp_out, C);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -46,10 +46,29 @@ def test_legacy_quantizer_golden(name):
 
 
 @pytest.mark.parametrize("shape", [(1, 1), (1, 64), (255, 3), (256, 3), (257, 3), (1030, 8),
-                                   (4096, 128), (32768, 128), (5000, 37)])
+                                   (4096, 128), (32768, 128), (5000, 37), (7, 4097), (3, 300),
+                                   (2049, 129), (100003, 3), (9, 512), (65536, 256)])
 def test_legacy_quantizer_shapes(shape):
     kv = np.random.RandomState(shape[0]).randn(*shape).astype(np.float32)
     assert_same(ops.quantize_int4(kv, backend="cuda"), oracle.quantize_int4(kv))
+
+
+def test_legacy_quantizer_twice_in_a_row_and_misaligned_rows():
+    """The scale / zp outputs double as the running min / max keys during a
+    call: a second call on the same outputs, and a call on an input whose rows
+    start 4 bytes off a 16-byte boundary (the scalar-load path), both still
+    match the oracle bit for bit."""
+    kv = np.random.RandomState(3).randn(3001, 128).astype(np.float32) * 3 + 1
+    t = torch.from_numpy(kv).cuda()
+    first = C.quantize_int4(t)
+    second = C.quantize_int4(t)
+    ref = oracle.quantize_int4(kv)
+    for got in (first, second):
+        assert_same([x.cpu().numpy() for x in got], ref)
+    buf = torch.empty((kv.size + 1,), dtype=torch.float32, device="cuda")
+    view = buf[1:].view(kv.shape)  # 4-byte offset: not 16-byte aligned
+    view.copy_(t)
+    assert_same([x.cpu().numpy() for x in C.quantize_int4(view)], ref)
 
 
 def test_legacy_quantizer_anchor_distribution():
