@@ -138,12 +138,12 @@ struct Chunk {
 
 // The next non-empty chunk at or after tile `cur` (tiles of 16 rows, tpp per
 // page) and before `end`; advances `cur` past it. Uniform across the CTA.
-__device__ __forceinline__ bool next_chunk(const DenseArgs& a, int tpp, long long& cur,
-                                           long long end, Chunk& c) {
+__device__ __forceinline__ bool next_chunk(const DenseArgs& a, int tpp, int& cur, int end,
+                                           Chunk& c) {
   while (cur < end) {
-    const int pi = (int)(cur / tpp);
-    const int i = (int)(cur - (long long)pi * tpp);
-    const int nt = (int)min((long long)min(4, tpp - i), end - cur);
+    const int pi = cur / tpp;
+    const int i = cur - pi * tpp;
+    const int nt = min(min(4, tpp - i), end - cur);
     cur += nt;
     const int pg = a.ids ? __ldg(a.ids + pi) : pi;
     if (pg < 0 || pg >= a.num_blocks) continue;  // unknown block id: skipped, never read
@@ -169,7 +169,17 @@ __device__ __forceinline__ void load_chunk(const DenseArgs& a, const Chunk& c, c
   const uint8_t* gk = a.kq + ((size_t)c.pg * a.bs + c.row0) * RB;
   const char* gv = static_cast<const char*>(a.v) + ((size_t)c.pg * a.bs + c.row0) * a.D * Cf::VB;
   const int vrow = a.D * Cf::VB;
-  if (aligned) {
+  if (aligned && a.D == DP) {  // full rows: 16-byte pieces per row known at compile time
+    constexpr int KP = (PACKED ? DP / 2 : DP) / 16, VP = DP * Cf::VB / 16;
+    for (int i = threadIdx.x; i < c.rows * KP; i += kThreads) {
+      const int r = i / KP, j = i - r * KP;
+      cp_async16(sk + r * Cf::KROW + 16 * j, gk + (size_t)r * (KP * 16) + 16 * j);
+    }
+    for (int i = threadIdx.x; i < c.rows * VP; i += kThreads) {
+      const int r = i / VP, j = i - r * VP;
+      cp_async16(sv + (size_t)r * DP * Cf::VB + 16 * j, gv + (size_t)r * (VP * 16) + 16 * j);
+    }
+  } else if (aligned) {
     const int kp = RB / 16, vp = vrow / 16;
     for (int i = threadIdx.x; i < c.rows * kp; i += kThreads) {
       const int r = i / kp, j = i - r * kp;
@@ -300,9 +310,9 @@ shared_stream_decode_kernel(DenseArgs a) {
 
   // this CTA's contiguous range of 16-row tiles of the stream
   const int tpp = (a.bs + 15) / 16;
-  const long long total = (long long)a.np * tpp;
-  long long cur = total * rank / S;
-  const long long end = total * (rank + 1) / S;
+  const int total = a.np * tpp;  // < 2^31 (checked on the host)
+  int cur = (int)((long long)total * rank / S);
+  const int end = (int)((long long)total * (rank + 1) / S);
   const int RB = PACKED ? (a.D + 1) / 2 : a.D;
   const bool aligned = (RB % 16 == 0) && ((a.D * Cf::VB) % 16 == 0) &&
                        ((reinterpret_cast<uintptr_t>(a.kq) | reinterpret_cast<uintptr_t>(a.v)) & 15u) == 0;
@@ -440,13 +450,13 @@ shared_stream_decode_kernel(DenseArgs a) {
       const float* pb = pa + Cf::PROW;
       float ch[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll 4
-      for (int r = 0; r < c.rows; ++r) {
+      for (int r = 0; r < c.rows; ++r) {  // paired FMAs: bit-identical to fmaf per lane
         const float4 v4 = load_v4<VK>(vp + (size_t)r * DP * Cf::VB);
         const float x = pa[r], y = pb[r];
-        ch[0][0] = fmaf(x, v4.x, ch[0][0]); ch[0][1] = fmaf(x, v4.y, ch[0][1]);
-        ch[0][2] = fmaf(x, v4.z, ch[0][2]); ch[0][3] = fmaf(x, v4.w, ch[0][3]);
-        ch[1][0] = fmaf(y, v4.x, ch[1][0]); ch[1][1] = fmaf(y, v4.y, ch[1][1]);
-        ch[1][2] = fmaf(y, v4.z, ch[1][2]); ch[1][3] = fmaf(y, v4.w, ch[1][3]);
+        fma2_rn(ch[0][0], ch[0][1], v4.x, v4.y, x);
+        fma2_rn(ch[0][2], ch[0][3], v4.z, v4.w, x);
+        fma2_rn(ch[1][0], ch[1][1], v4.x, v4.y, y);
+        fma2_rn(ch[1][2], ch[1][3], v4.z, v4.w, y);
       }
       const float ca = s_corr[2 * qp], cb = s_corr[2 * qp + 1];
 #pragma unroll
@@ -564,6 +574,7 @@ cudaError_t check(const float* query, const uint8_t* k_q, const float* k_scale, 
 }
 
 cudaError_t run(const DenseArgs& a, bool packed, int value_dtype, cudaStream_t stream) {
+  if ((long long)a.np * ((a.bs + 15) / 16) >= (1LL << 31)) return cudaErrorInvalidValue;
   if (a.np == 0 || a.bs == 0) {  // an empty stream: every output is 0 (reference: o / max(0, 1e-10))
     const cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)a.nq * a.D * sizeof(float), stream);
     return e != cudaSuccess ? e : cudaGetLastError();

@@ -119,8 +119,9 @@ struct DecodeArgs {
   char* part_out;  // nullable: write per-stream partial records instead of outputs
   int kv_heads;    // heads of the pools; `heads` (query heads, one stream each) is a
   int group_q;     // multiple: query head h reads kv head h / group_q (GQA)
-  int gs;          // warps sharing one ring (query heads served per staged page)
-  int vheads;      // heads / gs: the page streams of the work decomposition
+  int gs;          // warps sharing one ring
+  int hw;          // query heads per warp (the kernel's HW); gs * hw heads share a staged page
+  int vheads;      // heads / (gs * hw): the page streams of the work decomposition
   // Fused sequence-split exchange (xworld > 0): every stream's GPU-local
   // (m, l, acc) goes to every rank's exchange buffer, and the final output is
   // the merge of all ranks' records. xbuf[r] = rank r's buffer as mapped here.
@@ -204,7 +205,7 @@ __device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx,
   d.phys = phys;
   d.gphys = gphys;
   d.meta = ((gok && pok) ? ntok : 0) | (first ? (1 << 8) : 0) | ((grp && gok) ? (1 << 9) : 0) |
-           (((h * a.gs) / a.group_q) << 16);
+           (((h * a.gs * a.hw) / a.group_q) << 16);
   d.stream = b * a.vheads + h;
   return d;
 }
@@ -228,7 +229,7 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
   uint32_t bytes = 0;
   if (ntok) bytes += (uint32_t)ntok * (D * C::VB + D / 2);
   if (has_sz) bytes += 2 * D * 4;
-  if (has_q) bytes += (uint32_t)a.gs * D * 4;
+  if (has_q) bytes += (uint32_t)a.gs * a.hw * D * 4;
   fence_proxy_async_smem();
   mbar_arrive_expect_tx(bar, bytes);
   if (ntok) {
@@ -242,7 +243,8 @@ __device__ __forceinline__ void issue_page(const DecodeArgs& a, const Desc& d, c
              a.sz_pool + ((size_t)d.gphys * a.kv_heads + kvh) * 2 * D, 2 * D * 4, bar);
   }
   if (has_q)
-    bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * D, (uint32_t)a.gs * D * 4, bar);
+    bulk_g2s(slot + C::Q_OFF, a.q + (size_t)d.stream * a.gs * a.hw * D,
+             (uint32_t)a.gs * a.hw * D * 4, bar);
 }
 
 
@@ -292,6 +294,56 @@ __device__ __forceinline__ void pv_row(const char* vs, float pt, int t, int lane
   }
 }
 
+
+// ps[h] += pt[h] * V[t, lane's dims] for the HW heads of a warp: the value row
+// is loaded (and 16-bit values widened) once for all heads.
+template <int D, int VK, int HW>
+__device__ __forceinline__ void pv_row_heads(const char* vs, const float* pt_row, int t, int lane,
+                                             float (&ps)[HW][D / 32]) {
+  constexpr int DPL = D / 32;
+  float pt[HW];
+  if constexpr (HW == 4) {
+    const float4 x = *reinterpret_cast<const float4*>(pt_row);
+    pt[0] = x.x; pt[1] = x.y; pt[2] = x.z; pt[3] = x.w;
+  } else if constexpr (HW == 2) {
+    const float2 x = *reinterpret_cast<const float2*>(pt_row);
+    pt[0] = x.x; pt[1] = x.y;
+  } else {
+#pragma unroll
+    for (int h = 0; h < HW; ++h) pt[h] = pt_row[h];
+  }
+  float v[DPL];
+  if constexpr (VK == 0) {
+    const float* row = reinterpret_cast<const float*>(vs) + t * D;
+    if constexpr (DPL == 2) {
+      const float2 x = *reinterpret_cast<const float2*>(row + 2 * lane);
+      v[0] = x.x; v[1] = x.y;
+    } else {
+#pragma unroll
+      for (int v4 = 0; v4 < DPL / 4; ++v4) {
+        const float4 x = *reinterpret_cast<const float4*>(row + v4 * 128 + 4 * lane);
+        v[4 * v4] = x.x; v[4 * v4 + 1] = x.y; v[4 * v4 + 2] = x.z; v[4 * v4 + 3] = x.w;
+      }
+    }
+  } else {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(vs) + t * D;
+    if constexpr (DPL == 2) {
+      const float2 x = widen2<VK>(*reinterpret_cast<const uint32_t*>(row + 2 * lane));
+      v[0] = x.x; v[1] = x.y;
+    } else {
+#pragma unroll
+      for (int v4 = 0; v4 < DPL / 4; ++v4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(row + v4 * 128 + 4 * lane);
+        const float2 lo = widen2<VK>(w.x), hi = widen2<VK>(w.y);
+        v[4 * v4] = lo.x; v[4 * v4 + 1] = lo.y; v[4 * v4 + 2] = hi.x; v[4 * v4 + 3] = hi.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HW; ++h)
+#pragma unroll
+    for (int k = 0; k < DPL; k += 2) fma2_rn(ps[h][k], ps[h][k + 1], v[k], v[k + 1], pt[h]);
+}
 
 // Fused split exchange, push side: store this GPU's (m, l, acc) of query
 // stream qs into every rank's buffer (plain 16-byte stores through the peer
@@ -414,8 +466,18 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
 // shared memory; registers are capped at 128 so that four could be resident,
 // but the grid launches three per SM (I4KV_DECODE_MAX_CTAS_16: measured 45.5
 // us at config 0 against 46.5 with four and 53.5 with two).
-template <int D, int WARPS, int STAGES, int VK>
-__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? 1 : 4)
+//
+// HW = query heads per warp (grouped-query attention, HW in {1, 2, 4}): one
+// warp serves HW consecutive query heads of every kv page it takes. With
+// HW > 1 the heads sit in the MMA's columns: pass p's eight B columns are
+// (head, digit) pairs -- for HW = 4, columns 2t and 2t + 1 are digits 2p and
+// 2p + 1 of head t -- so after HW passes lane (g, t) holds head t's logits of
+// tokens g and g + 8 without any cross-lane sum, and the softmax of the HW
+// heads runs side by side across the lanes (lane t owns head t * HW / 4). The
+// page's codes are loaded into A fragments once and each value row once for all
+// heads. HW = 1 is plain one-head-per-warp decoding.
+template <int D, int WARPS, int STAGES, int VK, int HW>
+__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? 1 : (HW > 1 ? 3 : 4))
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
@@ -427,16 +489,17 @@ paged_decode_kernel(DecodeArgs a) {
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int fg = lane >> 2, ft = lane & 3;  // mma fragment row group / thread in group
+  const int hl = (ft * HW) / 4;              // HW > 1: the head whose softmax this lane runs
   // Ring groups: gs warps share one ring of STAGES * gs slots; warp gj of the
-  // group serves query head vh * gs + gj of every page the group stages
-  // (gs = 1 without GQA: one warp, one ring, one query).
+  // group serves query heads (vh * gs + gj) * HW + k, k < HW, of every page the
+  // group stages (gs = 1, HW = 1 without GQA: one warp, one ring, one query).
   const int gs = a.gs, gpc = WARPS / gs;
   const int gi = warp / gs, gj = warp - gi * gs;
   // slots per ring: STAGES pages per warp alone; a ring group keeps gs pages
   // in flight (its queries share each page, so it needs fewer bytes in flight
   // and fits more CTAs per SM)
   const int depth = gs == 1 ? STAGES : gs;
-  const int sb = C::Q_OFF + gs * D * 4;  // stage bytes with gs queries
+  const int sb = C::Q_OFF + gs * HW * D * 4;  // stage bytes with gs * HW queries
   const bool leader = gj == 0;
   {  // the block table into L2 while the lengths load (first descriptors hit L2)
     const size_t bt_bytes = (size_t)a.batch * a.max_pages * 4;
@@ -469,7 +532,7 @@ paged_decode_kernel(DecodeArgs a) {
   const long long gw = (long long)blockIdx.x * gpc + gi;
   const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
   const int n = g1 - g0;
-  const bool xmode = a.xworld > 0;
+  const bool xmode = HW == 1 && a.xworld > 0;  // the fused split runs one head per warp
   if (n <= 0) {
     if (xmode) {  // no pages here, but maybe empty streams to exchange
       bool dead = false;
@@ -484,11 +547,11 @@ paged_decode_kernel(DecodeArgs a) {
   // this warp's digit staging bytes (4 rows of D + 32: the padding puts the
   // four rows a round reads in different banks), dig[g * (D + 32) + c]
   // = digit g (mod 4) of channel c; the page's softmax weights reuse its
-  // first 64 bytes between group changes
+  // first 64 * HW bytes between group changes
   constexpr int kDigRow = D + 32;
   uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)gpc * depth * sb +
                                             (size_t)warp * 4 * kDigRow);
-  float* p_tab = reinterpret_cast<float*>(dig);
+  float* p_tab = reinterpret_cast<float*>(dig);  // [16 tokens][HW heads]
   if (leader && lane == 0) {
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
@@ -511,22 +574,28 @@ paged_decode_kernel(DecodeArgs a) {
   // of code x digit p for the two digits p = 2t, 2t+1 of this lane, and
   // float64 weights 2^(E - 7 - 7p) recombine them. Truncation is below
   // 2^(E-56) per channel, as fine as float64 accumulation.
-  uint32_t bfrag[2 * C::KT][2];  // mma B operands: [2e + parity][half] of k-tile e
-  float qv[DPL];                 // this warp's query at channels lane * DPL + j
-  double w0 = 0.0, w1 = 0.0;     // weights of digits 2ft and 2ft + 1
-  double bias = 0.0;
+  uint32_t bfrag[HW][2 * C::KT][2];  // mma B operands: [head][2e + parity][half] of k-tile e
+  float qv[HW][DPL];                 // the warp's queries at channels lane * DPL + j
+  double w0[HW], w1[HW];             // weights of digits 2ft and 2ft + 1
+  double bias[HW];
   // Value and denominator sums: float32 with a Kahan compensation term, so
   // long page runs accumulate without float64 conversions on the hot path.
-  float acc[DPL], acc_c[DPL];
-  float l_lane = 0.f, l_c = 0.f;
-  double m_run = -INFINITY;
+  float acc[HW][DPL], acc_c[HW][DPL];
+  float l_lane[HW], l_c[HW];
+  double m_run[HW];
   int seg_stream = -1;
   bool aborted = false;
   int abort_at = 0;
 #pragma unroll
-  for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; qv[k] = 0.f; }
+  for (int h = 0; h < HW; ++h) {
+    w0[h] = w1[h] = bias[h] = 0.0;
+    l_lane[h] = l_c[h] = 0.f;
+    m_run[h] = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < 2 * C::KT; ++k) { bfrag[k][0] = 0u; bfrag[k][1] = 0u; }
+    for (int k = 0; k < DPL; ++k) { acc[h][k] = 0.f; acc_c[h][k] = 0.f; qv[h][k] = 0.f; }
+#pragma unroll
+    for (int k = 0; k < 2 * C::KT; ++k) { bfrag[h][k][0] = 0u; bfrag[h][k][1] = 0u; }
+  }
 
   int xm0 = -1, xm1 = -1;  // exchange mode: streams this warp merged locally (at most 2)
   int* counters = reinterpret_cast<int*>(a.ws);
@@ -543,9 +612,9 @@ paged_decode_kernel(DecodeArgs a) {
     return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
   };
 
-  // Warp-wide sum of the lanes' denominators (float32 sum minus compensation).
-  auto lane_sum = [&]() -> double {
-    double lsum = (double)l_lane - (double)l_c;
+  // Warp-wide sum of head h's lane denominators (float32 sum minus compensation).
+  auto lane_sum = [&](int h) -> double {
+    double lsum = (double)l_lane[h] - (double)l_c[h];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(kFull, lsum, o);
     return lsum;
@@ -559,23 +628,47 @@ paged_decode_kernel(DecodeArgs a) {
     store_lane_vec<D>(reinterpret_cast<float*>(rec + 16), o, lane);
   };
 
-  // A stream this warp covered alone: write its output (or, in partial mode,
-  // its record) straight from the running state.
-  auto finish_alone = [&](int stream) {
-    const size_t qstream = (size_t)stream * gs + gj;
-    const double lsum = lane_sum();
-    float o[DPL];
-    if (a.part_out || xmode) {
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-      if (xmode) x_push<D>(a, streams, (long long)qstream, m_run, lsum, o, lane);
-      else put_record(a.part_out + qstream * C::REC_BYTES, m_run, lsum, o);
-      return;
+  // Per-head running max and denominator. HW = 1: the warp's own state. HW > 1:
+  // lane (g, t) keeps the state of head t * HW / 4 in m_run[0] / l_lane[0]
+  // (for HW = 2 the odd lanes t duplicate the even ones and add nothing).
+  auto head_src = [&](int h) -> int { return (h * 4) / HW; };  // lane (0, t) of head h
+  auto head_m = [&](int h) -> double {
+    if constexpr (HW == 1) return m_run[h];
+    else return __shfl_sync(kFull, m_run[0], head_src(h));
+  };
+  auto head_l = [&](int h) -> double {
+    if constexpr (HW == 1) {
+      return lane_sum(h);
+    } else {
+      double x = (HW == 2 && (ft & 1)) ? 0.0 : (double)l_lane[0] - (double)l_c[0];
+      x += __shfl_xor_sync(kFull, x, 4);
+      x += __shfl_xor_sync(kFull, x, 8);
+      x += __shfl_xor_sync(kFull, x, 16);
+      return __shfl_sync(kFull, x, head_src(h));
     }
-    const double den = fmax(lsum, 1e-10);
+  };
+
+  // A stream this warp covered alone: write its outputs (or, in partial mode,
+  // its records) straight from the running state, head by head.
+  auto finish_alone = [&](int stream) {
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[k] - (double)acc_c[k]) / den);
-    store_lane_vec<D>(a.out + qstream * D, o, lane);
+    for (int h = 0; h < HW; ++h) {
+      const size_t qstream = ((size_t)stream * gs + gj) * HW + h;
+      const double lsum = head_l(h);
+      const double mh = head_m(h);
+      float o[DPL];
+      if (a.part_out || xmode) {
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
+        if (xmode) x_push<D>(a, streams, (long long)qstream, mh, lsum, o, lane);
+        else put_record(a.part_out + qstream * C::REC_BYTES, mh, lsum, o);
+        continue;
+      }
+      const double den = fmax(lsum, 1e-10);
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[h][k] - (double)acc_c[h][k]) / den);
+      store_lane_vec<D>(a.out + qstream * D, o, lane);
+    }
   };
 
   // Merge every contributor's record of `stream` (this warp arrived last) and
@@ -587,6 +680,8 @@ paged_decode_kernel(DecodeArgs a) {
   auto merge_stream = [&](int stream, long long w_lo, long long w_hi) {
     constexpr int CH = 32 / DPL;   // records per chunk (registers: CH * DPL floats)
     const bool all_run = T >= NW;  // then every warp in [w_lo, w_hi] wrote a record
+#pragma unroll 1
+    for (int h = 0; h < HW; ++h) {
     double M = -INFINITY, L = 0.0, O[DPL];
 #pragma unroll
     for (int k = 0; k < DPL; ++k) O[k] = 0.0;
@@ -596,7 +691,7 @@ paged_decode_kernel(DecodeArgs a) {
       const bool okj = lane < cnt && (all_run || (wj * T) / NW != ((wj + 1) * T) / NW);
       double mj = -INFINITY, lj = 0.0;
       if (okj) {
-        const char* r = recs + ((size_t)(wj + stream) * gs + gj) * C::REC_BYTES;
+        const char* r = recs + (((size_t)(wj + stream) * gs + gj) * HW + h) * C::REC_BYTES;
         mj = __ldcg(reinterpret_cast<const double*>(r));
         lj = __ldcg(reinterpret_cast<const double*>(r + 8));
       }
@@ -605,7 +700,7 @@ paged_decode_kernel(DecodeArgs a) {
       for (int j = 0; j < CH; ++j) {
         if (j < cnt) {
           load_lane_vec_cg<D>(reinterpret_cast<const float*>(
-              recs + ((size_t)(base + j + stream) * gs + gj) * C::REC_BYTES + 16), v[j], lane);
+              recs + (((size_t)(base + j + stream) * gs + gj) * HW + h) * C::REC_BYTES + 16), v[j], lane);
         }
       }
       double cm = mj;
@@ -632,7 +727,7 @@ paged_decode_kernel(DecodeArgs a) {
       }
       M = m_new;
     }
-    const size_t qstream = (size_t)stream * gs + gj;
+    const size_t qstream = ((size_t)stream * gs + gj) * HW + h;
     float o[DPL];
     if (a.part_out || xmode) {  // the merged (M, L, O) of this GPU's share of the stream
 #pragma unroll
@@ -643,18 +738,20 @@ paged_decode_kernel(DecodeArgs a) {
       } else {
         put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
       }
-      return;
+      continue;
     }
     const double den = fmax(L, 1e-10);
 #pragma unroll
     for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
     store_lane_vec<D>(a.out + qstream * D, o, lane);
+    }
   };
 
   // The warp's first segment, when its stream is shared with earlier warps and
-  // ends inside this run: its record is held in registers and published with
-  // the last segment's at the end of the run, so the run never stalls on a
-  // fence or an atomic in the middle.
+  // ends inside this run: its record is held in registers (HW = 1) or stored
+  // to its slot at once (HW > 1, plain stores) and published with the last
+  // segment's at the end of the run, so the run never stalls on a fence or an
+  // atomic in the middle.
   int held_stream = -1;
   double held_m = 0.0, held_l = 0.0;
   float held_o[DPL];
@@ -668,10 +765,21 @@ paged_decode_kernel(DecodeArgs a) {
       return;
     }
     held_stream = stream;  // only the run's first segment can get here mid-run
-    held_m = m_run;
-    held_l = lane_sum();
+    if constexpr (HW == 1) {
+      held_m = m_run[0];
+      held_l = lane_sum(0);
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) held_o[k] = (float)((double)acc[k] - (double)acc_c[k]);
+      for (int k = 0; k < DPL; ++k) held_o[k] = (float)((double)acc[0][k] - (double)acc_c[0][k]);
+    } else {
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        float o[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
+        const double lh = head_l(h), mh = head_m(h);
+        put_record(recs + (((size_t)(gw + stream) * gs + gj) * HW + h) * C::REC_BYTES, mh, lh, o);
+      }
+    }
   };
 
   // End of the run: publish the held record and the last segment's record
@@ -688,14 +796,21 @@ paged_decode_kernel(DecodeArgs a) {
     const bool pub_cur = n_cur > 1, pub_held = held_stream >= 0;
     if (!pub_cur && !pub_held) return;
     if (pub_cur) {
-      float o[DPL];
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[k] - (double)acc_c[k]);
-      const double lsum = lane_sum();
-      put_record(recs + ((size_t)(gw + seg_stream) * gs + gj) * C::REC_BYTES, m_run, lsum, o);
+      for (int h = 0; h < HW; ++h) {
+        float o[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
+        const double lsum = head_l(h), mh = head_m(h);
+        put_record(recs + (((size_t)(gw + seg_stream) * gs + gj) * HW + h) * C::REC_BYTES,
+                   mh, lsum, o);
+      }
     }
-    if (pub_held)
-      put_record(recs + ((size_t)(gw + held_stream) * gs + gj) * C::REC_BYTES, held_m, held_l, held_o);
+    if constexpr (HW == 1) {
+      if (pub_held)
+        put_record(recs + ((size_t)(gw + held_stream) * gs + gj) * C::REC_BYTES, held_m, held_l,
+                   held_o);
+    }
     fence_acq_rel_gpu();
     __syncwarp();
     int last = 0;
@@ -744,21 +859,27 @@ paged_decode_kernel(DecodeArgs a) {
       if (has_q) {
         if (seg_stream >= 0) end_segment(seg_stream);
         seg_stream = d.stream;
-        m_run = -INFINITY;
-        l_lane = 0.f;
-        l_c = 0.f;
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) { acc[k] = 0.f; acc_c[k] = 0.f; }
-        // this lane's query channels lane * DPL + j, kept for the segment's groups
-        const float* qsrc = reinterpret_cast<const float*>(slot + C::Q_OFF + gj * D * 4) + lane * DPL;
+        for (int h = 0; h < HW; ++h) {
+          m_run[h] = -INFINITY;
+          l_lane[h] = 0.f;
+          l_c[h] = 0.f;
 #pragma unroll
-        for (int j = 0; j < DPL; j += 2) {
-          const float2 x = *reinterpret_cast<const float2*>(qsrc + j);
-          qv[j] = x.x;
-          qv[j + 1] = x.y;
+          for (int k = 0; k < DPL; ++k) { acc[h][k] = 0.f; acc_c[h][k] = 0.f; }
+          // this lane's query channels lane * DPL + j, kept for the segment's groups
+          const float* qsrc =
+              reinterpret_cast<const float*>(slot + C::Q_OFF + (gj * HW + h) * D * 4) + lane * DPL;
+#pragma unroll
+          for (int j = 0; j < DPL; j += 2) {
+            const float2 x = *reinterpret_cast<const float2*>(qsrc + j);
+            qv[h][j] = x.x;
+            qv[h][j + 1] = x.y;
+          }
         }
       }
       if (has_sz) {
+#pragma unroll
+        for (int hh = 0; hh < HW; ++hh) {
         // Each lane takes its DPL channels c = lane * DPL + j: q*s, the bias
         // terms and the fixed-point digits; the digits go through the warp's
         // staging bytes to the lanes whose mma B operands hold them (lane
@@ -774,7 +895,7 @@ paged_decode_kernel(DecodeArgs a) {
           const float sa[2] = {s2.x, s2.y}, za[2] = {z2.x, z2.y};
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
-            const double qd = (double)qv[j + k], sd = (double)sa[k];
+            const double qd = (double)qv[hh][j + k], sd = (double)sa[k];
             qsj[j + k] = qd * sd;  // exact product
             amax = fmax(amax, fabs(qsj[j + k]));
             bsum = fma(qd, (double)za[k] * sd, bsum);
@@ -783,7 +904,8 @@ paged_decode_kernel(DecodeArgs a) {
         // butterfly sums: every lane ends with the same value
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(kFull, bsum, o);
-        bias = bsum;
+        if constexpr (HW == 1) bias[hh] = bsum;
+        else if (hl == hh) bias[0] = bsum;  // the head whose softmax this lane runs
         // |qs| < 2^E; q and s are float32, so a nonzero product lies in
         // [2^-298, 2^256] and every power of two used below is a normal double
         int bexp = amax > 0.0 ? ((__double2hiint(amax) >> 20) & 0x7FF) : 0;
@@ -791,8 +913,13 @@ paged_decode_kernel(DecodeArgs a) {
         for (int o = 16; o > 0; o >>= 1) bexp = max(bexp, __shfl_xor_sync(kFull, bexp, o));
         const int E = bexp > 0 ? bexp - 1022 : 0;
         const double scale = __hiloint2double((1023 + 56 - E) << 20, 0);
-        w0 = __hiloint2double((1023 + E - 7 - 14 * ft) << 20, 0);
-        w1 = __hiloint2double((1023 + E - 14 - 14 * ft) << 20, 0);
+        if constexpr (HW == 1) {
+          w0[hh] = __hiloint2double((1023 + E - 7 - 14 * ft) << 20, 0);
+          w1[hh] = __hiloint2double((1023 + E - 14 - 14 * ft) << 20, 0);
+        } else if (hl == hh) {
+          // weight of this lane's first C column in pass 0: digit (2 ft) mod (8 / HW)
+          w0[0] = __hiloint2double((1023 + E - 7 - 7 * ((2 * ft) % (8 / HW))) << 20, 0);
+        }
         long long X[DPL];
 #pragma unroll
         for (int j = 0; j < DPL; ++j) X[j] = __double2ll_rn(qsj[j] * scale);  // |X| < 2^56
@@ -819,33 +946,61 @@ paged_decode_kernel(DecodeArgs a) {
             }
           }
           __syncwarp();
-          if ((fg >> 2) == half) {
+          if constexpr (HW == 1) {
+            if ((fg >> 2) == half) {
 #pragma unroll
-            for (int e = 0; e < C::KT; ++e) {
+              for (int e = 0; e < C::KT; ++e) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint2 v =
-                    *reinterpret_cast<const uint2*>(dig + (fg & 3) * kDigRow + 64 * e + 32 * h + 8 * ft);
-                bfrag[2 * e][h] = __byte_perm(v.x, v.y, 0x6420);      // even channels
-                bfrag[2 * e + 1][h] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
+                for (int hf = 0; hf < 2; ++hf) {
+                  const uint2 v =
+                      *reinterpret_cast<const uint2*>(dig + (fg & 3) * kDigRow + 64 * e + 32 * hf + 8 * ft);
+                  bfrag[hh][2 * e][hf] = __byte_perm(v.x, v.y, 0x6420);      // even channels
+                  bfrag[hh][2 * e + 1][hf] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
+                }
+              }
+            }
+          } else if ((fg * HW) / 8 == hh) {
+            // B role: this lane holds column fg = (head fg * HW / 8, digit
+            // p * (8 / HW) + fg % (8 / HW)) of every pass p
+#pragma unroll
+            for (int pp = 0; pp < HW; ++pp) {
+              const int dg = pp * (8 / HW) + fg % (8 / HW);
+              if ((dg >> 2) == half) {
+#pragma unroll
+                for (int e = 0; e < C::KT; ++e) {
+#pragma unroll
+                  for (int hf = 0; hf < 2; ++hf) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(dig + (dg & 3) * kDigRow + 64 * e +
+                                                                   32 * hf + 8 * ft);
+                    bfrag[pp][2 * e][hf] = __byte_perm(v.x, v.y, 0x6420);      // even channels
+                    bfrag[pp][2 * e + 1][hf] = __byte_perm(v.x, v.y, 0x7531);  // odd channels
+                  }
+                }
               }
             }
           }
         }
         __syncwarp();  // staging read before the page weights overwrite it
+        }
       }
 
       if (ntok > 0) {
         // ---- logits of tokens fg and fg + 8 (every lane of the row group) ----
         const char* krow = slot + C::K_OFF + ((lane & 7) + 8 * ((lane >> 3) & 1)) * (D / 2) +
                            16 * (lane >> 4);
-        // float32 pools: four independent MMA chains (even / odd channels x
-        // even / odd 32-byte chunk) instead of one chain of 2 KT -- integer
-        // sums, so the split changes no bit of the result; measured 63.2 ->
-        // 62.2 us at config 0. The 16-bit pools keep one chain (their GQA
-        // step measured 0.8 us slower with four).
-        constexpr bool kSplit = VK == 0;
-        int cs[4][4] = {};
+        // float32 pools with one head per warp: four independent MMA chains
+        // (even / odd channels x even / odd 32-byte chunk) instead of one chain
+        // of 2 KT -- integer sums, so the split changes no bit of the result;
+        // measured 63.2 -> 62.2 us at config 0. The 16-bit pools keep one chain
+        // (their GQA step measured 0.8 us slower with four), and so do warps
+        // serving several heads, whose heads are independent chains already.
+        constexpr bool kSplit = VK == 0 && HW == 1;
+        constexpr int NCH = kSplit ? 4 : 1;
+        int cs[HW][NCH][4];
+#pragma unroll
+        for (int h = 0; h < HW; ++h)
+#pragma unroll
+          for (int c4 = 0; c4 < NCH; ++c4) cs[h][c4][0] = cs[h][c4][1] = cs[h][c4][2] = cs[h][c4][3] = 0;
 #pragma unroll
         for (int e = 0; e < C::KT; ++e) {
           uint32_t r[4];
@@ -854,65 +1009,130 @@ paged_decode_kernel(DecodeArgs a) {
                                   r[3] & 0x0F0F0F0Fu};
           const uint32_t hi[4] = {(r[0] >> 4) & 0x0F0F0F0Fu, (r[1] >> 4) & 0x0F0F0F0Fu,
                                   (r[2] >> 4) & 0x0F0F0F0Fu, (r[3] >> 4) & 0x0F0F0F0Fu};
-          mma_u8s8_16832(cs[kSplit ? 2 * (e & 1) : 0], lo, bfrag[2 * e][0], bfrag[2 * e][1]);
-          mma_u8s8_16832(cs[kSplit ? 2 * (e & 1) + 1 : 0], hi, bfrag[2 * e + 1][0], bfrag[2 * e + 1][1]);
-        }
-        if constexpr (kSplit) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) cs[0][k] = (cs[0][k] + cs[1][k]) + (cs[2][k] + cs[3][k]);
+          for (int h = 0; h < HW; ++h) {
+            mma_u8s8_16832(cs[h][kSplit ? 2 * (e & 1) : 0], lo, bfrag[h][2 * e][0], bfrag[h][2 * e][1]);
+            mma_u8s8_16832(cs[h][kSplit ? 2 * (e & 1) + 1 : 0], hi, bfrag[h][2 * e + 1][0],
+                           bfrag[h][2 * e + 1][1]);
+          }
         }
-        double lg0 = fma((double)cs[0][1], w1, (double)cs[0][0] * w0);
-        double lg1 = fma((double)cs[0][3], w1, (double)cs[0][2] * w0);
-        lg0 += __shfl_xor_sync(kFull, lg0, 1);
-        lg1 += __shfl_xor_sync(kFull, lg1, 1);
-        lg0 += __shfl_xor_sync(kFull, lg0, 2);
-        lg1 += __shfl_xor_sync(kFull, lg1, 2);
-        lg0 = fg < ntok ? lg0 - bias : -INFINITY;
-        lg1 = fg + 8 < ntok ? lg1 - bias : -INFINITY;
+        if constexpr (HW == 1) {
+          if constexpr (kSplit) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              cs[0][0][k] = (cs[0][0][k] + cs[0][1 % NCH][k]) + (cs[0][2 % NCH][k] + cs[0][3 % NCH][k]);
+          }
+          double x0 = fma((double)cs[0][0][1], w1[0], (double)cs[0][0][0] * w0[0]);
+          double x1 = fma((double)cs[0][0][3], w1[0], (double)cs[0][0][2] * w0[0]);
+          x0 += __shfl_xor_sync(kFull, x0, 1);
+          x1 += __shfl_xor_sync(kFull, x1, 1);
+          x0 += __shfl_xor_sync(kFull, x0, 2);
+          x1 += __shfl_xor_sync(kFull, x1, 2);
+          const double lg0 = fg < ntok ? x0 - bias[0] : -INFINITY;
+          const double lg1 = fg + 8 < ntok ? x1 - bias[0] : -INFINITY;
 
-        // ---- online softmax: rescale only when the running max moves ----
-        if (__any_sync(kFull, lg0 > m_run || lg1 > m_run)) {
+          // ---- online softmax: rescale only when the running max moves ----
+          if (__any_sync(kFull, lg0 > m_run[0] || lg1 > m_run[0])) {
+            double pmax = fmax(lg0, lg1);
+#pragma unroll
+            for (int o = 16; o > 2; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
+            const double m_new = fmax(m_run[0], pmax);
+            const float corr = exp_neg(m_run[0] - m_new);
+            l_lane[0] *= corr;
+            l_c[0] *= corr;
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) { acc[0][k] *= corr; acc_c[0][k] *= corr; }
+            m_run[0] = m_new;
+          }
+          const float p0 = exp_neg(lg0 - m_run[0]), p1 = exp_neg(lg1 - m_run[0]);
+          if (ft == 0) {  // one lane per row group owns tokens fg and fg + 8
+            kahan_rescale_add(l_lane[0], l_c[0], 1.f, p0);
+            kahan_rescale_add(l_lane[0], l_c[0], 1.f, p1);
+            p_tab[fg] = p0;
+            p_tab[fg + 8] = p1;
+          }
+        } else {
+          // Column heads: pass p's C columns 2ft, 2ft + 1 are two digits of head
+          // hl, weighted 2^(E - 7 - 7 dg); the passes advance dg by 8 / HW.
+          double x0 = 0.0, x1 = 0.0, wa = w0[0];
+          constexpr double kStep = HW == 4 ? 0x1p-14 : 0x1p-28;  // 2^(-7 * 8 / HW)
+#pragma unroll
+          for (int pp = 0; pp < HW; ++pp) {
+            const double wb = wa * 0.0078125;  // the column's second digit: 2^-7 lower
+            x0 = fma((double)cs[pp][0][0], wa, x0);
+            x0 = fma((double)cs[pp][0][1], wb, x0);
+            x1 = fma((double)cs[pp][0][2], wa, x1);
+            x1 = fma((double)cs[pp][0][3], wb, x1);
+            wa *= kStep;
+          }
+          if constexpr (HW == 2) {  // lanes ft and ft ^ 1 hold complementary digits of a head
+            x0 += __shfl_xor_sync(kFull, x0, 1);
+            x1 += __shfl_xor_sync(kFull, x1, 1);
+          }
+          const double lg0 = fg < ntok ? x0 - bias[0] : -INFINITY;
+          const double lg1 = fg + 8 < ntok ? x1 - bias[0] : -INFINITY;
+
+          // ---- online softmax of head hl across its lanes (g = 0..7) ----
           double pmax = fmax(lg0, lg1);
+          pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, 4));
+          pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, 8));
+          pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, 16));
+          if (__any_sync(kFull, pmax > m_run[0])) {
+            const double m_new = fmax(m_run[0], pmax);
+            const float corr = exp_neg(m_run[0] - m_new);  // exactly 1 when unmoved
+            l_lane[0] *= corr;
+            l_c[0] *= corr;
+            m_run[0] = m_new;
 #pragma unroll
-          for (int o = 16; o > 2; o >>= 1) pmax = fmax(pmax, __shfl_xor_sync(kFull, pmax, o));
-          const double m_new = fmax(m_run, pmax);
-          const float corr = exp_neg(m_run - m_new);
-          l_lane *= corr;
-          l_c *= corr;
+            for (int h = 0; h < HW; ++h) {  // every lane holds channels of every head
+              const float ch = __shfl_sync(kFull, corr, head_src(h));
+              if (ch != 1.f) {
 #pragma unroll
-          for (int k = 0; k < DPL; ++k) { acc[k] *= corr; acc_c[k] *= corr; }
-          m_run = m_new;
-        }
-        const float p0 = exp_neg(lg0 - m_run), p1 = exp_neg(lg1 - m_run);
-        if (ft == 0) {  // one lane per row group owns tokens fg and fg + 8
-          kahan_rescale_add(l_lane, l_c, 1.f, p0);
-          kahan_rescale_add(l_lane, l_c, 1.f, p1);
-          p_tab[fg] = p0;
-          p_tab[fg + 8] = p1;
+                for (int k = 0; k < DPL; ++k) { acc[h][k] *= ch; acc_c[h][k] *= ch; }
+              }
+            }
+          }
+          const float p0 = exp_neg(lg0 - m_run[0]), p1 = exp_neg(lg1 - m_run[0]);
+          if (HW == 4 || (ft & 1) == 0) {  // one lane per (row group, head)
+            kahan_rescale_add(l_lane[0], l_c[0], 1.f, p0);
+            kahan_rescale_add(l_lane[0], l_c[0], 1.f, p1);
+            p_tab[fg * HW + hl] = p0;
+            p_tab[(fg + 8) * HW + hl] = p1;
+          }
         }
         __syncwarp();
 
-        // ---- P.V over the page's valid rows (float32 page sum, Kahan into the run) ----
+        // ---- P.V over the page's valid rows (float32 page sums, Kahan into the run);
+        // each value row is loaded once for all HW heads ----
         const char* vs = slot + C::V_OFF;
-        float ps[DPL];
+        float ps[HW][DPL];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) ps[k] = 0.f;
-        if (ntok == kPage) {
+        for (int h = 0; h < HW; ++h)
 #pragma unroll
-          for (int t4 = 0; t4 < kPage / 4; ++t4) {
-            const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
-            pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps);
-            pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, ps);
-            pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps);
-            pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps);
+          for (int k = 0; k < DPL; ++k) ps[h][k] = 0.f;
+        if constexpr (HW == 1) {
+          if (ntok == kPage) {
+#pragma unroll
+            for (int t4 = 0; t4 < kPage / 4; ++t4) {
+              const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
+              pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps[0]);
+              pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, ps[0]);
+              pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps[0]);
+              pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps[0]);
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < kPage; ++t)
+              if (t < ntok) pv_row<D, VK>(vs, p_tab[t], t, lane, ps[0]);
           }
         } else {
-#pragma unroll
-          for (int t = 0; t < kPage; ++t)
-            if (t < ntok) pv_row<D, VK>(vs, p_tab[t], t, lane, ps);
+#pragma unroll 4
+          for (int t = 0; t < ntok; ++t) pv_row_heads<D, VK, HW>(vs, p_tab + t * HW, t, lane, ps);
         }
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[k], acc_c[k], 1.f, ps[k]);
+        for (int h = 0; h < HW; ++h)
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[h][k], acc_c[h][k], 1.f, ps[h][k]);
       }
 
     }
@@ -1026,34 +1246,52 @@ constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 constexpr int kMaxCtasF32 = I4KV_DECODE_MAX_CTAS_F32;
 constexpr int kMaxCtas16 = I4KV_DECODE_MAX_CTAS_16;
 
+// Query heads per warp for GQA ratio g at head dim d: 4 when 4 divides g (up
+// to d128: the per-head registers of d256 do not fit), 2 when 2 does, else 1.
+// The fused split exchange runs one head per warp.
+// Measured at config 0's shape with 32 query heads (G = 2, 4, 8, 32): one
+// head per warp 45 us for every G; two heads per warp 45-51 us; four 71 us
+// (232 registers: two CTAs per SM, and the warp serializes the heads' digit,
+// softmax and merge work). Default: one head per warp.
+#ifndef I4KV_MAX_HEADS_PER_WARP
+#define I4KV_MAX_HEADS_PER_WARP 1
+#endif
+int heads_per_warp(int g, int d, bool xmode) {
+  constexpr int kMaxHw = I4KV_MAX_HEADS_PER_WARP;
+  if (xmode) return 1;
+  if (kMaxHw >= 4 && g % 4 == 0 && d <= 128) return 4;
+  if (kMaxHw >= 2 && g % 2 == 0) return 2;
+  return 1;
+}
+
 // Warps sharing one ring: the largest divisor of kWarps (a power of two) that
-// divides the GQA ratio, so a CTA holds whole groups of query heads.
-int ring_group(int num_q_heads, int num_kv_heads) {
-  const int g = num_q_heads / num_kv_heads;
+// divides g / hw, so a CTA holds whole groups of query heads.
+int ring_group(int num_q_heads, int num_kv_heads, int hw) {
+  const int g = num_q_heads / num_kv_heads / hw;
   int x = kWarps;
   while (g % x) x >>= 1;
   return x;
 }
 
 template <int D, int VK>
-size_t dyn_smem(int batch, int gs) {
+size_t dyn_smem(int batch, int gs, int hw) {
   using C = Cfg<D, kWarps, kStages, VK>;
   const size_t ring_slots = gs == 1 ? (size_t)kWarps * kStages : (size_t)kWarps;  // groups x depth
-  return 256 + pfx_bytes(batch) + ring_slots * (C::Q_OFF + (size_t)gs * D * 4) +
+  return 256 + pfx_bytes(batch) + ring_slots * (C::Q_OFF + (size_t)gs * hw * D * 4) +
          (size_t)kWarps * 4 * (D + 32);  // rings, then per-warp digit staging / page weights
 }
 
 struct OccCache {
   std::mutex mu;
-  int dev[32] = {};
-  int key[32] = {};  // (D * 4 + value kind) * 8 + ring group
-  size_t smem[32] = {};
-  int grid[32] = {};
+  int dev[128] = {};
+  int key[128] = {};  // ((D * 4 + value kind) * 8 + ring group) * 8 + heads per warp
+  size_t smem[128] = {};
+  int grid[128] = {};
   int n = 0;
   // Dynamic shared-memory opt-in per (device, kernel): only ever raised, so a
   // launch whose grid came from the cache never exceeds the kernel's limit.
   int attr_dev[128] = {};
-  int attr_key[128] = {};  // D * 4 + value kind
+  int attr_key[128] = {};  // (D * 4 + value kind) * 8 + heads per warp
   size_t attr_max[128] = {};
   int n_attr = 0;
 };
@@ -1069,7 +1307,7 @@ cudaError_t ensure_smem_attr(K kern, int dev, int kkey, size_t smem) {
   const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (i == g_occ.n_attr) {
-    if (g_occ.n_attr == 128) return cudaSuccess;  // 9 kernels x 14 devices fit; never reached
+    if (g_occ.n_attr == 128) return cudaSuccess;  // 24 kernels x 5 devices fit; never reached
     g_occ.attr_dev[i] = dev;
     g_occ.attr_key[i] = kkey;
     ++g_occ.n_attr;
@@ -1078,13 +1316,13 @@ cudaError_t ensure_smem_attr(K kern, int dev, int kkey, size_t smem) {
   return cudaSuccess;
 }
 
-template <int D, int VK>
+template <int D, int VK, int HW>
 cudaError_t decode_grid(int batch, int gs, int* grid_out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const size_t smem = dyn_smem<D, VK>(batch, gs);
-  const int key = (D * 4 + VK) * 8 + gs;
+  const size_t smem = dyn_smem<D, VK>(batch, gs, HW);
+  const int key = ((D * 4 + VK) * 8 + gs) * 8 + HW;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
     for (int i = 0; i < g_occ.n; ++i)
@@ -1093,8 +1331,8 @@ cudaError_t decode_grid(int batch, int gs, int* grid_out) {
         return cudaSuccess;
       }
   }
-  auto kern = paged_decode_kernel<D, kWarps, kStages, VK>;
-  e = ensure_smem_attr(kern, dev, D * 4 + VK, smem);
+  auto kern = paged_decode_kernel<D, kWarps, kStages, VK, HW>;
+  e = ensure_smem_attr(kern, dev, (D * 4 + VK) * 8 + HW, smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0, sms = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem);
@@ -1107,7 +1345,7 @@ cudaError_t decode_grid(int batch, int gs, int* grid_out) {
   const int grid = per_sm * sms;
   {
     std::lock_guard<std::mutex> lk(g_occ.mu);
-    if (g_occ.n < 32) {
+    if (g_occ.n < 128) {
       g_occ.dev[g_occ.n] = dev; g_occ.key[g_occ.n] = key; g_occ.smem[g_occ.n] = smem;
       g_occ.grid[g_occ.n] = grid; ++g_occ.n;
     }
@@ -1116,34 +1354,73 @@ cudaError_t decode_grid(int batch, int gs, int* grid_out) {
   return cudaSuccess;
 }
 
-template <int D, int VK>
-cudaError_t ws_size(int batch, int heads, int gs, size_t* out) {
+// Records: one per (warp, head) slot of the grid plus one per query stream.
+template <int D, int VK, int HW>
+cudaError_t ws_size_hw(int batch, int heads, int gs, size_t* out) {
   int grid = 0;
-  cudaError_t e = decode_grid<D, VK>(batch, gs, &grid);
+  cudaError_t e = decode_grid<D, VK, HW>(batch, gs, &grid);
   if (e != cudaSuccess) return e;
   const long long streams = (long long)batch * heads;
-  const size_t nrec = (size_t)grid * kWarps + (size_t)streams;
+  const size_t nrec = (size_t)grid * kWarps * HW + (size_t)streams;
   *out = cnt_bytes(streams) + nrec * Cfg<D, kWarps, kStages, VK>::REC_BYTES;
+  return cudaSuccess;
+}
+
+template <int D, int VK>
+cudaError_t ws_size_one(int batch, int heads, int kv_heads, int hw, size_t* out) {
+  const int gs = ring_group(heads, kv_heads, hw);
+  switch (hw) {
+    case 4:
+      if constexpr (D <= 128) return ws_size_hw<D, VK, 4>(batch, heads, gs, out);
+      return cudaErrorInvalidValue;
+    case 2: return ws_size_hw<D, VK, 2>(batch, heads, gs, out);
+    default: return ws_size_hw<D, VK, 1>(batch, heads, gs, out);
+  }
+}
+
+// The workspace of a (batch, heads) shape: enough for the heads-per-warp the
+// plain decode uses and for the one head per warp of the fused split.
+template <int D, int VK>
+cudaError_t ws_size(int batch, int heads, int kv_heads, size_t* out) {
+  const int g = heads / kv_heads;
+  size_t a = 0, b = 0;
+  cudaError_t e = ws_size_one<D, VK>(batch, heads, kv_heads, heads_per_warp(g, D, false), &a);
+  if (e != cudaSuccess) return e;
+  e = ws_size_one<D, VK>(batch, heads, kv_heads, 1, &b);
+  if (e != cudaSuccess) return e;
+  *out = a > b ? a : b;
+  return cudaSuccess;
+}
+
+template <int D, int VK, int HW>
+cudaError_t launch_hw(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
+                      cudaEvent_t ev_before, cudaEvent_t ev_after) {
+  int grid = 0;
+  cudaError_t e = decode_grid<D, VK, HW>(a.batch, a.gs, &grid);
+  if (e != cudaSuccess) return e;
+  size_t need = 0;
+  e = ws_size_hw<D, VK, HW>(a.batch, a.heads, a.gs, &need);
+  if (e != cudaSuccess) return e;
+  if (ws_bytes < need) return cudaErrorInvalidValue;
+  if (ev_before && (e = cudaEventRecord(ev_before, stream)) != cudaSuccess) return e;
+  paged_decode_kernel<D, kWarps, kStages, VK, HW>
+      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch, a.gs, HW), stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 
 template <int D, int VK>
 cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
                    cudaEvent_t ev_before, cudaEvent_t ev_after) {
-  int grid = 0;
-  cudaError_t e = decode_grid<D, VK>(a.batch, a.gs, &grid);
-  if (e != cudaSuccess) return e;
-  size_t need = 0;
-  e = ws_size<D, VK>(a.batch, a.heads, a.gs, &need);
-  if (e != cudaSuccess) return e;
-  if (ws_bytes < need) return cudaErrorInvalidValue;
-  if (ev_before && (e = cudaEventRecord(ev_before, stream)) != cudaSuccess) return e;
-  paged_decode_kernel<D, kWarps, kStages, VK>
-      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch, a.gs), stream>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;
-  return cudaSuccess;
+  switch (a.hw) {
+    case 4:
+      if constexpr (D <= 128) return launch_hw<D, VK, 4>(a, ws_bytes, stream, ev_before, ev_after);
+      return cudaErrorInvalidValue;
+    case 2: return launch_hw<D, VK, 2>(a, ws_bytes, stream, ev_before, ev_after);
+    default: return launch_hw<D, VK, 1>(a, ws_bytes, stream, ev_before, ev_after);
+  }
 }
 
 template <int D>
@@ -1158,11 +1435,11 @@ cudaError_t launch_kind(int vk, const DecodeArgs& a, size_t ws_bytes, cudaStream
 }
 
 template <int D>
-cudaError_t ws_size_kind(int vk, int batch, int heads, int gs, size_t* out) {
+cudaError_t ws_size_kind(int vk, int batch, int heads, int kv_heads, size_t* out) {
   switch (vk) {
-    case INT4KV_VALUES_F32: return ws_size<D, 0>(batch, heads, gs, out);
-    case INT4KV_VALUES_F16: return ws_size<D, 1>(batch, heads, gs, out);
-    case INT4KV_VALUES_BF16: return ws_size<D, 2>(batch, heads, gs, out);
+    case INT4KV_VALUES_F32: return ws_size<D, 0>(batch, heads, kv_heads, out);
+    case INT4KV_VALUES_F16: return ws_size<D, 1>(batch, heads, kv_heads, out);
+    case INT4KV_VALUES_BF16: return ws_size<D, 2>(batch, heads, kv_heads, out);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1193,9 +1470,10 @@ cudaError_t paged_entry(const float* query, const uint8_t* k_pool, const void* v
   if ((out && !al16(out)) || (part_out && !al16(part_out))) return cudaErrorInvalidValue;
   DecodeArgs a{query, k_pool, v_pool, sz_pool, block_table, seq_lens, out, batch, num_q_heads,
                max_pages, num_pages, group_tokens / kPage, static_cast<char*>(workspace), status,
-               part_out, num_kv_heads, num_q_heads / num_kv_heads,
-               ring_group(num_q_heads, num_kv_heads), 0};
-  a.vheads = num_q_heads / a.gs;
+               part_out, num_kv_heads, num_q_heads / num_kv_heads, 1, 1, 0};
+  a.hw = heads_per_warp(num_q_heads / num_kv_heads, head_dim, xworld > 0);
+  a.gs = ring_group(num_q_heads, num_kv_heads, a.hw);
+  a.vheads = num_q_heads / (a.gs * a.hw);
   if (xworld > 0) {  // fused split exchange: outputs merged over the ranks' records
     if (xworld > kXRanks || xrank < 0 || xrank >= xworld || !xbufs || part_out || !out)
       return cudaErrorInvalidValue;
@@ -1225,9 +1503,9 @@ cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int n
     return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size<64, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
-    case 128: return ws_size<128, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
-    case 256: return ws_size<256, 0>(batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 64: return ws_size<64, 0>(batch, num_q_heads, num_kv_heads, bytes);
+    case 128: return ws_size<128, 0>(batch, num_q_heads, num_kv_heads, bytes);
+    case 256: return ws_size<256, 0>(batch, num_q_heads, num_kv_heads, bytes);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1239,9 +1517,9 @@ cudaError_t int4kv_paged_decode_workspace_size_ex(int batch, int num_q_heads, in
     return cudaErrorInvalidValue;
   if (batch > kMaxPagedBatch) return cudaErrorInvalidValue;
   switch (head_dim) {
-    case 64: return ws_size_kind<64>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
-    case 128: return ws_size_kind<128>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
-    case 256: return ws_size_kind<256>(value_dtype, batch, num_q_heads, ring_group(num_q_heads, num_kv_heads), bytes);
+    case 64: return ws_size_kind<64>(value_dtype, batch, num_q_heads, num_kv_heads, bytes);
+    case 128: return ws_size_kind<128>(value_dtype, batch, num_q_heads, num_kv_heads, bytes);
+    case 256: return ws_size_kind<256>(value_dtype, batch, num_q_heads, num_kv_heads, bytes);
     default: return cudaErrorInvalidValue;
   }
 }

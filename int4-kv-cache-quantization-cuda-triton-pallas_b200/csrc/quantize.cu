@@ -698,6 +698,8 @@ legacy_keys_init(float* __restrict__ scale_out, float* __restrict__ zp_out, int 
   allow_dependent_launch();
 }
 
+constexpr int kLegRes = 16;  // rows per warp held in registers (all loads in flight at once)
+
 template <bool VEC>
 __global__ void __launch_bounds__(kLegWarps * 32)
 legacy_minmax(const float* __restrict__ kv, int rows, int C, int chunk,
@@ -715,22 +717,22 @@ legacy_minmax(const float* __restrict__ kv, int rows, int C, int chunk,
     const int c = c0 + 4 * lane;
     if (c < C) {
       const float* p = kv + (size_t)r0 * C + c;
-      int r = r0 + warp;
-      for (; r + kLegWarps < r1; r += 2 * kLegWarps) {  // two rows in flight per warp
-        const float4 a = __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0) * C));
-        const float4 b =
-            __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0 + kLegWarps) * C));
-        lo[0] = fmin3f(lo[0], a.x, b.x); hi[0] = fmax3f(hi[0], a.x, b.x);
-        lo[1] = fmin3f(lo[1], a.y, b.y); hi[1] = fmax3f(hi[1], a.y, b.y);
-        lo[2] = fmin3f(lo[2], a.z, b.z); hi[2] = fmax3f(hi[2], a.z, b.z);
-        lo[3] = fmin3f(lo[3], a.w, b.w); hi[3] = fmax3f(hi[3], a.w, b.w);
-      }
-      if (r < r1) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0) * C));
-        lo[0] = fminf(lo[0], a.x); hi[0] = fmaxf(hi[0], a.x);
-        lo[1] = fminf(lo[1], a.y); hi[1] = fmaxf(hi[1], a.y);
-        lo[2] = fminf(lo[2], a.z); hi[2] = fmaxf(hi[2], a.z);
-        lo[3] = fminf(lo[3], a.w); hi[3] = fmaxf(hi[3], a.w);
+      for (int rb = r0 + warp; rb < r1; rb += kLegRes * kLegWarps) {
+        float4 v[kLegRes];  // up to kLegRes rows of this warp requested before any is used
+#pragma unroll
+        for (int k = 0; k < kLegRes; ++k) {
+          const int r = rb + k * kLegWarps;
+          if (r < r1) v[k] = __ldg(reinterpret_cast<const float4*>(p + (size_t)(r - r0) * C));
+        }
+#pragma unroll
+        for (int k = 0; k < kLegRes; ++k) {
+          if (rb + k * kLegWarps < r1) {
+            lo[0] = fminf(lo[0], v[k].x); hi[0] = fmaxf(hi[0], v[k].x);
+            lo[1] = fminf(lo[1], v[k].y); hi[1] = fmaxf(hi[1], v[k].y);
+            lo[2] = fminf(lo[2], v[k].z); hi[2] = fmaxf(hi[2], v[k].z);
+            lo[3] = fminf(lo[3], v[k].w); hi[3] = fmaxf(hi[3], v[k].w);
+          }
+        }
       }
     }
 #pragma unroll
@@ -784,6 +786,19 @@ legacy_codes(const float* __restrict__ kv, int rows, int C, int chunk,
   const int r0 = blockIdx.x * chunk;
   const int r1 = min(rows, r0 + chunk);
   const int t = threadIdx.x;
+  const int cv = c0 + 4 * lane;
+  // The input does not depend on the previous launch: a chunk that fits in
+  // registers is requested before waiting for the keys, so its loads overlap
+  // the min / max step's tail.
+  const bool resident = VEC && chunk <= kLegRes * kLegWarps;
+  float4 v[kLegRes];
+  if (resident && cv < C) {
+#pragma unroll
+    for (int k = 0; k < kLegRes; ++k) {
+      const int r = r0 + warp + k * kLegWarps;
+      if (r < r1) v[k] = __ldg(reinterpret_cast<const float4*>(kv + (size_t)r * C + cv));
+    }
+  }
   grid_dependency_wait();  // every chunk's min / max has landed in the keys
   if (t < kLegTile) {
     float mn = 0.f, sc = 1.f;
@@ -800,14 +815,22 @@ legacy_codes(const float* __restrict__ kv, int rows, int C, int chunk,
   __syncthreads();
   allow_dependent_launch();
   if constexpr (VEC) {
-    const int c = c0 + 4 * lane;
-    if (c >= C) return;
+    if (cv >= C) return;
     const float4 mn = reinterpret_cast<const float4*>(s_mn)[lane];
     const float4 sc = reinterpret_cast<const float4*>(s_sc)[lane];
     const float4 rc = reinterpret_cast<const float4*>(s_rc)[lane];
-    for (int r = r0 + warp; r < r1; r += kLegWarps) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(kv + (size_t)r * C + c));
-      *reinterpret_cast<uint32_t*>(q_out + (size_t)r * C + c) = codes4_rcp(v, mn, sc, rc);
+    if (resident) {
+#pragma unroll
+      for (int k = 0; k < kLegRes; ++k) {
+        const int r = r0 + warp + k * kLegWarps;
+        if (r < r1)
+          *reinterpret_cast<uint32_t*>(q_out + (size_t)r * C + cv) = codes4_rcp(v[k], mn, sc, rc);
+      }
+    } else {
+      for (int r = r0 + warp; r < r1; r += kLegWarps) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(kv + (size_t)r * C + cv));
+        *reinterpret_cast<uint32_t*>(q_out + (size_t)r * C + cv) = codes4_rcp(x, mn, sc, rc);
+      }
     }
   } else {
 #pragma unroll
@@ -932,8 +955,10 @@ cudaError_t cu_quantize_int4(const float* kv, int num_rows, int num_channels, ui
   if (!kv || !q_out || !scale_out || !zp_out) return cudaErrorInvalidValue;
   const int C = num_channels;
   const int tiles = (C + kLegTile - 1) / kLegTile;
-  // about two CTAs per SM in all; at least 8 rows (one per warp) per chunk
+  // about two CTAs per SM in all, more when that keeps every chunk within the
+  // rows the warps hold in registers; at least 8 rows (one per warp) per chunk
   int chunks = (2 * device_sms() + tiles - 1) / tiles;
+  chunks = max(chunks, (num_rows + kLegRes * kLegWarps - 1) / (kLegRes * kLegWarps));
   chunks = min(chunks, (num_rows + kLegWarps - 1) / kLegWarps);
   chunks = max(chunks, 1);
   const int chunk = (num_rows + chunks - 1) / chunks;
