@@ -68,8 +68,12 @@ def parse():
                     help="skip the config 2 / config 3 sweep and the reference-API records (N=1)")
     ap.add_argument("--no-split", action="store_true",
                     help="skip the sequence-split leg of a multi-GPU run")
-    ap.add_argument("--no-seed-check", action="store_true",
-                    help="skip re-timing rank 0's problem on every rank (N>1)")
+    ap.add_argument("--rank-seeds", action="store_true",
+                    help="N>1: each rank draws its own config-0 problem (seed 7 + 1000 * rank) "
+                         "instead of rank 0's, and also re-times rank 0's problem on every rank")
+    ap.add_argument("--reference-api-only", action="store_true",
+                    help="time only the reference's two drop-in launchers (cu_flash_decode_int4, "
+                         "cu_quantize_int4) at its published shapes and print that record")
     return ap.parse_args()
 
 
@@ -448,7 +452,14 @@ def run_ours(args):
     shape = W.config_shape(args.config)
     vdtype = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.values]
     shape.value_bytes = 4 if args.values == "f32" else 2
-    prob = W.torch_build_cache(shape, seed=7 + 1000 * rank, value_dtype=vdtype)
+    # Weak scaling: by default every rank decodes the same seeded problem (rank
+    # 0's), so N ranks repeat the one-GPU measurement. The kernel's time
+    # depends on where the block table puts the pages (measured on one B200:
+    # 61.9-66.5 us over 8 seeds; the table, not the data, sets it), so
+    # per-rank problems (--rank-seeds) would add that spread to the max over
+    # ranks.
+    seed = 7 + 1000 * rank if args.rank_seeds else 7
+    prob = W.torch_build_cache(shape, seed=seed, value_dtype=vdtype)
     cache, query = prob["cache"], prob["query"]
     ids = list(range(shape.batch))
     bt, sl = cache.block_table(ids)
@@ -606,7 +617,6 @@ def run_ours(args):
     sampler.stop()
 
     # ---- per-rank view of the weak-scaling step (N > 1) ----
-    seed = 7 + 1000 * rank
     per_rank = None
     if world > 1:
         stats = gather_per_rank(torch, [sum(step_ms) / K * 1e3, sum(kern_ms) / K * 1e3, seed],
@@ -614,9 +624,9 @@ def run_ours(args):
         per_rank = {"step_us": [round(x[0], 2) for x in stats],
                     "kernel_us": [round(x[1], 2) for x in stats],
                     "seed": [int(x[2]) for x in stats]}
-        # every rank decodes rank 0's problem (seed 7) once more: separates the
-        # block table / data of each rank from the GPU it runs on
-        if not args.no_seed_check:
+        # with per-rank problems, every rank decodes rank 0's problem (seed 7)
+        # once more: separates each rank's block table / data from its GPU
+        if args.rank_seeds:
             prob0 = W.torch_build_cache(shape, seed=7, value_dtype=vdtype)
             r0 = decode_timing(torch, lib, C, shape, prob0, vdtype, K, flush, seed=rank)
             del prob0
@@ -667,7 +677,9 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None,
         "dtype": f"fp32 (exact integer logits, fp64 recombination), int4 keys, {args.values} values",
         "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
-        "config": workload_config(shape, args.config, world),
+        "config": dict(workload_config(shape, args.config, world),
+                       problem_per_rank=("own seed per rank: 7 + 1000 * rank" if args.rank_seeds
+                                         else "rank 0's seeded problem (seed 7) on every rank")),
         "decode_us": round(mean_step * 1e3, 2),
         "step_us_percentiles": {k: round(float(np.percentile(step_ms, q)) * 1e3, 2)
                                 for k, q in (("p10", 10), ("p50", 50), ("p90", 90), ("max", 100))},
@@ -1101,8 +1113,21 @@ def run_step(args):
         dist.destroy_process_group()
 
 
+def run_reference_api(args):
+    """The `reference_api` record alone (one GPU): a small, self-contained case."""
+    import importlib
+    import torch
+    importlib.import_module(PKG + "._build").build()
+    lib = importlib.import_module(PKG + "._lib").load()
+    rec = reference_api_records(torch, lib, L2Flush(torch))
+    print(json.dumps({"reference_api": rec}), flush=True)
+
+
 def main():
     args = parse()
+    if args.reference_api_only:
+        run_reference_api(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "cfg4_long" and dist_env()[1] > 1:

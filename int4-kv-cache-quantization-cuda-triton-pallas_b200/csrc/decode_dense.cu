@@ -9,7 +9,8 @@
 // every staged key / value byte serves a tile of queries. B200 mapping:
 //
 //   * Grid: query tiles x S stream ranges; the S CTAs of one query tile form a
-//     thread-block cluster (S <= 8). Each CTA runs an online softmax over its
+//     thread-block cluster (S <= 16: the non-portable size where the GPU can
+//     schedule it, else 8). Each CTA runs an online softmax over its
 //     contiguous range of 16-row page tiles; the S partial (m, l, acc) states
 //     are merged through distributed shared memory at the end -- split-KV with
 //     no workspace and no second launch.
@@ -49,7 +50,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = 64;     // staged rows per chunk: four 16-row MMA tiles
 constexpr int kDig = 8;        // base-128 digits of the fixed-point q * s
-constexpr int kMaxSplit = 8;   // cluster size (portable limit)
+constexpr int kMaxSplit = 16;  // cluster size: 16 where the GPU allows it (non-portable), else 8
 constexpr int kMaxD = 256;
 constexpr uint32_t kFull = 0xffffffffu;
 
@@ -513,7 +514,7 @@ template <int DP, bool PACKED, int VK>
 cudaError_t launch_shared(const DenseArgs& a, cudaStream_t stream) {
   using Cf = DCfg<DP, PACKED, VK>;
   static std::mutex mu;
-  static bool attr_done[64] = {};
+  static int max_split[64] = {};  // per device: 16 when a 16-CTA cluster can be scheduled
   int dev = 0, sms = 148;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -521,19 +522,42 @@ cudaError_t launch_shared(const DenseArgs& a, cudaStream_t stream) {
   auto kern = shared_stream_decode_kernel<DP, PACKED, VK>;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (!attr_done[dev]) {
+    if (!max_split[dev]) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::SMEM);
       if (e != cudaSuccess) return e;
-      attr_done[dev] = true;
+      int ms = 8;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+          cudaSuccess) {
+        cudaLaunchConfig_t probe = {};
+        probe.gridDim = dim3(16, 1, 1);
+        probe.blockDim = dim3(kThreads, 1, 1);
+        probe.dynamicSmemBytes = Cf::SMEM;
+        cudaLaunchAttribute pa[1];
+        pa[0].id = cudaLaunchAttributeClusterDimension;
+        pa[0].val.clusterDim.x = 16;
+        pa[0].val.clusterDim.y = 1;
+        pa[0].val.clusterDim.z = 1;
+        probe.attrs = pa;
+        probe.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &probe) == cudaSuccess && clusters >= 8)
+          ms = 16;
+      }
+      (void)cudaGetLastError();  // a refused query leaves no error behind
+      max_split[dev] = ms;
     }
   }
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int qtiles = (a.nq + Cf::QT - 1) / Cf::QT;
   const long long tiles = (long long)a.np * ((a.bs + 15) / 16);
   // enough stream ranges to give the GPU about two CTAs per SM, at most one
-  // cluster of 8 per query tile and no more ranges than 16-row tiles
+  // cluster per query tile and no more ranges than 16-row tiles. Clusters of
+  // 16 only when each CTA still gets at least four 64-row chunks: measured at
+  // 8 x 32 queries, 16 ranges took s8192 from 104 to 95 us and s32768 from 382
+  // to 316 us, but s2048 from 35 to 41 us and s512 from 19 to 31 us.
+  const int cap = tiles >= 16LL * 16 ? max_split[dev] : 8;
   int S = (2 * sms + qtiles - 1) / qtiles;
-  S = (int)max(1LL, min((long long)min(S, kMaxSplit), tiles));
+  S = (int)max(1LL, min((long long)min(S, cap), tiles));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(qtiles * S), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

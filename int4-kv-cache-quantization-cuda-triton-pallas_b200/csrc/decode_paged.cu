@@ -1249,10 +1249,14 @@ constexpr int kMaxCtas16 = I4KV_DECODE_MAX_CTAS_16;
 // Query heads per warp for GQA ratio g at head dim d: 4 when 4 divides g (up
 // to d128: the per-head registers of d256 do not fit), 2 when 2 does, else 1.
 // The fused split exchange runs one head per warp.
-// Measured at config 0's shape with 32 query heads (G = 2, 4, 8, 32): one
-// head per warp 45 us for every G; two heads per warp 45-51 us; four 71 us
-// (232 registers: two CTAs per SM, and the warp serializes the heads' digit,
-// softmax and merge work). Default: one head per warp.
+// Measured at config 0's shape with 32 query heads (G = 2, 4, 8, 32), float32
+// values, L2 flushed: one head per warp 45.0 us for every G; two heads per
+// warp 45.0-49.9 us; four heads per warp 65.6-69.1 us (column heads; 71-72 us
+// with one head per MMA column block) -- a warp serving 4 heads takes a
+// quarter of the pages, so its run of ~7 pages is dominated by the run's
+// fixed costs (first page, digits of 4 heads, 4 heads of record merges).
+// Default: one head per warp; the multi-head kernels are compiled only when
+// this is raised.
 #ifndef I4KV_MAX_HEADS_PER_WARP
 #define I4KV_MAX_HEADS_PER_WARP 1
 #endif
@@ -1371,9 +1375,12 @@ cudaError_t ws_size_one(int batch, int heads, int kv_heads, int hw, size_t* out)
   const int gs = ring_group(heads, kv_heads, hw);
   switch (hw) {
     case 4:
-      if constexpr (D <= 128) return ws_size_hw<D, VK, 4>(batch, heads, gs, out);
+      if constexpr (D <= 128 && I4KV_MAX_HEADS_PER_WARP >= 4)
+        return ws_size_hw<D, VK, 4>(batch, heads, gs, out);
       return cudaErrorInvalidValue;
-    case 2: return ws_size_hw<D, VK, 2>(batch, heads, gs, out);
+    case 2:
+      if constexpr (I4KV_MAX_HEADS_PER_WARP >= 2) return ws_size_hw<D, VK, 2>(batch, heads, gs, out);
+      return cudaErrorInvalidValue;
     default: return ws_size_hw<D, VK, 1>(batch, heads, gs, out);
   }
 }
@@ -1416,9 +1423,13 @@ cudaError_t launch(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
                    cudaEvent_t ev_before, cudaEvent_t ev_after) {
   switch (a.hw) {
     case 4:
-      if constexpr (D <= 128) return launch_hw<D, VK, 4>(a, ws_bytes, stream, ev_before, ev_after);
+      if constexpr (D <= 128 && I4KV_MAX_HEADS_PER_WARP >= 4)
+        return launch_hw<D, VK, 4>(a, ws_bytes, stream, ev_before, ev_after);
       return cudaErrorInvalidValue;
-    case 2: return launch_hw<D, VK, 2>(a, ws_bytes, stream, ev_before, ev_after);
+    case 2:
+      if constexpr (I4KV_MAX_HEADS_PER_WARP >= 2)
+        return launch_hw<D, VK, 2>(a, ws_bytes, stream, ev_before, ev_after);
+      return cudaErrorInvalidValue;
     default: return launch_hw<D, VK, 1>(a, ws_bytes, stream, ev_before, ev_after);
   }
 }
