@@ -76,6 +76,11 @@ __host__ __device__ inline size_t x_bytes(long long S, int d) {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of wall time
 
+// Pages in flight per warp of a GQA ring group (the ring holds gs times this).
+#ifndef I4KV_GQA_RING_PAGES_PER_WARP
+#define I4KV_GQA_RING_PAGES_PER_WARP 1
+#endif
+
 // Value storage kinds (INT4KV_VALUES_*): 0 float32, 1 float16, 2 bfloat16.
 template <int VK>
 struct ValueKind {
@@ -498,7 +503,7 @@ paged_decode_kernel(DecodeArgs a) {
   // slots per ring: STAGES pages per warp alone; a ring group keeps gs pages
   // in flight (its queries share each page, so it needs fewer bytes in flight
   // and fits more CTAs per SM)
-  const int depth = gs == 1 ? STAGES : gs;
+  const int depth = gs == 1 ? STAGES : gs * I4KV_GQA_RING_PAGES_PER_WARP;
   const int sb = C::Q_OFF + gs * HW * D * 4;  // stage bytes with gs * HW queries
   const bool leader = gj == 0;
   {  // the block table into L2 while the lengths load (first descriptors hit L2)
@@ -1280,7 +1285,8 @@ int ring_group(int num_q_heads, int num_kv_heads, int hw) {
 template <int D, int VK>
 size_t dyn_smem(int batch, int gs, int hw) {
   using C = Cfg<D, kWarps, kStages, VK>;
-  const size_t ring_slots = gs == 1 ? (size_t)kWarps * kStages : (size_t)kWarps;  // groups x depth
+  const size_t ring_slots = gs == 1 ? (size_t)kWarps * kStages
+                                     : (size_t)kWarps * I4KV_GQA_RING_PAGES_PER_WARP;  // groups x depth
   return 256 + pfx_bytes(batch) + ring_slots * (C::Q_OFF + (size_t)gs * hw * D * 4) +
          (size_t)kWarps * 4 * (D + 32);  // rings, then per-warp digit staging / page weights
 }
