@@ -125,8 +125,21 @@ def workload_config(shape, name, world):
             "parallelism": f"dp{world} (batch x heads sharded, no collective)"}
 
 
+def _nvml_handle(nv, index):
+    """The NVML handle of CUDA device `index`, matched by PCI bus id (NVML and
+    CUDA may number the GPUs differently); by index if that fails."""
+    try:
+        import torch
+        pr = torch.cuda.get_device_properties(index)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        return nv.nvmlDeviceGetHandleByPciBusId(bus)
+    except Exception:
+        return nv.nvmlDeviceGetHandleByIndex(index)
+
+
 class ClockSampler:
-    """NVML sampling of SM clock and throttle reasons in a background thread."""
+    """NVML sampling of SM and memory clocks and throttle reasons in a
+    background thread."""
 
     def __init__(self, index, period=0.002):
         self.samples = []
@@ -137,7 +150,7 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self._h = _nvml_handle(pynvml, index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:
@@ -159,7 +172,8 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 mhz = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM)
-                self.samples.append((time.perf_counter(), mhz, self._reasons()))
+                mem = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_MEM)
+                self.samples.append((time.perf_counter(), mhz, self._reasons(), mem))
             except Exception:
                 pass
             time.sleep(self.period)
@@ -185,10 +199,16 @@ class ClockSampler:
         use = inside if len(inside) >= 3 else self.samples
         reasons = sorted({r for s in use for r in s[2]} - {"gpu_idle"})
         return {"sm_mhz": statistics.median(s[1] for s in use), "sm_max_mhz": self.max_mhz,
+                "mem_mhz": statistics.median(s[3] for s in use),
                 "reasons": reasons, "samples": len(use), "period_ms": round(self.period * 1e3, 1),
                 "window": (self.window if use is inside else "warmup + timed loops")}
 
     window = "timed region"
+
+
+CLOCK_REASONS = ("applications_clocks_setting", "sw_power_cap", "hw_slowdown",
+                 "sw_thermal_slowdown", "hw_thermal_slowdown", "hw_power_brake_slowdown",
+                 "display_clock_setting")
 
 
 def _all_reduce_max(x, world):
@@ -619,11 +639,17 @@ def run_ours(args):
     # ---- per-rank view of the weak-scaling step (N > 1) ----
     per_rank = None
     if world > 1:
-        stats = gather_per_rank(torch, [sum(step_ms) / K * 1e3, sum(kern_ms) / K * 1e3, seed],
-                                world)
+        ck = sampler.summary()
+        reason_bits = sum(1 << i for i, n in enumerate(CLOCK_REASONS) if n in ck["reasons"])
+        stats = gather_per_rank(torch, [sum(step_ms) / K * 1e3, sum(kern_ms) / K * 1e3, seed,
+                                        float(ck["sm_mhz"] or 0), float(ck.get("mem_mhz") or 0),
+                                        float(reason_bits)], world)
         per_rank = {"step_us": [round(x[0], 2) for x in stats],
                     "kernel_us": [round(x[1], 2) for x in stats],
-                    "seed": [int(x[2]) for x in stats]}
+                    "seed": [int(x[2]) for x in stats],
+                    "sm_mhz": [x[3] for x in stats], "mem_mhz": [x[4] for x in stats],
+                    "clock_reasons": [[n for i, n in enumerate(CLOCK_REASONS) if int(x[5]) >> i & 1]
+                                      for x in stats]}
         # with per-rank problems, every rank decodes rank 0's problem (seed 7)
         # once more: separates each rank's block table / data from its GPU
         if args.rank_seeds:

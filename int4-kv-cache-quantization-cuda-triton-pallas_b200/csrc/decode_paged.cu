@@ -76,6 +76,12 @@ __host__ __device__ inline size_t x_bytes(long long S, int d) {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of wall time
 
+// P.V of a full page as two interleaved float32 sums (even / odd rows) in
+// place of one.
+#ifndef I4KV_PV_TWO_CHAINS
+#define I4KV_PV_TWO_CHAINS 0
+#endif
+
 // Pages in flight per warp of a GQA ring group (the ring holds gs times this).
 #ifndef I4KV_GQA_RING_PAGES_PER_WARP
 #define I4KV_GQA_RING_PAGES_PER_WARP 1
@@ -1117,6 +1123,22 @@ paged_decode_kernel(DecodeArgs a) {
           for (int k = 0; k < DPL; ++k) ps[h][k] = 0.f;
         if constexpr (HW == 1) {
           if (ntok == kPage) {
+#if I4KV_PV_TWO_CHAINS
+            // even and odd rows into separate sums: half the FMA chain depth
+            float pq[DPL];
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) pq[k] = 0.f;
+#pragma unroll
+            for (int t4 = 0; t4 < kPage / 4; ++t4) {
+              const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
+              pv_row<D, VK>(vs, pt.x, 4 * t4 + 0, lane, ps[0]);
+              pv_row<D, VK>(vs, pt.y, 4 * t4 + 1, lane, pq);
+              pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps[0]);
+              pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, pq);
+            }
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) ps[0][k] += pq[k];
+#else
 #pragma unroll
             for (int t4 = 0; t4 < kPage / 4; ++t4) {
               const float4 pt = reinterpret_cast<const float4*>(p_tab)[t4];
@@ -1125,6 +1147,7 @@ paged_decode_kernel(DecodeArgs a) {
               pv_row<D, VK>(vs, pt.z, 4 * t4 + 2, lane, ps[0]);
               pv_row<D, VK>(vs, pt.w, 4 * t4 + 3, lane, ps[0]);
             }
+#endif
           } else {
 #pragma unroll
             for (int t = 0; t < kPage; ++t)
