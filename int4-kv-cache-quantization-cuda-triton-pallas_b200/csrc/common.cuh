@@ -76,6 +76,26 @@ I4KV_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), its commit group and
+// the wait for all but the newest N groups.
+I4KV_DEVINL void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+I4KV_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+I4KV_DEVINL void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Atomic add with release and acquire semantics at GPU scope; returns the
+// old value.
+I4KV_DEVINL int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Store o[DPL] (this lane's dims of a D-vector) at dst with the P.V lane layout.
 template <int D>
 I4KV_DEVINL void store_lane_vec(float* dst, const float* o, int lane) {
@@ -100,6 +120,22 @@ I4KV_DEVINL void load_lane_vec_cg(const float* src, float* o, int lane) {
 #pragma unroll
     for (int v4 = 0; v4 < DPL / 4; ++v4) {
       const float4 v = __ldcg(reinterpret_cast<const float4*>(src + v4 * 128 + 4 * lane));
+      o[4 * v4] = v.x; o[4 * v4 + 1] = v.y; o[4 * v4 + 2] = v.z; o[4 * v4 + 3] = v.w;
+    }
+  }
+}
+
+// The same lane layout read from shared memory.
+template <int D>
+I4KV_DEVINL void load_lane_vec_smem(const float* src, float* o, int lane) {
+  constexpr int DPL = D / 32;
+  if constexpr (DPL == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(src + 2 * lane);
+    o[0] = v.x; o[1] = v.y;
+  } else {
+#pragma unroll
+    for (int v4 = 0; v4 < DPL / 4; ++v4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + v4 * 128 + 4 * lane);
       o[4 * v4] = v.x; o[4 * v4 + 1] = v.y; o[4 * v4 + 2] = v.z; o[4 * v4 + 3] = v.w;
     }
   }
@@ -262,6 +298,55 @@ I4KV_DEVINL float exp_neg(double x) {
   float r;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
   return r;
+}
+
+// 1/d in float64 for normal 0 < d < 2^100: a float32 reciprocal estimate and
+// two Newton-Raphson steps y += y(1 - dy), each squaring the relative error
+// (2^-23 -> 2^-46 -> below the float64 rounding).
+I4KV_DEVINL double rcp_f64(double d) {
+  float yf;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yf) : "f"((float)d));
+  double y = (double)yf;
+  double e = fma(-d, y, 1.0);
+  y = fma(y, e, y);
+  e = fma(-d, y, 1.0);
+  return fma(y, e, y);
+}
+
+// floor(x / t) for 0 <= x < 2^52 and 0 < t < 2^31: a float64 quotient estimate
+// (off by at most 2) corrected in exact integer arithmetic, in place of the
+// 64-bit integer division routine.
+I4KV_DEVINL long long floor_div_s52(long long x, long long t) {
+  long long q = (long long)((double)x * rcp_f64((double)t));
+  long long r = x - q * t;
+  while (r < 0) { --q; r += t; }
+  while (r >= t) { ++q; r -= t; }
+  return q;
+}
+
+// e^x for x <= 0 in float64: Cody-Waite reduction x = n ln2 + r, |r| <= ln2/2,
+// with ln2 split into a head of 21 significant bits (n * head is exact) and a
+// tail, then the degree-11 Taylor polynomial of e^r (relative truncation error
+// below 1e-14 on that range) and the exact scaling by 2^n. Arguments below
+// -708 (and -inf) give 0.
+I4KV_DEVINL double exp_nonpos(double x) {
+  if (!(x >= -708.0)) return 0.0;
+  const double n = rint(x * 1.4426950408889634);
+  double r = fma(n, -0x1.62e42p-1, x);
+  r = fma(n, -0x1.fdf473de6af28p-22, r);
+  double p = 2.505210838544172e-08;  // 1/11!
+  p = fma(p, r, 2.755731922398589e-07);
+  p = fma(p, r, 2.755731922398589e-06);
+  p = fma(p, r, 2.48015873015873e-05);
+  p = fma(p, r, 0.0001984126984126984);
+  p = fma(p, r, 0.001388888888888889);
+  p = fma(p, r, 0.008333333333333333);
+  p = fma(p, r, 0.041666666666666664);
+  p = fma(p, r, 0.16666666666666666);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  return p * __hiloint2double(((int)n + 1023) << 20, 0);
 }
 
 // sum = sum*r + x with a running compensation term c (Kahan): the rescale

@@ -23,6 +23,10 @@
 // an (m, l, acc[D]) partial, bumps the stream's counter, and the warp that
 // arrives last merges the partials and writes the output (counters reset to
 // zero on the way out, so the workspace stays zero-filled between launches).
+// A warp publishes its first segment's partial as soon as that segment ends
+// (the other contributors reach that stream only at the ends of their runs)
+// and its last segment's at the end of its run, so a warp has at most one
+// merge to do when its run is over.
 //
 // Data movement: each ring group owns STAGES * gs shared-memory slots and one
 // lane streams its pages into them with 1-D bulk async copies (cp.async.bulk,
@@ -139,6 +143,7 @@ struct DecodeArgs {
   int xworld, xrank;
   char* xbuf[kXRanks];
 };
+
 
 __device__ __forceinline__ void set_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
@@ -476,7 +481,9 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
 // 16-bit value pools halve the stage size, so up to four CTAs fit an SM's
 // shared memory; registers are capped at 128 so that four could be resident,
 // but the grid launches three per SM (I4KV_DECODE_MAX_CTAS_16: measured 45.5
-// us at config 0 against 46.5 with four and 53.5 with two).
+// us at config 0 against 46.5 with four and 53.5 with two). Float32 pools with
+// D <= 128 are held to 168 registers, the budget of three 128-thread CTAs per
+// SM that a grouped-query ring group runs at (D = 256 keeps its full budget).
 //
 // HW = query heads per warp (grouped-query attention, HW in {1, 2, 4}): one
 // warp serves HW consecutive query heads of every kv page it takes. With
@@ -488,7 +495,7 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
 // page's codes are loaded into A fragments once and each value row once for all
 // heads. HW = 1 is plain one-head-per-warp decoding.
 template <int D, int WARPS, int STAGES, int VK, int HW>
-__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? 1 : (HW > 1 ? 3 : 4))
+__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? 3 : 1) : (HW > 1 ? 3 : 4))
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
@@ -518,33 +525,42 @@ paged_decode_kernel(DecodeArgs a) {
     if (off < bt_bytes)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.block_table) + off));
   }
+  uint64_t* bar = bars + gi * depth;
+  if (leader && lane == 0) {  // ordered before every wait by the barriers of the length prefix
+    for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+  }
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
   const long long streams = (long long)a.batch * a.heads;
 
   // Empty streams get exact zeros (the reference returns 0 / max(0, 1e-10)),
-  // or, in partial mode, the empty record (m = -inf, l = 0, acc = 0).
-  for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < streams;
-       s += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(s / a.heads);
-    if (s_pfx[b + 1] == s_pfx[b] && a.xworld == 0) {
-      float* dst = a.out + (size_t)s * D;
-      if (a.part_out) {
-        char* rec = a.part_out + (size_t)s * C::REC_BYTES;
-        *reinterpret_cast<double*>(rec) = -INFINITY;
-        *reinterpret_cast<double*>(rec + 8) = 0.0;
-        dst = reinterpret_cast<float*>(rec + 16);
+  // or, in partial mode, the empty record (m = -inf, l = 0, acc = 0); run
+  // after this warp's first copies are out.
+  auto zero_empty_streams = [&]() {
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < streams;
+         s += (long long)gridDim.x * blockDim.x) {
+      const int b = (int)(s / a.heads);
+      if (s_pfx[b + 1] == s_pfx[b] && a.xworld == 0) {
+        float* dst = a.out + (size_t)s * D;
+        if (a.part_out) {
+          char* rec = a.part_out + (size_t)s * C::REC_BYTES;
+          *reinterpret_cast<double*>(rec) = -INFINITY;
+          *reinterpret_cast<double*>(rec + 8) = 0.0;
+          dst = reinterpret_cast<float*>(rec + 16);
+        }
+        for (int k = 0; k < D; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int k = 0; k < D; k += 4) *reinterpret_cast<float4*>(dst + k) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-  }
+  };
 
   const long long T = (long long)a.vheads * total_pages;  // < 2^31 (checked on the host)
   const long long NW = (long long)gridDim.x * gpc;         // ring groups in the grid
   const long long gw = (long long)blockIdx.x * gpc + gi;
-  const int g0 = (int)(gw * T / NW), g1 = (int)((gw + 1) * T / NW);
+  const int g0 = (int)floor_div_s52(gw * T, NW), g1 = (int)floor_div_s52((gw + 1) * T, NW);
   const int n = g1 - g0;
   const bool xmode = HW == 1 && a.xworld > 0;  // the fused split runs one head per warp
   if (n <= 0) {
+    zero_empty_streams();
     if (xmode) {  // no pages here, but maybe empty streams to exchange
       bool dead = false;
       x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, false, dead);
@@ -553,7 +569,6 @@ paged_decode_kernel(DecodeArgs a) {
     return;
   }
 
-  uint64_t* bar = bars + gi * depth;
   char* ring = stages + (size_t)gi * depth * sb;
   // this warp's digit staging bytes (4 rows of D + 32: the padding puts the
   // four rows a round reads in different banks), dig[g * (D + 32) + c]
@@ -563,18 +578,14 @@ paged_decode_kernel(DecodeArgs a) {
   uint8_t* dig = reinterpret_cast<uint8_t*>(stages + (size_t)gpc * depth * sb +
                                             (size_t)warp * 4 * kDigRow);
   float* p_tab = reinterpret_cast<float*>(dig);  // [16 tokens][HW heads]
-  if (leader && lane == 0) {
-    for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
-    fence_barrier_init();
-  }
-  if (gs == 1) __syncwarp(); else named_bar_sync(1 + gi, gs * 32);
 
   Desc cur = make_desc(a, s_pfx, g0 + lane, g0, g1);
-  Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
   for (int i = 0; i < depth; ++i) {  // prologue: the first `depth` pages (all in chunk 0)
     const Desc d = shfl_desc(cur, i);
     if (leader && lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
   }
+  Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
+  zero_empty_streams();
 
   // Logits of the current group: q.k = sum_c qs_c code_c - bias with
   // qs_c = q_c s_c (exact in float64) and bias = sum_c q_c zp_c s_c. The code
@@ -618,8 +629,8 @@ paged_decode_kernel(DecodeArgs a) {
     const int b = stream / a.vheads, h = stream - b * a.vheads;
     const int np = s_pfx[b + 1] - s_pfx[b];
     const long long gs0 = (long long)a.vheads * s_pfx[b] + (long long)h * np, ge = gs0 + np;
-    w_lo = ((gs0 + 1) * NW - 1) / T;
-    w_hi = (ge * NW - 1) / T;
+    w_lo = floor_div_s52((gs0 + 1) * NW - 1, T);
+    w_hi = floor_div_s52(ge * NW - 1, T);
     return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
   };
 
@@ -675,137 +686,149 @@ paged_decode_kernel(DecodeArgs a) {
         else put_record(a.part_out + qstream * C::REC_BYTES, mh, lsum, o);
         continue;
       }
-      const double den = fmax(lsum, 1e-10);
+      const double rden = rcp_f64(fmax(lsum, 1e-10));
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[h][k] - (double)acc_c[h][k]) / den);
+      for (int k = 0; k < DPL; ++k) o[k] = (float)(((double)acc[h][k] - (double)acc_c[h][k]) * rden);
       store_lane_vec<D>(a.out + qstream * D, o, lane);
     }
   };
 
   // Merge every contributor's record of `stream` (this warp arrived last) and
   // write the output, or in partial mode the merged record. Contributors are
-  // taken in chunks: lane j loads the (m, l) of the chunk's j-th record while
-  // every lane loads its dims of all the chunk's value sums, so a chunk costs
-  // one round trip to L2 (the records were written by other SMs, often on the
-  // other die); chunks combine online in float64.
+  // taken eight at a time: lane j loads the (m, l) of the round's j-th record
+  // while 16-byte asynchronous copies bring the round's value sums into the
+  // warp's ring slot, so a round costs one round trip to L2 (the records were
+  // written by other SMs, often on the other die); rounds combine online in
+  // float64. The loops stay rolled: this code runs once per warp, at the end
+  // of the launch, where every branch target and constant is fetched cold.
   auto merge_stream = [&](int stream, long long w_lo, long long w_hi) {
-    constexpr int CH = 32 / DPL;   // records per chunk (registers: CH * DPL floats)
-    const bool all_run = T >= NW;  // then every warp in [w_lo, w_hi] wrote a record
+    constexpr int MC = 8;  // records per round: (m, l) in lanes 0..7, values staged in shared memory
+    // the warp's staging area: a ring slot, free once the group's run is over
+    // (slot gj of a group ring is at least MC * D floats for every instantiation)
+    char* stage = ring + (size_t)(gj % depth) * sb;
+    const bool all_run = T >= NW;
 #pragma unroll 1
     for (int h = 0; h < HW; ++h) {
-    double M = -INFINITY, L = 0.0, O[DPL];
+      double M = -INFINITY, L = 0.0, O[DPL];
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) O[k] = 0.0;
-    for (long long base = w_lo; base <= w_hi; base += CH) {
-      const int cnt = (int)min((long long)CH, w_hi - base + 1);
-      const long long wj = base + lane;
-      const bool okj = lane < cnt && (all_run || (wj * T) / NW != ((wj + 1) * T) / NW);
-      double mj = -INFINITY, lj = 0.0;
-      if (okj) {
-        const char* r = recs + (((size_t)(wj + stream) * gs + gj) * HW + h) * C::REC_BYTES;
-        mj = __ldcg(reinterpret_cast<const double*>(r));
-        lj = __ldcg(reinterpret_cast<const double*>(r + 8));
-      }
-      float v[CH][DPL];
-#pragma unroll
-      for (int j = 0; j < CH; ++j) {
-        if (j < cnt) {
-          load_lane_vec_cg<D>(reinterpret_cast<const float*>(
-              recs + (((size_t)(base + j + stream) * gs + gj) * HW + h) * C::REC_BYTES + 16), v[j], lane);
+      for (int k = 0; k < DPL; ++k) O[k] = 0.0;
+#pragma unroll 1
+      for (long long base = w_lo; base <= w_hi; base += MC) {
+        const int cnt = (int)min((long long)MC, w_hi - base + 1);
+#pragma unroll 1
+        for (int j = 0; j < cnt; ++j) {
+          const char* src = recs + (((size_t)(base + j + stream) * gs + gj) * HW + h) * C::REC_BYTES + 16;
+          for (int u = 16 * lane; u < 4 * D; u += 512) cp_async16(stage + j * 4 * D + u, src + u);
         }
-      }
-      double cm = mj;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) cm = fmax(cm, __shfl_xor_sync(kFull, cm, o));
-      const double m_new = fmax(M, cm);
-      if (m_new == -INFINITY) continue;  // nothing live yet
-      // float64 exponentials (a handful per stream, off the page loop)
-      const double c = (M == -INFINITY) ? 0.0 : exp(M - m_new);
-      const double ej = (okj && mj != -INFINITY) ? exp(mj - m_new) : 0.0;
-      double lc = lj * ej;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) lc += __shfl_xor_sync(kFull, lc, o);
-      L = fma(L, c, lc);
-#pragma unroll
-      for (int k = 0; k < DPL; ++k) O[k] *= c;
-#pragma unroll
-      for (int j = 0; j < CH; ++j) {
-        const double e = __shfl_sync(kFull, ej, j);
-        if (j < cnt && e != 0.0) {  // records of empty runs are never read into the sum
-#pragma unroll
-          for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[j][k], e, O[k]);
+        cp_async_commit();
+        const long long wj = base + lane;
+        const bool okj = lane < cnt && (all_run || floor_div_s52(wj * T, NW) != floor_div_s52((wj + 1) * T, NW));
+        double mj = -INFINITY, lj = 0.0;
+        if (okj) {
+          const char* r = recs + (((size_t)(wj + stream) * gs + gj) * HW + h) * C::REC_BYTES;
+          mj = __ldcg(reinterpret_cast<const double*>(r));
+          lj = __ldcg(reinterpret_cast<const double*>(r + 8));
         }
-      }
-      M = m_new;
-    }
-    const size_t qstream = ((size_t)stream * gs + gj) * HW + h;
-    float o[DPL];
-    if (a.part_out || xmode) {  // the merged (M, L, O) of this GPU's share of the stream
+        double cm = mj;
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
-      if (xmode) {
-        x_push<D>(a, streams, (long long)qstream, M, L, o, lane);
-        (xm0 < 0 ? xm0 : xm1) = stream;  // finished after the warp's last push
-      } else {
-        put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
-      }
-      continue;
-    }
-    const double den = fmax(L, 1e-10);
+        for (int o = MC / 2; o > 0; o >>= 1) cm = fmax(cm, __shfl_xor_sync(kFull, cm, o));
+        const double m_new = fmax(M, __shfl_sync(kFull, cm, 0));
+        cp_async_wait<0>();
+        __syncwarp();
+        if (m_new == -INFINITY) continue;  // nothing live yet
+        double c = 0.0;  // rescale of the earlier rounds (streams with more than MC records)
+        if (M != -INFINITY) c = exp_nonpos(M - m_new);
+        const double ej = (okj && mj != -INFINITY) ? exp_nonpos(mj - m_new) : 0.0;
+        double lc = lj * ej;
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] / den);
-    store_lane_vec<D>(a.out + qstream * D, o, lane);
+        for (int o = MC / 2; o > 0; o >>= 1) lc += __shfl_xor_sync(kFull, lc, o);
+        L = fma(L, c, __shfl_sync(kFull, lc, 0));
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) O[k] *= c;
+#pragma unroll 1
+        for (int j = 0; j < cnt; ++j) {
+          const double e = __shfl_sync(kFull, ej, j);
+          if (e != 0.0) {  // records of empty runs are never read into the sum
+            float v[DPL];
+            load_lane_vec_smem<D>(reinterpret_cast<const float*>(stage + j * 4 * D), v, lane);
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) O[k] = fma((double)v[k], e, O[k]);
+          }
+        }
+        __syncwarp();  // the stage is read before the next round's copies
+        M = m_new;
+      }
+      const size_t qstream = ((size_t)stream * gs + gj) * HW + h;
+      float o[DPL];
+      if (a.part_out || xmode) {  // the merged (M, L, O) of this GPU's share of the stream
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)O[k];
+        if (xmode) {
+          x_push<D>(a, streams, (long long)qstream, M, L, o, lane);
+          (xm0 < 0 ? xm0 : xm1) = stream;  // finished after the warp's last push
+        } else {
+          put_record(a.part_out + qstream * C::REC_BYTES, M, L, o);
+        }
+        continue;
+      }
+      const double rden = rcp_f64(fmax(L, 1e-10));
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)(O[k] * rden);
+      store_lane_vec<D>(a.out + qstream * D, o, lane);
     }
   };
 
   // The warp's first segment, when its stream is shared with earlier warps and
-  // ends inside this run: its record is held in registers (HW = 1) or stored
-  // to its slot at once (HW > 1, plain stores) and published with the last
-  // segment's at the end of the run, so the run never stalls on a fence or an
-  // atomic in the middle.
-  int held_stream = -1;
-  double held_m = 0.0, held_l = 0.0;
-  float held_o[DPL];
-#pragma unroll
-  for (int k = 0; k < DPL; ++k) held_o[k] = 0.f;
+  // ends inside this run: its record is stored and its arrival counted as soon
+  // as the segment ends; the arrival's ticket (the counter's old value) is
+  // read only at the end of the run.
+  int held_stream = -1, held_n = 0, held_ticket = 0;
 
   auto end_segment = [&](int stream) {
     long long w_lo, w_hi;
-    if (contributors_of(stream, w_lo, w_hi) == 1) {
+    const int nc = contributors_of(stream, w_lo, w_hi);
+    if (nc == 1) {
       finish_alone(stream);
       return;
     }
-    held_stream = stream;  // only the run's first segment can get here mid-run
-    if constexpr (HW == 1) {
-      held_m = m_run[0];
-      held_l = lane_sum(0);
+    // Only the run's first segment can get here mid-run. Its record is
+    // published now and its arrival counted at once; the ticket is read only
+    // at the end of the run, so the atomic's round trip overlaps the pages
+    // that follow (the other contributors reach this stream at the ends of
+    // their runs, so this warp is almost never the last arrival).
+    held_stream = stream;
+    held_n = nc;
 #pragma unroll
-      for (int k = 0; k < DPL; ++k) held_o[k] = (float)((double)acc[0][k] - (double)acc_c[0][k]);
-    } else {
+    for (int h = 0; h < HW; ++h) {
+      float o[DPL];
 #pragma unroll
-      for (int h = 0; h < HW; ++h) {
-        float o[DPL];
-#pragma unroll
-        for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
-        const double lh = head_l(h), mh = head_m(h);
-        put_record(recs + (((size_t)(gw + stream) * gs + gj) * HW + h) * C::REC_BYTES, mh, lh, o);
-      }
+      for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
+      const double lh = head_l(h), mh = head_m(h);
+      put_record(recs + (((size_t)(gw + stream) * gs + gj) * HW + h) * C::REC_BYTES, mh, lh, o);
     }
+    __syncwarp();
+    if (lane == 0) held_ticket = atom_add_acq_rel_gpu(&counters[(size_t)stream * gs + gj], 1);
   };
 
-  // End of the run: publish the held record and the last segment's record
-  // (if shared), one fence, both arrivals counted in parallel, then merge
-  // every stream this warp arrived last at.
+  // End of the run: publish the last segment's record (if shared) with one
+  // release + acquire arrival, then merge every stream this warp arrived last
+  // at (the first segment's only when its ticket says so, which is rare).
   auto end_run = [&]() {
-    long long lo_c = 0, hi_c = -1, lo_h = 0, hi_h = -1;
-    int n_cur = 0, n_held = 0;
+    long long lo_c = 0, hi_c = -1;
+    int n_cur = 0;
     if (seg_stream >= 0) {
       n_cur = contributors_of(seg_stream, lo_c, hi_c);
       if (n_cur == 1) finish_alone(seg_stream);
     }
-    if (held_stream >= 0) n_held = contributors_of(held_stream, lo_h, hi_h);
-    const bool pub_cur = n_cur > 1, pub_held = held_stream >= 0;
-    if (!pub_cur && !pub_held) return;
+    const bool pub_cur = n_cur > 1;
+    bool last_held = false;
+    if (held_stream >= 0) {
+      const int t = __shfl_sync(kFull, held_ticket, 0);
+      last_held = t == held_n - 1;
+      if (last_held && lane == 0) counters[(size_t)held_stream * gs + gj] = 0;  // zero-filled again
+    }
+    if (!pub_cur && !last_held) return;
+    bool last_cur = false;
     if (pub_cur) {
 #pragma unroll
       for (int h = 0; h < HW; ++h) {
@@ -816,31 +839,27 @@ paged_decode_kernel(DecodeArgs a) {
         put_record(recs + (((size_t)(gw + seg_stream) * gs + gj) * HW + h) * C::REC_BYTES,
                    mh, lsum, o);
       }
+      // the warp's record stores, then one release + acquire arrival (the warp
+      // barrier orders every lane's stores before the release)
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        int* ctr = &counters[(size_t)seg_stream * gs + gj];
+        last = atom_add_acq_rel_gpu(ctr, 1) == n_cur - 1;
+        if (last) *ctr = 0;  // leave the workspace zero-filled
+      }
+      last_cur = __shfl_sync(kFull, last, 0) != 0;
     }
-    if constexpr (HW == 1) {
-      if (pub_held)
-        put_record(recs + ((size_t)(gw + held_stream) * gs + gj) * C::REC_BYTES, held_m, held_l,
-                   held_o);
-    }
-    fence_acq_rel_gpu();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0 && pub_held) {
-      int* ctr = &counters[(size_t)held_stream * gs + gj];
-      last = atomicAdd(ctr, 1) == n_held - 1;
-      if (last) *ctr = 0;  // leave the workspace zero-filled
-    }
-    if (lane == 1 && pub_cur) {
-      int* ctr = &counters[(size_t)seg_stream * gs + gj];
-      last = atomicAdd(ctr, 1) == n_cur - 1;
-      if (last) *ctr = 0;
-    }
-    const bool last_held = __shfl_sync(kFull, last, 0) != 0;
-    const bool last_cur = __shfl_sync(kFull, last, 1) != 0;
     if (!last_held && !last_cur) return;
-    fence_acq_rel_gpu();
-    if (last_held) merge_stream(held_stream, lo_h, hi_h);
-    if (last_cur) merge_stream(seg_stream, lo_c, hi_c);
+    __syncwarp();  // the acquiring lane's view before every lane's record loads
+    // one merge site for both streams, so a second merge runs cached code
+#pragma unroll 1
+    for (int t = 0; t < 2; ++t) {
+      if (!(t == 0 ? last_held : last_cur)) continue;
+      long long lo = lo_c, hi = hi_c;
+      if (t == 0) contributors_of(held_stream, lo, hi);
+      merge_stream(t == 0 ? held_stream : seg_stream, lo, hi);
+    }
   };
 
   int st = 0;          // ring slot of page i
