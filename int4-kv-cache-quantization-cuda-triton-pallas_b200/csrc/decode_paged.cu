@@ -193,28 +193,39 @@ struct Desc {
   int stream; // b * vheads + h (queries stream * gs + j, j < gs, read it)
 };
 
-__device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx, int g, int g0,
-                                          int g1) {
-  Desc d{0, 0, 0, -1};
-  if (g >= g1) return d;
+// Sequence b, head h and page p of page-head g of the end-to-end order.
+__device__ __forceinline__ void locate_page(const DecodeArgs& a, const int* s_pfx, int g, int& b, int& h,
+                                            int& p, int& np) {
   const int gq = g / a.vheads;
   int lo = 0, hi = a.batch - 1;  // last b with pfx[b] <= gq
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (s_pfx[mid] <= gq) lo = mid; else hi = mid - 1;
   }
-  const int b = lo;
-  const int np = s_pfx[b + 1] - s_pfx[b];
+  b = lo;
+  np = s_pfx[b + 1] - s_pfx[b];
   const int rem = g - a.vheads * s_pfx[b];
-  const int h = rem / np;
-  const int p = rem - h * np;
+  h = rem / np;
+  p = rem - h * np;
+}
+
+// Descriptor of page-head g for a warp whose pages lie in [glo, ghi) and whose
+// first page is gfirst; `backward` warps take their pages in descending order,
+// so their segments start at a stream's last page and their groups at a
+// group's last page.
+__device__ __forceinline__ Desc make_desc(const DecodeArgs& a, const int* s_pfx, int g, int gfirst,
+                                          int glo, int ghi, bool backward) {
+  Desc d{0, 0, 0, -1};
+  if (g < glo || g >= ghi) return d;
+  int b, h, p, np;
+  locate_page(a, s_pfx, g, b, h, p, np);
   const int len = clamp_len(a.seq_lens[b], a.max_pages * kPage);
   const int ntok = min(kPage, len - p * kPage);
   const int32_t* row = a.block_table + (size_t)b * a.max_pages;
   const int phys = row[p];
   const int gphys = row[(p / a.group_pages) * a.group_pages];
-  const bool first = (g == g0) || (p == 0);
-  const bool grp = first || (p % a.group_pages) == 0;
+  const bool first = (g == gfirst) || (backward ? p == np - 1 : p == 0);
+  const bool grp = first || (p % a.group_pages) == (backward ? a.group_pages - 1 : 0);
   const bool gok = gphys >= 0 && gphys < a.num_pages;
   const bool pok = phys >= 0 && phys < a.num_pages;
   if (!gok || !pok) set_status(a.status, kStatusBadPage);
@@ -502,6 +513,11 @@ paged_decode_kernel(DecodeArgs a) {
   extern __shared__ __align__(128) char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // WARPS*STAGES
   int* s_tmp = reinterpret_cast<int*>(smem + 8 * WARPS * STAGES);      // WARPS ints
+  // warp pairs: claim word (forward count | backward count << 32) and the
+  // end-of-run handoff counter of each pair
+  unsigned long long* s_claim = reinterpret_cast<unsigned long long*>(smem + 128);  // WARPS / 2
+  int* s_pair_done = reinterpret_cast<int*>(smem + 128 + 8 * (WARPS / 2));         // WARPS / 2
+  static_assert(8 * WARPS * STAGES + 4 * WARPS <= 128 && 128 + 12 * (WARPS / 2) <= 256, "header layout");
   int* s_pfx = reinterpret_cast<int*>(smem + 256);                     // batch+1 ints
   char* stages = smem + 256 + pfx_bytes(a.batch);
 
@@ -525,10 +541,22 @@ paged_decode_kernel(DecodeArgs a) {
     if (off < bt_bytes)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.block_table) + off));
   }
+  const bool xmode = HW == 1 && a.xworld > 0;  // the fused split runs one head per warp
+  // Warp pairs: with one warp per ring (no grouped-query sharing) in a plain
+  // decode, warps 2k and 2k + 1 share one run; the first takes its pages
+  // forward from the run's start, the second backward from its end, each
+  // claiming its next page from the pair's shared claim word, so the pair
+  // finishes together however its two warps' page rates differ.
+  const bool paired = HW == 1 && (WARPS % 2 == 0) && STAGES >= 2 && gs == 1 && !xmode && a.part_out == nullptr;
+  const bool bwd = paired && (warp & 1);
   uint64_t* bar = bars + gi * depth;
   if (leader && lane == 0) {  // ordered before every wait by the barriers of the length prefix
     for (int s = 0; s < depth; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
+  }
+  if (paired && !bwd && lane == 0) {
+    s_claim[warp / 2] = 0ull;
+    s_pair_done[warp / 2] = 0;
   }
   const int total_pages = block_page_prefix(a, s_pfx, s_tmp);
   const long long streams = (long long)a.batch * a.heads;
@@ -556,9 +584,38 @@ paged_decode_kernel(DecodeArgs a) {
   const long long T = (long long)a.vheads * total_pages;  // < 2^31 (checked on the host)
   const long long NW = (long long)gridDim.x * gpc;         // ring groups in the grid
   const long long gw = (long long)blockIdx.x * gpc + gi;
-  const int g0 = (int)floor_div_s52(gw * T, NW), g1 = (int)floor_div_s52((gw + 1) * T, NW);
-  const int n = g1 - g0;
-  const bool xmode = HW == 1 && a.xworld > 0;  // the fused split runs one head per warp
+  // contribution units of the stream-K order: warp pairs, or ring groups
+  const long long NU = paired ? (long long)gridDim.x * (WARPS / 2) : NW;
+  const long long gu = paired ? (long long)blockIdx.x * (WARPS / 2) + warp / 2 : gw;
+  const int g0 = (int)floor_div_s52(gu * T, NU), g1 = (int)floor_div_s52((gu + 1) * T, NU);
+  // page-head of the warp's i-th page, and its page count (in a pair, the
+  // pair's length until a claim fails)
+  auto page_at = [&](int i) -> int { return bwd ? g1 - 1 - i : g0 + i; };
+  const int gfirst = bwd ? g1 - 1 : g0;
+  int n = g1 - g0;
+  // Each warp of a pair takes the first 3/8 of the run from its end without
+  // asking; only the middle quarter is claimed page by page (enough to absorb
+  // page rates 25 % apart), so most pages cost no claim.
+  const int n_own = paired ? (int)(((long long)n * 3) / 8) : n;
+  // Claims are pipelined: after a claim succeeds, lane 0 sends the next one at
+  // once and its answer is read when that page is due, so the shared-memory
+  // atomic's round trip overlaps a page of work. Claims go in page order, so
+  // every claim that succeeds is consumed.
+  unsigned long long claim_word = 0ull;  // lane 0: the outstanding claim's answer
+  bool claim_out = false;                // a claim is outstanding (warp-uniform)
+  auto claim_send = [&]() {
+    if (lane == 0) claim_word = atomicAdd(&s_claim[warp / 2], bwd ? (1ull << 32) : 1ull);
+    claim_out = true;
+  };
+  auto claim = [&](int i) -> bool {  // the warp's i-th page, unless the partner has taken it
+    if (i < n_own) return true;
+    if (!claim_out) claim_send();
+    const unsigned long long old = __shfl_sync(kFull, claim_word, 0);
+    claim_out = false;
+    const bool ok = (long long)(uint32_t)old + (long long)(old >> 32) < (long long)(g1 - g0 - 2 * n_own);
+    if (ok) claim_send();
+    return ok;
+  };
   if (n <= 0) {
     zero_empty_streams();
     if (xmode) {  // no pages here, but maybe empty streams to exchange
@@ -579,12 +636,16 @@ paged_decode_kernel(DecodeArgs a) {
                                             (size_t)warp * 4 * kDigRow);
   float* p_tab = reinterpret_cast<float*>(dig);  // [16 tokens][HW heads]
 
-  Desc cur = make_desc(a, s_pfx, g0 + lane, g0, g1);
-  for (int i = 0; i < depth; ++i) {  // prologue: the first `depth` pages (all in chunk 0)
+  Desc cur = make_desc(a, s_pfx, page_at(lane), gfirst, g0, g1, bwd);
+  for (int i = 0; i < depth && i < n; ++i) {  // prologue: the first `depth` pages (all in chunk 0)
+    if (paired && !claim(i)) {
+      n = i;
+      break;
+    }
     const Desc d = shfl_desc(cur, i);
-    if (leader && lane == 0 && i < n) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
+    if (leader && lane == 0) issue_page<D, WARPS, STAGES, VK>(a, d, ring + i * sb, &bar[i]);
   }
-  Desc nxt = make_desc(a, s_pfx, g0 + 32 + lane, g0, g1);
+  Desc nxt = make_desc(a, s_pfx, page_at(32 + lane), gfirst, g0, g1, bwd);
   zero_empty_streams();
 
   // Logits of the current group: q.k = sum_c qs_c code_c - bias with
@@ -629,9 +690,9 @@ paged_decode_kernel(DecodeArgs a) {
     const int b = stream / a.vheads, h = stream - b * a.vheads;
     const int np = s_pfx[b + 1] - s_pfx[b];
     const long long gs0 = (long long)a.vheads * s_pfx[b] + (long long)h * np, ge = gs0 + np;
-    w_lo = floor_div_s52((gs0 + 1) * NW - 1, T);
-    w_hi = floor_div_s52(ge * NW - 1, T);
-    return (T >= NW) ? (int)(w_hi - w_lo + 1) : np;
+    w_lo = floor_div_s52((gs0 + 1) * NU - 1, T);
+    w_hi = floor_div_s52(ge * NU - 1, T);
+    return (T >= NU) ? (int)(w_hi - w_lo + 1) : np;
   };
 
   // Warp-wide sum of head h's lane denominators (float32 sum minus compensation).
@@ -706,7 +767,7 @@ paged_decode_kernel(DecodeArgs a) {
     // the warp's staging area: a ring slot, free once the group's run is over
     // (slot gj of a group ring is at least MC * D floats for every instantiation)
     char* stage = ring + (size_t)(gj % depth) * sb;
-    const bool all_run = T >= NW;
+    const bool all_run = T >= NU;
 #pragma unroll 1
     for (int h = 0; h < HW; ++h) {
       double M = -INFINITY, L = 0.0, O[DPL];
@@ -722,7 +783,7 @@ paged_decode_kernel(DecodeArgs a) {
         }
         cp_async_commit();
         const long long wj = base + lane;
-        const bool okj = lane < cnt && (all_run || floor_div_s52(wj * T, NW) != floor_div_s52((wj + 1) * T, NW));
+        const bool okj = lane < cnt && (all_run || floor_div_s52(wj * T, NU) != floor_div_s52((wj + 1) * T, NU));
         double mj = -INFINITY, lj = 0.0;
         if (okj) {
           const char* r = recs + (((size_t)(wj + stream) * gs + gj) * HW + h) * C::REC_BYTES;
@@ -804,7 +865,7 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
       for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
       const double lh = head_l(h), mh = head_m(h);
-      put_record(recs + (((size_t)(gw + stream) * gs + gj) * HW + h) * C::REC_BYTES, mh, lh, o);
+      put_record(recs + (((size_t)(gu + stream) * gs + gj) * HW + h) * C::REC_BYTES, mh, lh, o);
     }
     __syncwarp();
     if (lane == 0) held_ticket = atom_add_acq_rel_gpu(&counters[(size_t)stream * gs + gj], 1);
@@ -816,11 +877,67 @@ paged_decode_kernel(DecodeArgs a) {
   auto end_run = [&]() {
     long long lo_c = 0, hi_c = -1;
     int n_cur = 0;
-    if (seg_stream >= 0) {
-      n_cur = contributors_of(seg_stream, lo_c, hi_c);
-      if (n_cur == 1) finish_alone(seg_stream);
+    if (seg_stream >= 0) n_cur = contributors_of(seg_stream, lo_c, hi_c);
+    // A pair's meeting point m splits its run: the forward warp took [g0, m),
+    // the backward one [m, g1). When both warps' last segments lie in the same
+    // stream, each leaves its partial in its ring's last slot (free now; the
+    // merges below stage in slot 0) and the second to arrive merges the two;
+    // that stream then counts as one contributor of the pair, like every other
+    // stream of the run.
+    bool have_cur = seg_stream >= 0;  // this warp holds the last segment's state
+    bool pair_merged = false;         // ... merged with the partner's (in pm, pl, po)
+    double pm = 0.0, pl = 0.0, po[DPL];
+    if (paired && have_cur) {
+      const int m = bwd ? g1 - n : g0 + n;
+      bool split = false;
+      if (bwd ? m > g0 : m < g1) {
+        int b, h, p, np;
+        locate_page(a, s_pfx, bwd ? m - 1 : m, b, h, p, np);
+        split = b * a.vheads + h == seg_stream;
+      }
+      if (split) {
+        float o[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = __fsub_rn(acc[0][k], acc_c[0][k]);
+        const double lsum = lane_sum(0);
+        put_record(ring + (size_t)(depth - 1) * sb, m_run[0], lsum, o);
+        __threadfence_block();
+        __syncwarp();
+        int arrived = 0;
+        if (lane == 0) arrived = atomicAdd(&s_pair_done[warp / 2], 1);
+        arrived = __shfl_sync(kFull, arrived, 0);
+        if (arrived == 0) {
+          have_cur = false;  // the partner finishes the stream
+        } else {
+          __threadfence_block();
+          __syncwarp();
+          const char* other = stages + ((size_t)(warp ^ 1) * depth + depth - 1) * sb;
+          const double m2 = *reinterpret_cast<const double*>(other);
+          const double l2 = *reinterpret_cast<const double*>(other + 8);
+          float o2[DPL];
+          load_lane_vec_smem<D>(reinterpret_cast<const float*>(other + 16), o2, lane);
+          pm = fmax(m_run[0], m2);
+          const double e1 = exp_nonpos(m_run[0] - pm), e2 = exp_nonpos(m2 - pm);
+          pl = fma(lsum, e1, l2 * e2);
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) po[k] = fma((double)o[k], e1, (double)o2[k] * e2);
+          pair_merged = true;
+        }
+      }
     }
-    const bool pub_cur = n_cur > 1;
+    if (have_cur && n_cur == 1) {  // the stream lies inside this run (or pair): finish it here
+      if (pair_merged) {
+        const double rden = rcp_f64(fmax(pl, 1e-10));
+        float o[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)(po[k] * rden);
+        store_lane_vec<D>(a.out + (size_t)seg_stream * D, o, lane);
+      } else {
+        finish_alone(seg_stream);
+      }
+      have_cur = false;
+    }
+    const bool pub_cur = have_cur;
     bool last_held = false;
     if (held_stream >= 0) {
       const int t = __shfl_sync(kFull, held_ticket, 0);
@@ -830,14 +947,21 @@ paged_decode_kernel(DecodeArgs a) {
     if (!pub_cur && !last_held) return;
     bool last_cur = false;
     if (pub_cur) {
-#pragma unroll
-      for (int h = 0; h < HW; ++h) {
+      if (pair_merged) {
         float o[DPL];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
-        const double lsum = head_l(h), mh = head_m(h);
-        put_record(recs + (((size_t)(gw + seg_stream) * gs + gj) * HW + h) * C::REC_BYTES,
-                   mh, lsum, o);
+        for (int k = 0; k < DPL; ++k) o[k] = (float)po[k];
+        put_record(recs + (size_t)(gu + seg_stream) * C::REC_BYTES, pm, pl, o);
+      } else {
+#pragma unroll
+        for (int h = 0; h < HW; ++h) {
+          float o[DPL];
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) o[k] = (float)((double)acc[h][k] - (double)acc_c[h][k]);
+          const double lsum = head_l(h), mh = head_m(h);
+          put_record(recs + (((size_t)(gu + seg_stream) * gs + gj) * HW + h) * C::REC_BYTES,
+                     mh, lsum, o);
+        }
       }
       // the warp's record stores, then one release + acquire arrival (the warp
       // barrier orders every lane's stores before the release)
@@ -867,7 +991,7 @@ paged_decode_kernel(DecodeArgs a) {
   for (int i = 0; i < n; ++i) {
     if (i > 0 && (i & 31) == 0) {
       cur = nxt;
-      nxt = make_desc(a, s_pfx, g0 + i + 32 + lane, g0, g1);
+      nxt = make_desc(a, s_pfx, page_at(i + 32 + lane), gfirst, g0, g1, bwd);
     }
     char* slot = ring + st * sb;
     const Desc d = shfl_desc(cur, i & 31);
@@ -1193,6 +1317,7 @@ paged_decode_kernel(DecodeArgs a) {
       break;
     }
     const int nx = i + depth;
+    if (nx < n && paired && !claim(nx)) n = nx;  // the partner took it: this warp's pages end at nx
     if (nx < n) {
       const int src = nx & 31;
       const Desc dn = (nx >> 5) == (i >> 5) ? shfl_desc(cur, src) : shfl_desc(nxt, src);
@@ -1220,8 +1345,8 @@ paged_decode_kernel(DecodeArgs a) {
     // merged as the last local arrival, and its share of the empty streams
     bool dead = false;
     x_empty_streams<D>(a, s_pfx, streams, gw, NW, gs, gj, lane, false, dead);
-    const int v_first = make_desc(a, s_pfx, g0, g0, g1).stream;
-    const int v_last = make_desc(a, s_pfx, g1 - 1, g0, g1).stream;
+    const int v_first = make_desc(a, s_pfx, g0, g0, g0, g1, false).stream;
+    const int v_last = make_desc(a, s_pfx, g1 - 1, g0, g0, g1, false).stream;
     for (int vs = v_first; vs <= v_last; ++vs) {
       const int b = vs / a.vheads;
       if (s_pfx[b + 1] == s_pfx[b]) continue;  // no pages here: an empty stream's duty
