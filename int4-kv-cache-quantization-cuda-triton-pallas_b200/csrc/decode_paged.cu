@@ -86,6 +86,20 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of w
 #define I4KV_PV_TWO_CHAINS 0
 #endif
 
+// Share of a warp pair's run each warp takes unasked, in eighths (the rest
+// is claimed page by page), for float32 and for 16-bit value pools. Measured
+// side by side on one B200 (float32): 3/8 against 2/8 and 0 (every page
+// claimed) -- config 0 61.2 / 61.8 / 62.1 us, cfg2 L=512 29.1 / 29.2 / 30.0,
+// cfg2 L=8192 193.6 / 194.1 / 194.5, cfg3 d64 757 / 767 / 804, cfg3 d128
+// 1432 / 1429 / 1445; 16-bit values at config 0: 46.5 (3/8), 47.2 (2/8),
+// 49.1 (0) -- a claim sits on the page's dependency chain.
+#ifndef I4KV_PAIR_OWN_EIGHTHS_F32
+#define I4KV_PAIR_OWN_EIGHTHS_F32 3
+#endif
+#ifndef I4KV_PAIR_OWN_EIGHTHS_16
+#define I4KV_PAIR_OWN_EIGHTHS_16 3
+#endif
+
 // Pages in flight per warp of a GQA ring group (the ring holds gs times this).
 #ifndef I4KV_GQA_RING_PAGES_PER_WARP
 #define I4KV_GQA_RING_PAGES_PER_WARP 1
@@ -593,10 +607,11 @@ paged_decode_kernel(DecodeArgs a) {
   auto page_at = [&](int i) -> int { return bwd ? g1 - 1 - i : g0 + i; };
   const int gfirst = bwd ? g1 - 1 : g0;
   int n = g1 - g0;
-  // Each warp of a pair takes the first 3/8 of the run from its end without
-  // asking; only the middle quarter is claimed page by page (enough to absorb
-  // page rates 25 % apart), so most pages cost no claim.
-  const int n_own = paired ? (int)(((long long)n * 3) / 8) : n;
+  // Each warp of a pair takes a share of the run from its end without asking
+  // (3/8 each, leaving a middle quarter -- enough to absorb page rates 25 %
+  // apart -- so most pages cost no claim); the rest is claimed page by page.
+  constexpr int kOwnEighths = VK == 0 ? I4KV_PAIR_OWN_EIGHTHS_F32 : I4KV_PAIR_OWN_EIGHTHS_16;
+  const int n_own = paired ? (int)(((long long)n * kOwnEighths) / 8) : n;
   // Claims are pipelined: after a claim succeeds, lane 0 sends the next one at
   // once and its answer is read when that page is due, so the shared-memory
   // atomic's round trip overlaps a page of work. Claims go in page order, so
