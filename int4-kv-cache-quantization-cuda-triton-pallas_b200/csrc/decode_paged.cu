@@ -520,7 +520,7 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
 // page's codes are loaded into A fragments once and each value row once for all
 // heads. HW = 1 is plain one-head-per-warp decoding.
 template <int D, int WARPS, int STAGES, int VK, int HW>
-__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? 3 : 1) : (HW > 1 ? 3 : 4))
+__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? (HW >= 4 ? 2 : 3) : 1) : (HW > 1 ? 3 : 4))
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
@@ -561,7 +561,7 @@ paged_decode_kernel(DecodeArgs a) {
   // forward from the run's start, the second backward from its end, each
   // claiming its next page from the pair's shared claim word, so the pair
   // finishes together however its two warps' page rates differ.
-  const bool paired = HW == 1 && (WARPS % 2 == 0) && STAGES >= 2 && gs == 1 && !xmode && a.part_out == nullptr;
+  const bool paired = (WARPS % 2 == 0) && STAGES >= 2 && gs == 1 && !xmode && a.part_out == nullptr;
   const bool bwd = paired && (warp & 1);
   uint64_t* bar = bars + gi * depth;
   if (leader && lane == 0) {  // ordered before every wait by the barriers of the length prefix
@@ -777,6 +777,7 @@ paged_decode_kernel(DecodeArgs a) {
   // written by other SMs, often on the other die); rounds combine online in
   // float64. The loops stay rolled: this code runs once per warp, at the end
   // of the launch, where every branch target and constant is fetched cold.
+  bool keep_last_slot = false;  // a pair partner still reads this warp's last ring slot
   auto merge_stream = [&](int stream, long long w_lo, long long w_hi) {
     constexpr int MC = 8;  // records per round: (m, l) in lanes 0..7, values staged in shared memory
     // the warp's staging area: a ring slot, free once the group's run is over
@@ -854,6 +855,103 @@ paged_decode_kernel(DecodeArgs a) {
     }
   };
 
+  // The same merge for a warp serving HW > 1 heads: a contributor's HW records
+  // are adjacent, so each round stages whole contributors (every head's record,
+  // headers included) with one set of 16-byte asynchronous copies, and lane
+  // j * HW + h takes the (m, l) of contributor j's head h from the staged
+  // copy. A round thus costs one round trip to L2 for all heads, where a round
+  // per head would cost HW. Contributors per round: as many as the warp's free
+  // ring bytes hold, at most 32 / HW.
+  auto merge_stream_heads = [&](int stream, long long w_lo, long long w_hi) {
+    constexpr int REC = C::REC_BYTES;
+    char* stage = ring + (size_t)(gj % depth) * sb;
+    // bytes of the ring this warp owns, less a last slot its pair partner may still read
+    const int cap = gs == 1 ? (keep_last_slot ? depth - 1 : depth) * sb : sb;
+    const int per = min(32 / HW, cap / (HW * REC));
+    const bool all_run = T >= NU;
+    double M = -INFINITY, L = 0.0;  // running (m, l) of head lane % HW
+    double O[HW][DPL];
+#pragma unroll
+    for (int h = 0; h < HW; ++h)
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) O[h][k] = 0.0;
+#pragma unroll 1
+    for (long long base = w_lo; base <= w_hi; base += per) {
+      const int cnt = (int)min((long long)per, w_hi - base + 1);
+#pragma unroll 1
+      for (int j = 0; j < cnt; ++j) {
+        const char* src = recs + (((size_t)(base + j + stream) * gs + gj) * HW) * REC;
+        for (int u = 16 * lane; u < HW * REC; u += 512) cp_async16(stage + j * HW * REC + u, src + u);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncwarp();
+      const int jl = lane / HW;
+      const long long wj = base + jl;
+      const bool okj = jl < cnt && (all_run || floor_div_s52(wj * T, NU) != floor_div_s52((wj + 1) * T, NU));
+      double mj = -INFINITY, lj = 0.0;
+      if (okj) {
+        const char* r = stage + (size_t)lane * REC;  // contributor jl, head lane % HW
+        mj = *reinterpret_cast<const double*>(r);
+        lj = *reinterpret_cast<const double*>(r + 8);
+      }
+      double cm = mj;
+#pragma unroll
+      for (int o = HW; o < 32; o <<= 1) cm = fmax(cm, __shfl_xor_sync(kFull, cm, o));
+      const double m_new = fmax(M, cm);
+      double c = 1.0, ej = 0.0;
+      if (m_new != -INFINITY) {
+        c = M != -INFINITY ? exp_nonpos(M - m_new) : 0.0;
+        ej = (okj && mj != -INFINITY) ? exp_nonpos(mj - m_new) : 0.0;
+      }
+      double lc = lj * ej;
+#pragma unroll
+      for (int o = HW; o < 32; o <<= 1) lc += __shfl_xor_sync(kFull, lc, o);
+      L = m_new != -INFINITY ? fma(L, c, lc) : L;
+#pragma unroll
+      for (int h = 0; h < HW; ++h) {
+        const double ch = __shfl_sync(kFull, c, h);
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) O[h][k] *= ch;
+      }
+      // branch-free, so the loads and shuffles of a contributor's heads issue
+      // together; a record with weight 0 (an empty run's, never written) is
+      // replaced by zeros before it can reach the sum
+#pragma unroll 1
+      for (int j = 0; j < cnt; ++j) {
+        double e[HW];
+        float v[HW][DPL];
+#pragma unroll
+        for (int h = 0; h < HW; ++h) {
+          e[h] = __shfl_sync(kFull, ej, j * HW + h);
+          load_lane_vec_smem<D>(reinterpret_cast<const float*>(stage + (size_t)(j * HW + h) * REC + 16), v[h], lane);
+        }
+#pragma unroll
+        for (int h = 0; h < HW; ++h)
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) O[h][k] = fma(e[h] != 0.0 ? (double)v[h][k] : 0.0, e[h], O[h][k]);
+      }
+      __syncwarp();  // the stage is read before the next round's copies
+      M = m_new;
+    }
+#pragma unroll
+    for (int h = 0; h < HW; ++h) {
+      const double Mh = __shfl_sync(kFull, M, h), Lh = __shfl_sync(kFull, L, h);
+      const size_t qstream = ((size_t)stream * gs + gj) * HW + h;
+      float o[DPL];
+      if (a.part_out) {  // the merged (M, L, O) of this launch's share of the stream
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) o[k] = (float)O[h][k];
+        put_record(a.part_out + qstream * C::REC_BYTES, Mh, Lh, o);
+        continue;
+      }
+      const double rden = rcp_f64(fmax(Lh, 1e-10));
+#pragma unroll
+      for (int k = 0; k < DPL; ++k) o[k] = (float)(O[h][k] * rden);
+      store_lane_vec<D>(a.out + qstream * D, o, lane);
+    }
+  };
+
   // The warp's first segment, when its stream is shared with earlier warps and
   // ends inside this run: its record is stored and its arrival counted as soon
   // as the segment ends; the arrival's ticket (the counter's old value) is
@@ -895,13 +993,14 @@ paged_decode_kernel(DecodeArgs a) {
     if (seg_stream >= 0) n_cur = contributors_of(seg_stream, lo_c, hi_c);
     // A pair's meeting point m splits its run: the forward warp took [g0, m),
     // the backward one [m, g1). When both warps' last segments lie in the same
-    // stream, each leaves its partial in its ring's last slot (free now; the
-    // merges below stage in slot 0) and the second to arrive merges the two;
+    // stream, each leaves its partial(s) in its ring's last slot (free now;
+    // the merges below stage in the slots before it while the partner may
+    // still read it) and the second to arrive merges the two;
     // that stream then counts as one contributor of the pair, like every other
     // stream of the run.
     bool have_cur = seg_stream >= 0;  // this warp holds the last segment's state
     bool pair_merged = false;         // ... merged with the partner's (in pm, pl, po)
-    double pm = 0.0, pl = 0.0, po[DPL];
+    double pm[HW], pl[HW], po[HW][DPL];
     if (paired && have_cur) {
       const int m = bwd ? g1 - n : g0 + n;
       bool split = false;
@@ -911,11 +1010,16 @@ paged_decode_kernel(DecodeArgs a) {
         split = b * a.vheads + h == seg_stream;
       }
       if (split) {
-        float o[DPL];
+        float o[HW][DPL];
+        double lsum[HW], mh[HW];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) o[k] = __fsub_rn(acc[0][k], acc_c[0][k]);
-        const double lsum = lane_sum(0);
-        put_record(ring + (size_t)(depth - 1) * sb, m_run[0], lsum, o);
+        for (int h = 0; h < HW; ++h) {
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) o[h][k] = __fsub_rn(acc[h][k], acc_c[h][k]);
+          lsum[h] = head_l(h);
+          mh[h] = head_m(h);
+          put_record(ring + (size_t)(depth - 1) * sb + (size_t)h * C::REC_BYTES, mh[h], lsum[h], o[h]);
+        }
         __threadfence_block();
         __syncwarp();
         int arrived = 0;
@@ -923,30 +1027,38 @@ paged_decode_kernel(DecodeArgs a) {
         arrived = __shfl_sync(kFull, arrived, 0);
         if (arrived == 0) {
           have_cur = false;  // the partner finishes the stream
+          keep_last_slot = true;  // ... reading this warp's record from its last ring slot
         } else {
           __threadfence_block();
           __syncwarp();
           const char* other = stages + ((size_t)(warp ^ 1) * depth + depth - 1) * sb;
-          const double m2 = *reinterpret_cast<const double*>(other);
-          const double l2 = *reinterpret_cast<const double*>(other + 8);
-          float o2[DPL];
-          load_lane_vec_smem<D>(reinterpret_cast<const float*>(other + 16), o2, lane);
-          pm = fmax(m_run[0], m2);
-          const double e1 = exp_nonpos(m_run[0] - pm), e2 = exp_nonpos(m2 - pm);
-          pl = fma(lsum, e1, l2 * e2);
 #pragma unroll
-          for (int k = 0; k < DPL; ++k) po[k] = fma((double)o[k], e1, (double)o2[k] * e2);
+          for (int h = 0; h < HW; ++h) {
+            const char* oh = other + (size_t)h * C::REC_BYTES;
+            const double m2 = *reinterpret_cast<const double*>(oh);
+            const double l2 = *reinterpret_cast<const double*>(oh + 8);
+            float o2[DPL];
+            load_lane_vec_smem<D>(reinterpret_cast<const float*>(oh + 16), o2, lane);
+            pm[h] = fmax(mh[h], m2);
+            const double e1 = exp_nonpos(mh[h] - pm[h]), e2 = exp_nonpos(m2 - pm[h]);
+            pl[h] = fma(lsum[h], e1, l2 * e2);
+#pragma unroll
+            for (int k = 0; k < DPL; ++k) po[h][k] = fma((double)o[h][k], e1, (double)o2[k] * e2);
+          }
           pair_merged = true;
         }
       }
     }
     if (have_cur && n_cur == 1) {  // the stream lies inside this run (or pair): finish it here
       if (pair_merged) {
-        const double rden = rcp_f64(fmax(pl, 1e-10));
-        float o[DPL];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) o[k] = (float)(po[k] * rden);
-        store_lane_vec<D>(a.out + (size_t)seg_stream * D, o, lane);
+        for (int h = 0; h < HW; ++h) {
+          const double rden = rcp_f64(fmax(pl[h], 1e-10));
+          float o[DPL];
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) o[k] = (float)(po[h][k] * rden);
+          store_lane_vec<D>(a.out + ((size_t)seg_stream * HW + h) * D, o, lane);
+        }
       } else {
         finish_alone(seg_stream);
       }
@@ -963,10 +1075,13 @@ paged_decode_kernel(DecodeArgs a) {
     bool last_cur = false;
     if (pub_cur) {
       if (pair_merged) {
-        float o[DPL];
 #pragma unroll
-        for (int k = 0; k < DPL; ++k) o[k] = (float)po[k];
-        put_record(recs + (size_t)(gu + seg_stream) * C::REC_BYTES, pm, pl, o);
+        for (int h = 0; h < HW; ++h) {
+          float o[DPL];
+#pragma unroll
+          for (int k = 0; k < DPL; ++k) o[k] = (float)po[h][k];
+          put_record(recs + ((size_t)(gu + seg_stream) * HW + h) * C::REC_BYTES, pm[h], pl[h], o);
+        }
       } else {
 #pragma unroll
         for (int h = 0; h < HW; ++h) {
@@ -997,7 +1112,8 @@ paged_decode_kernel(DecodeArgs a) {
       if (!(t == 0 ? last_held : last_cur)) continue;
       long long lo = lo_c, hi = hi_c;
       if (t == 0) contributors_of(held_stream, lo, hi);
-      merge_stream(t == 0 ? held_stream : seg_stream, lo, hi);
+      if constexpr (HW > 1) merge_stream_heads(t == 0 ? held_stream : seg_stream, lo, hi);
+      else merge_stream(t == 0 ? held_stream : seg_stream, lo, hi);
     }
   };
 
@@ -1433,25 +1549,26 @@ constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 constexpr int kMaxCtasF32 = I4KV_DECODE_MAX_CTAS_F32;
 constexpr int kMaxCtas16 = I4KV_DECODE_MAX_CTAS_16;
 
-// Query heads per warp for GQA ratio g at head dim d: 4 when 4 divides g (up
-// to d128: the per-head registers of d256 do not fit), 2 when 2 does, else 1.
-// The fused split exchange runs one head per warp.
-// Measured at config 0's shape with 32 query heads (G = 2, 4, 8, 32), float32
-// values, L2 flushed: one head per warp 45.0 us for every G; two heads per
-// warp 45.0-49.9 us; four heads per warp 65.6-69.1 us (column heads; 71-72 us
-// with one head per MMA column block) -- a warp serving 4 heads takes a
-// quarter of the pages, so its run of ~7 pages is dominated by the run's
-// fixed costs (first page, digits of 4 heads, 4 heads of record merges).
-// Default: one head per warp; the multi-head kernels are compiled only when
-// this is raised.
+// Query heads per warp for GQA ratio g at head dim d: all of a kv head's
+// queries when g is 2, or 4 at d <= 128 (the per-head registers of d256 do
+// not fit four), so a warp stages, unpacks and reads each kv page once for
+// them and warps pair up on one run; otherwise one head per warp, the warps
+// of a ring group sharing each staged page. The fused split exchange runs one
+// head per warp.
+// Measured at config 0's shape with 32 query heads, L2 flushed (one B200):
+// G = 4: 43.0 us (float32 values) / 41.1 us (float16) with four heads per
+// warp against 45.1 / 45.1 us with one; G = 2: 41.0 us with two against 45;
+// G = 8 as two-warp groups of four heads: 45-56 us against 43.2 us with one
+// head per warp in four-warp ring groups (no warp pairs in a ring group, and
+// each stream's many records are merged by one warp at the end).
 #ifndef I4KV_MAX_HEADS_PER_WARP
-#define I4KV_MAX_HEADS_PER_WARP 1
+#define I4KV_MAX_HEADS_PER_WARP 4
 #endif
 int heads_per_warp(int g, int d, bool xmode) {
   constexpr int kMaxHw = I4KV_MAX_HEADS_PER_WARP;
   if (xmode) return 1;
-  if (kMaxHw >= 4 && g % 4 == 0 && d <= 128) return 4;
-  if (kMaxHw >= 2 && g % 2 == 0) return 2;
+  if (kMaxHw >= 4 && g == 4 && d <= 128) return 4;
+  if (kMaxHw >= 2 && g == 2) return 2;
   return 1;
 }
 
