@@ -322,17 +322,23 @@ def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, 
 
 def sweep_records(torch, lib, C, W, K, flush, peak):
     """The other decode configurations of the benchmark definition on this GPU:
-    config 2's context sweep and config 3's ragged batch (d64, d128)."""
+    config 2's context sweep and config 3's ragged batch (d64, d128); then
+    config 0's shape with grouped-query heads (32 query heads over 8 and 4 kv
+    heads) and with 16-bit value pools."""
     recs = {}
-    for name in ("cfg2_512", "cfg2_8192", "cfg2_32768", "cfg3_d64", "cfg3_d128"):
+    runs = [(n, n, torch.float32) for n in ("cfg2_512", "cfg2_8192", "cfg2_32768", "cfg3_d64",
+                                            "cfg3_d128", "cfg0_gqa4", "cfg0_gqa8")]
+    runs += [("cfg0_f16", "cfg0", torch.float16), ("cfg0_bf16", "cfg0", torch.bfloat16)]
+    for label, name, vdtype in runs:
         shape = W.config_shape(name)
-        prob = W.torch_build_cache(shape, seed=7)
-        r = decode_timing(torch, lib, C, shape, prob, torch.float32, K, flush, seed=1)
+        shape.value_bytes = 4 if vdtype == torch.float32 else 2
+        prob = W.torch_build_cache(shape, seed=7, value_dtype=vdtype)
+        r = decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, seed=1)
         nbytes = shape.algorithmic_bytes()
         r.update({"algorithmic_bytes": nbytes,
                   "gbs": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9, 1),
                   "frac": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9 / peak, 4)})
-        recs[name] = r
+        recs[label] = r
         del prob
         torch.cuda.synchronize()
         torch.cuda.empty_cache()

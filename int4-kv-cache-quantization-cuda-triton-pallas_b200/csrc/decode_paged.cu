@@ -1549,33 +1549,35 @@ constexpr int kStages = I4KV_DECODE_STAGES;  // ring slots per warp
 constexpr int kMaxCtasF32 = I4KV_DECODE_MAX_CTAS_F32;
 constexpr int kMaxCtas16 = I4KV_DECODE_MAX_CTAS_16;
 
-// Query heads per warp for GQA ratio g at head dim d: all of a kv head's
-// queries when g is 2, or 4 at d <= 128 (the per-head registers of d256 do
-// not fit four), so a warp stages, unpacks and reads each kv page once for
-// them and warps pair up on one run; otherwise one head per warp, the warps
-// of a ring group sharing each staged page. The fused split exchange runs one
-// head per warp.
+// Query heads per warp for GQA ratio g at head dim d: four when 4 divides g
+// (at d <= 128: the per-head registers of d256 do not fit four), else two
+// when 2 does, so a warp stages, unpacks and reads each kv page once for
+// those heads, and warps pair up on one run as in plain decode; otherwise one
+// head per warp, the warps of a ring group sharing each staged page. The
+// fused split exchange runs one head per warp.
 // Measured at config 0's shape with 32 query heads, L2 flushed (one B200):
-// G = 4: 43.0 us (float32 values) / 41.1 us (float16) with four heads per
-// warp against 45.1 / 45.1 us with one; G = 2: 41.0 us with two against 45;
-// G = 8 as two-warp groups of four heads: 45-56 us against 43.2 us with one
-// head per warp in four-warp ring groups (no warp pairs in a ring group, and
-// each stream's many records are merged by one warp at the end).
+// G = 4: 39.9 us (float32 values) with four heads per warp against 45.1 us
+// with one; G = 2: 41.0 us with two against 45. Groups of four-head warps
+// sharing a page (G = 8 as two-warp groups) measured 45-56 us: no warp pairs
+// in a ring group, and each stream's many records are merged by one warp at
+// the end; so multi-head warps run alone, one run of pages per pair.
 #ifndef I4KV_MAX_HEADS_PER_WARP
 #define I4KV_MAX_HEADS_PER_WARP 4
 #endif
 int heads_per_warp(int g, int d, bool xmode) {
   constexpr int kMaxHw = I4KV_MAX_HEADS_PER_WARP;
   if (xmode) return 1;
-  if (kMaxHw >= 4 && g == 4 && d <= 128) return 4;
-  if (kMaxHw >= 2 && g == 2) return 2;
+  if (kMaxHw >= 4 && g % 4 == 0 && d <= 128) return 4;
+  if (kMaxHw >= 2 && g % 2 == 0) return 2;
   return 1;
 }
 
-// Warps sharing one ring: the largest divisor of kWarps (a power of two) that
-// divides g / hw, so a CTA holds whole groups of query heads.
+// Warps sharing one ring: one for multi-head warps; else the largest divisor
+// of kWarps (a power of two) that divides g, so a CTA holds whole groups of
+// query heads.
 int ring_group(int num_q_heads, int num_kv_heads, int hw) {
-  const int g = num_q_heads / num_kv_heads / hw;
+  if (hw > 1) return 1;
+  const int g = num_q_heads / num_kv_heads;
   int x = kWarps;
   while (g % x) x >>= 1;
   return x;
