@@ -144,3 +144,39 @@ def test_benchmark_config_full_size(name):
     check_streams(out, query, cache, bt, sl, streams)
     del cache, out
     _release()
+
+
+@pytest.mark.parametrize("name", ["cfg0_gqa2", "cfg0_gqa4", "cfg0_gqa8", "cfg0_gqa32"])
+def test_grouped_query_full_size(name):
+    """Config 0's shape with 32 query heads over 16 / 8 / 4 / 1 kv heads: every
+    (sequence, kv head) stream, all of its query heads, against the fp32 oracle
+    and the float64 arbiter. Covers the warps serving two (G = 2) and four
+    (G = 4, 8, 32) query heads each, paired on one run, with the multi-head
+    record merge."""
+    shape, cache, query, bt, sl, out = _run(name, seed=21)
+    assert torch.isfinite(out).all()
+    G = shape.query_heads // shape.heads
+    streams = [(b, h) for b in range(shape.batch) for h in range(shape.heads)]
+    r = check_streams(out, query, cache, bt, sl, streams, group_q=G)
+    assert len(r["oracle_off"]) <= max(2, len(streams) * G // 16), r["oracle_off"]
+    del cache, out
+    _release()
+
+
+@pytest.mark.parametrize("vdtype", ["float16", "bfloat16"])
+def test_config0_values16_full_size(vdtype):
+    """Config 0 with the value pool stored as float16 / bfloat16 (rounded to
+    nearest even by the cache writer; the oracle reads the stored values
+    widened to float32): a seeded sample of 64 streams."""
+    shape = W.config_shape("cfg0")
+    shape.value_bytes = 2
+    prob = W.torch_build_cache(shape, seed=31, value_dtype=getattr(torch, vdtype))
+    cache, query = prob["cache"], prob["query"]
+    ids = list(range(shape.batch))
+    bt, sl = cache.block_table(ids)
+    out = cache.decode(query, ids)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    check_streams(out, query, cache, bt, sl, _sample(shape, 64, seed=5))
+    del cache, out
+    _release()
