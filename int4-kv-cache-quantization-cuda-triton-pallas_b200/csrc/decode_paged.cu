@@ -8,11 +8,12 @@
 // 1/sqrt(d)), keys dequantized as code*scale - zp*scale with the scale/zp of the key's
 // 128-token group, output o / max(l, 1e-10); empty streams give exact zeros.
 //
-// Ring groups (GQA): gs = gcd(G, WARPS) warps share one ring of staged pages
-// and serve gs query heads of the same kv head from it, so a kv page crosses
-// HBM once for those gs queries; each warp still does its own query's logits,
-// softmax and P.V on the page (at config-0 sizes that work, not HBM, sets the
-// pace of a GQA step).
+// Grouped queries (GQA): when 4 (or 2) divides G, each warp serves HW = 4 (2)
+// query heads of one kv head: it stages, unpacks and reads each kv page once
+// for them, the heads' logits coming from one set of code fragments. For odd
+// G, ring groups: gs = gcd(G, WARPS) one-head warps share one ring of staged
+// pages, so a kv page crosses HBM once for those gs queries, and each warp
+// does its own query's logits, softmax and P.V on the page.
 //
 // Work decomposition (stream-K over pages): the page-heads of all page
 // streams (b, kv-head group) are laid end to end -- T of them -- and the
