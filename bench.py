@@ -324,10 +324,12 @@ def sweep_records(torch, lib, C, W, K, flush, peak):
     """The other decode configurations of the benchmark definition on this GPU:
     config 2's context sweep and config 3's ragged batch (d64, d128); then
     config 0's shape with grouped-query heads (32 query heads over 8 and 4 kv
-    heads) and with 16-bit value pools."""
+    heads), the same at 32768 tokens (over 8 kv heads), and config 0 with
+    16-bit value pools."""
     recs = {}
     runs = [(n, n, torch.float32) for n in ("cfg2_512", "cfg2_8192", "cfg2_32768", "cfg3_d64",
-                                            "cfg3_d128", "cfg0_gqa4", "cfg0_gqa8")]
+                                            "cfg3_d128", "cfg0_gqa4", "cfg0_gqa8",
+                                            "cfg2_32768_gqa4")]
     runs += [("cfg0_f16", "cfg0", torch.float16), ("cfg0_bf16", "cfg0", torch.bfloat16)]
     for label, name, vdtype in runs:
         shape = W.config_shape(name)

@@ -83,9 +83,14 @@ def config_shape(name: str, seed: int = 0) -> DecodeShape:
         if G <= 0 or 32 % G:
             raise ValueError(f"unknown config {name}")
         return DecodeShape(8, 32 // G, 128, [2048] * 8, pool_pages=8 * 128, q_heads=32)
-    if name.startswith("cfg2_"):
-        L = int(name.split("_")[1])
-        return DecodeShape(8, 32, 128, [L] * 8, pool_pages=8 * ((L + 15) // 16))
+    if name.startswith("cfg2_"):  # cfg2_<L>, or cfg2_<L>_gqa<G>: 32 query heads over 32 / G
+        parts = name.split("_")
+        L = int(parts[1])
+        G = int(parts[2][len("gqa"):]) if len(parts) > 2 and parts[2].startswith("gqa") else 1
+        if G <= 0 or 32 % G:
+            raise ValueError(f"unknown config {name}")
+        return DecodeShape(8, 32 // G, 128, [L] * 8, pool_pages=8 * ((L + 15) // 16),
+                           q_heads=32 if G > 1 else None)
     if name.startswith("cfg3_d"):
         d = int(name[len("cfg3_d"):])
         rng = np.random.default_rng(seed)
