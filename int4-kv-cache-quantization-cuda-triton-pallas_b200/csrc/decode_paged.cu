@@ -1308,8 +1308,10 @@ paged_decode_kernel(DecodeArgs a) {
             for (int k = 0; k < 4; ++k)
               cs[0][0][k] = (cs[0][0][k] + cs[0][1 % NCH][k]) + (cs[0][2 % NCH][k] + cs[0][3 % NCH][k]);
           }
-          double x0 = fma((double)cs[0][0][1], w1[0], (double)cs[0][0][0] * w0[0]);
-          double x1 = fma((double)cs[0][0][3], w1[0], (double)cs[0][0][2] * w0[0]);
+          // digits 2ft, 2ft + 1 weigh 128 w1 and w1: their int32 combination is
+          // exact (|sum| < 2^25), so this is the float64 value of both terms
+          double x0 = (double)(cs[0][0][0] * 128 + cs[0][0][1]) * w1[0];
+          double x1 = (double)(cs[0][0][2] * 128 + cs[0][0][3]) * w1[0];
           x0 += __shfl_xor_sync(kFull, x0, 1);
           x1 += __shfl_xor_sync(kFull, x1, 1);
           x0 += __shfl_xor_sync(kFull, x0, 2);
@@ -1344,11 +1346,11 @@ paged_decode_kernel(DecodeArgs a) {
           constexpr double kStep = HW == 4 ? 0x1p-14 : 0x1p-28;  // 2^(-7 * 8 / HW)
 #pragma unroll
           for (int pp = 0; pp < HW; ++pp) {
-            const double wb = wa * 0.0078125;  // the column's second digit: 2^-7 lower
-            x0 = fma((double)cs[pp][0][0], wa, x0);
-            x0 = fma((double)cs[pp][0][1], wb, x0);
-            x1 = fma((double)cs[pp][0][2], wa, x1);
-            x1 = fma((double)cs[pp][0][3], wb, x1);
+            // the column's two digits (the second 2^-7 lower), combined exactly
+            // in int32 (|sum| < 2^25) and weighed once
+            const double wb = wa * 0.0078125;
+            x0 = fma((double)(cs[pp][0][0] * 128 + cs[pp][0][1]), wb, x0);
+            x1 = fma((double)(cs[pp][0][2] * 128 + cs[pp][0][3]), wb, x1);
             wa *= kStep;
           }
           if constexpr (HW == 2) {  // lanes ft and ft ^ 1 hold complementary digits of a head
@@ -1435,7 +1437,8 @@ paged_decode_kernel(DecodeArgs a) {
 #pragma unroll
         for (int h = 0; h < HW; ++h)
 #pragma unroll
-          for (int k = 0; k < DPL; ++k) kahan_rescale_add(acc[h][k], acc_c[h][k], 1.f, ps[h][k]);
+          for (int k = 0; k < DPL; k += 2)
+            kahan_add2(acc[h][k], acc[h][k + 1], acc_c[h][k], acc_c[h][k + 1], ps[h][k], ps[h][k + 1]);
       }
 
     }
