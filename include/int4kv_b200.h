@@ -140,7 +140,10 @@ cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* to
  * Replaces the attention call of the reference's decode path
  * (src/ops.py:176-253 -> csrc/flash_decode_int4.cu:104-221) for distinct
  * per-(sequence, head) KV streams. `status` (nullable) collects
- * INT4KV_STATUS_* bits. */
+ * INT4KV_STATUS_* bits. `out` may also be the device pointer of mapped
+ * pinned host memory (cudaHostAlloc with cudaHostAllocMapped): every output
+ * row is stored once, with plain stores, so the result reaches the host
+ * without a separate device-to-host copy. */
 cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
                                                int head_dim, size_t* bytes);
 cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const float* v_pool,
