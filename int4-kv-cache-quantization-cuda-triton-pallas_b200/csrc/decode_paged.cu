@@ -101,6 +101,12 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of w
 #define I4KV_PAIR_OWN_EIGHTHS_16 3
 #endif
 
+// Minimum resident CTAs per SM the compiler plans registers for, for warps
+// serving several query heads over 16-bit value pools.
+#ifndef I4KV_MULTIHEAD16_MIN_CTAS
+#define I4KV_MULTIHEAD16_MIN_CTAS 3
+#endif
+
 // Pages in flight per warp of a GQA ring group (the ring holds gs times this).
 #ifndef I4KV_GQA_RING_PAGES_PER_WARP
 #define I4KV_GQA_RING_PAGES_PER_WARP 1
@@ -521,7 +527,8 @@ __device__ __forceinline__ void x_empty_streams(const DecodeArgs& a, const int* 
 // page's codes are loaded into A fragments once and each value row once for all
 // heads. HW = 1 is plain one-head-per-warp decoding.
 template <int D, int WARPS, int STAGES, int VK, int HW>
-__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? (HW >= 4 ? 2 : 3) : 1) : (HW > 1 ? 3 : 4))
+__global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? (HW >= 4 ? 2 : 3) : 1)
+                                                       : (HW > 1 ? I4KV_MULTIHEAD16_MIN_CTAS : 4))
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
@@ -702,14 +709,28 @@ paged_decode_kernel(DecodeArgs a) {
 
   // Warps [w_lo, w_hi] whose runs touch `stream`; returns how many of them
   // hold a non-empty run (those are the stream's contributors).
-  auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
+  // ... and the stream's pages [g_lo, g_hi) of the end-to-end order.
+  auto stream_span = [&](int stream, long long& w_lo, long long& w_hi, int& g_lo, int& g_hi) -> int {
     const int b = stream / a.vheads, h = stream - b * a.vheads;
     const int np = s_pfx[b + 1] - s_pfx[b];
     const long long gs0 = (long long)a.vheads * s_pfx[b] + (long long)h * np, ge = gs0 + np;
+    g_lo = (int)gs0;
+    g_hi = (int)ge;
     w_lo = floor_div_s52((gs0 + 1) * NU - 1, T);
     w_hi = floor_div_s52(ge * NU - 1, T);
     return (T >= NU) ? (int)(w_hi - w_lo + 1) : np;
   };
+  auto contributors_of = [&](int stream, long long& w_lo, long long& w_hi) -> int {
+    int g_lo, g_hi;
+    return stream_span(stream, w_lo, w_hi, g_lo, g_hi);
+  };
+  // Multi-head warps: the current segment's contributors and pages, worked out
+  // when the segment starts, so the end of the run (on the launch's critical
+  // path) does no index arithmetic. Measured side by side on one B200 (means
+  // of 22 launches): GQA-4 at config 0 39.0 -> 37.8 us; one-head warps keep
+  // the end-of-run arithmetic (their registers are tighter: config 0 61.1 vs
+  // 62.2 us with it).
+  int seg_nc = 0, seg_g0 = 0, seg_g1 = 0, seg_wlo = 0, seg_whi = -1;  // unit indices < 2^31
 
   // Warp-wide sum of head h's lane denominators (float32 sum minus compensation).
   auto lane_sum = [&](int h) -> double {
@@ -991,7 +1012,15 @@ paged_decode_kernel(DecodeArgs a) {
   auto end_run = [&]() {
     long long lo_c = 0, hi_c = -1;
     int n_cur = 0;
-    if (seg_stream >= 0) n_cur = contributors_of(seg_stream, lo_c, hi_c);
+    if (seg_stream >= 0) {
+      if constexpr (HW > 1) {
+        n_cur = seg_nc;
+        lo_c = seg_wlo;
+        hi_c = seg_whi;
+      } else {
+        n_cur = contributors_of(seg_stream, lo_c, hi_c);
+      }
+    }
     // A pair's meeting point m splits its run: the forward warp took [g0, m),
     // the backward one [m, g1). When both warps' last segments lie in the same
     // stream, each leaves its partial(s) in its ring's last slot (free now;
@@ -1005,7 +1034,11 @@ paged_decode_kernel(DecodeArgs a) {
     if (paired && have_cur) {
       const int m = bwd ? g1 - n : g0 + n;
       bool split = false;
-      if (bwd ? m > g0 : m < g1) {
+      if constexpr (HW > 1) {
+        // the partner's page next to the meeting point (m for the forward
+        // warp, m - 1 for the backward one) lies in this warp's last stream
+        split = bwd ? (m > g0 && m - 1 >= seg_g0) : (m < g1 && m < seg_g1);
+      } else if (bwd ? m > g0 : m < g1) {
         int b, h, p, np;
         locate_page(a, s_pfx, bwd ? m - 1 : m, b, h, p, np);
         split = b * a.vheads + h == seg_stream;
@@ -1145,6 +1178,12 @@ paged_decode_kernel(DecodeArgs a) {
       if (has_q) {
         if (seg_stream >= 0) end_segment(seg_stream);
         seg_stream = d.stream;
+        if constexpr (HW > 1) {
+          long long wl, wh;
+          seg_nc = stream_span(seg_stream, wl, wh, seg_g0, seg_g1);
+          seg_wlo = (int)wl;
+          seg_whi = (int)wh;
+        }
 #pragma unroll
         for (int h = 0; h < HW; ++h) {
           m_run[h] = -INFINITY;
