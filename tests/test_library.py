@@ -152,3 +152,22 @@ def test_split_decode_layout_and_argument_checks(lib):
     assert call(odd, 2, 0) == CUDA_ERROR_INVALID_VALUE      # a peer buffer not 128-byte aligned
     empty = (ctypes.c_void_p * 2)(1 << 20, 0)
     assert call(empty, 2, 1) == CUDA_ERROR_INVALID_VALUE    # a missing peer buffer
+
+
+def test_benchmark_config_shapes():
+    """The benchmark's decode configurations by name, including the grouped-
+    query forms at config 0's and config 2's shapes."""
+    W = pkg("workloads")
+    s = W.config_shape("cfg0")
+    assert (s.batch, s.heads, s.query_heads, s.head_dim, s.seq_lens[0]) == (8, 32, 32, 128, 2048)
+    assert s.algorithmic_bytes() == 306450432
+    g = W.config_shape("cfg0_gqa4")
+    assert (g.heads, g.query_heads) == (8, 32)
+    l = W.config_shape("cfg2_32768_gqa4")
+    assert (l.batch, l.heads, l.query_heads, l.seq_lens[0]) == (8, 8, 32, 32768)
+    assert l.pool_pages == 8 * 2048
+    m = W.config_shape("cfg2_512")
+    assert (m.heads, m.query_heads, m.seq_lens[0]) == (32, 32, 512)
+    for bad in ("cfg2_512_gqa5", "cfg0_gqa3", "cfg9"):
+        with pytest.raises(ValueError):
+            W.config_shape(bad)
