@@ -1,6 +1,6 @@
 """Paged decode where the warp pairs' runs hold many stream boundaries.
 
-One-warp-per-ring decodes run as warp pairs: two warps share one stream-K run
+Decodes without ring groups run as warp pairs: two warps share one stream-K run
 from both ends, claim its middle pages through a shared-memory word, and merge
 the stream that holds their meeting point through shared memory. These cases
 put many short ragged streams (some empty, some of one token, some page
@@ -39,7 +39,7 @@ def _lens(kind, seed):
     return [int(n) for n in lens]
 
 
-def _check(lens, heads, d, value_dtype, seed):
+def _check(lens, heads, d, value_dtype, seed, q_heads=None):
     g = torch.Generator(device="cuda").manual_seed(seed)
     cache = P.PagedKVCache(sum((n + 15) // 16 for n in lens) + 8, heads, d, device="cuda",
                            seed=seed, value_dtype=value_dtype)
@@ -51,7 +51,7 @@ def _check(lens, heads, d, value_dtype, seed):
         vs.append(torch.randn((n, heads, d), generator=g, device="cuda"))
     ids = list(range(len(lens)))
     cache.write_sequences(ids, ks, vs)
-    q = torch.randn((len(lens), heads, d), generator=g, device="cuda")
+    q = torch.randn((len(lens), q_heads or heads, d), generator=g, device="cuda")
     out = cache.decode(q, ids).cpu().numpy()
     bt, sl = cache.block_table(ids)
     exact = oracle.decode_paged(q.cpu().numpy(), cache.k_pool.cpu().numpy(),
@@ -70,6 +70,16 @@ def _check(lens, heads, d, value_dtype, seed):
 @pytest.mark.parametrize("d", [64, 128])
 def test_pairs_ragged_float32(kind, d):
     _check(_lens(kind, seed=d), 8, d, torch.float32, seed=len(kind) + d)
+
+
+@pytest.mark.parametrize("kind", ["fewer_pages_than_pairs", "about_two_pages_per_pair",
+                                  "page_aligned", "many_short"])
+@pytest.mark.parametrize("q_heads", [16, 32])
+def test_pairs_ragged_grouped_queries(kind, q_heads):
+    """Grouped queries over 8 kv heads: G = 2 runs two-head warps, G = 4
+    four-head warps, both paired on runs, with the multi-head record merge."""
+    _check(_lens(kind, seed=q_heads), 8, 128, torch.float32, seed=len(kind) + q_heads,
+           q_heads=q_heads)
 
 
 @pytest.mark.parametrize("kind", ["about_two_pages_per_pair", "many_short"])
@@ -93,3 +103,9 @@ def test_pairs_repeat_launches_identical():
     b = cache.decode(q, ids)
     torch.cuda.synchronize()
     assert float((a - b).abs().max()) <= 1e-6
+
+
+@pytest.mark.parametrize("kind", ["fewer_pages_than_pairs", "many_short"])
+@pytest.mark.parametrize("vdtype", ["float16", "bfloat16"])
+def test_pairs_ragged_grouped_queries_values16(kind, vdtype):
+    _check(_lens(kind, seed=3), 8, 128, getattr(torch, vdtype), seed=len(kind) + 7, q_heads=32)
