@@ -100,6 +100,12 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of w
 #ifndef I4KV_PAIR_OWN_EIGHTHS_16
 #define I4KV_PAIR_OWN_EIGHTHS_16 3
 #endif
+// ... and for warps serving several query heads (either value kind).
+// Measured side by side (GQA-4 at 32768 tokens, float32): 3/8 229.4 us,
+// 2/8 233.5, 1/8 237.6; equal within noise at config 0's shape.
+#ifndef I4KV_PAIR_OWN_EIGHTHS_MH
+#define I4KV_PAIR_OWN_EIGHTHS_MH 3
+#endif
 
 // Minimum resident CTAs per SM the compiler plans registers for, for warps
 // serving several query heads over 16-bit value pools.
@@ -618,7 +624,8 @@ paged_decode_kernel(DecodeArgs a) {
   // Each warp of a pair takes a share of the run from its end without asking
   // (3/8 each, leaving a middle quarter -- enough to absorb page rates 25 %
   // apart -- so most pages cost no claim); the rest is claimed page by page.
-  constexpr int kOwnEighths = VK == 0 ? I4KV_PAIR_OWN_EIGHTHS_F32 : I4KV_PAIR_OWN_EIGHTHS_16;
+  constexpr int kOwnEighths = HW > 1 ? I4KV_PAIR_OWN_EIGHTHS_MH
+                              : (VK == 0 ? I4KV_PAIR_OWN_EIGHTHS_F32 : I4KV_PAIR_OWN_EIGHTHS_16);
   const int n_own = paired ? (int)(((long long)n * kOwnEighths) / 8) : n;
   // Claims are pipelined: after a claim succeeds, lane 0 sends the next one at
   // once and its answer is read when that page is due, so the shared-memory
