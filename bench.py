@@ -604,6 +604,37 @@ def run_ours(args):
     mean_step = _all_reduce_max(sum(step_ms) / K, world)
     mean_kern = _all_reduce_max(sum(kern_ms) / K, world)
 
+    # ---- back to back: K launches between one pair of events, no flush ----
+    # How the reference times its operators (src/_prepared.py:1-18: repeated
+    # calls on device-resident inputs) and what a serving loop of decode steps
+    # sees: the launch overhead of one event-bracketed launch (~5 us, the same
+    # for an empty kernel) is amortised. Only where the step's inputs are more
+    # than twice the 126 MB L2, so a launch cannot find the previous launch's
+    # bytes there (a streaming read that large evicts them before they are
+    # reached again; DRAM bytes per launch in this order are checked by ncu).
+    b2b = None
+    bytes_step0 = shape.algorithmic_bytes()
+    if bytes_step0 > 2 * 126e6:
+        b0 = torch.cuda.Event(enable_timing=True)
+        b1 = torch.cuda.Event(enable_timing=True)
+        for _ in range(Wm):
+            if fn(*step_args):
+                raise RuntimeError("decode launch failed")
+        torch.cuda.synchronize()
+        _barrier(world)
+        torch.cuda.synchronize()
+        b0.record()
+        for _ in range(K):
+            rc = fn(*step_args)
+            if rc:
+                raise RuntimeError(f"decode launch failed: cudaError {rc}")
+        b1.record()
+        torch.cuda.synchronize()
+        b2b_ms = _all_reduce_max(b0.elapsed_time(b1) / K, world)
+        b2b = {"kernel_us": round(b2b_ms * 1e3, 2), "launches": K,
+               "achieved": round(bytes_step0 / (b2b_ms * 1e-3) / 1e9, 1),
+               "l2": f"not flushed: inputs {bytes_step0 / 1e6:.1f} MB/GPU > 2 x 126 MB L2"}
+
     # ---- end to end through the C ABI with host buffers ----
     # The step's inputs (query, block table, lengths) are staged in ONE pinned
     # host buffer and land in one device buffer with one copy; the output comes
@@ -760,7 +791,9 @@ def run_ours(args):
                                         "capture of this kernel at this config (not this run)")
                      if traffic is not None else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
-                     "measured" else "fallback 6.65 TB/s"},
+                     "measured" else "fallback 6.65 TB/s",
+                     "back_to_back": dict(b2b, frac=round(b2b["achieved"] / peak, 4))
+                     if b2b is not None else None},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5), "steps": KE,
                 "h2d_bytes_per_step": int(in_bytes),
