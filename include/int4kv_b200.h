@@ -10,6 +10,8 @@
  *     documented exceptions: int4kv_exchange_alloc allocates the peer-exchange
  *     buffer (its whole purpose), and int4kv_paged_decode_static_scratch uses a
  *     library-owned device array shared by every call on a device.
+ *   - int4kv_stage_inputs is the one entry point that reads host memory (mapped
+ *     pinned memory, passed by the caller).
  *
  * Numerical contract: quantizer bins, scales and zero-points are bit-identical
  * to the reference's NumPy oracle (src/quantize_int4_ref.py:51-75: IEEE float32,
@@ -401,6 +403,20 @@ cudaError_t int4kv_paged_decode_static_scratch(const float* query, const uint8_t
                                                int page_tokens, int group_tokens, int max_pages,
                                                int num_pages, float* out, uint32_t* status,
                                                size_t* scratch_needed, cudaStream_t stream);
+
+/* Copy `bytes` from mapped pinned host memory (`src`: the device-usable
+ * address of a cudaHostAlloc(..., cudaHostAllocMapped) buffer, from
+ * cudaHostGetDevicePointer) into device memory `dst`, on `stream`, by SM
+ * loads instead of the copy engine: a decode step's inputs (queries, block
+ * table, lengths) are a few hundred KB at most, where the copy engine's fixed
+ * cost dominates (135 KB: 17.1 us for a pinned cudaMemcpyAsync + a kernel
+ * against 12.3 us for this kernel + the same kernel, between CUDA events on
+ * B200). The loads bypass the device caches, so a host buffer rewritten
+ * between calls is read afresh. Both pointers 16-byte aligned, `bytes` a
+ * multiple of 16 (else cudaErrorInvalidValue, nothing launched). No
+ * counterpart in the reference, whose CUDA path moves every input to the
+ * device with a torch copy (src/ops.py:307). */
+cudaError_t int4kv_stage_inputs(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
 /* Library identification: returns a static string naming the build. */
 const char* int4kv_build_info(void);

@@ -37,6 +37,7 @@ _PROTOS = {
     "int4kv_cache_write_ex": [_c_void_p, _c_void_p, _c_void_p, _c_void_p] + [_c_int] * 6
                              + [_c_void_p, _c_int, _c_int] + [_c_void_p, _c_void_p, _c_int]
                              + [_c_void_p] * 3,
+    "int4kv_stage_inputs": [_c_void_p, _c_void_p, _c_size_t, _c_void_p],
     "int4kv_cache_append": [_c_void_p] * 5 + [_c_int] * 6 + [_c_void_p, _c_int, _c_int]
                            + [_c_void_p, _c_void_p, _c_int] + [_c_void_p] * 3,
     "int4kv_rope": [_c_void_p, _c_void_p] + [_c_int] * 3 + [_c_void_p, _c_void_p, _c_int]

@@ -68,3 +68,51 @@ def test_decode_output_to_mapped_host_memory(batch, heads, q_heads, lens, vdtype
                     assert np.all(got[b] == 0)
     finally:
         rt.cudaFreeHost(hptr)
+
+
+@pytest.mark.parametrize("nbytes", [16, 4112, 135200, 3 << 20])
+def test_stage_inputs_from_mapped_host_memory(nbytes):
+    """int4kv_stage_inputs copies mapped pinned host memory into device memory
+    with SM loads; a second call after the host rewrote the buffer sees the
+    new bytes (no stale copy cached on the device)."""
+    pkg("_build").build()
+    lib = pkg("_lib").load()
+    err, hptr = rt.cudaHostAlloc(nbytes, rt.cudaHostAllocMapped)
+    assert err == rt.cudaError_t.cudaSuccess
+    try:
+        err, dptr = rt.cudaHostGetDevicePointer(hptr, 0)
+        assert err == rt.cudaError_t.cudaSuccess
+        host = np.frombuffer((ctypes.c_uint8 * nbytes).from_address(hptr), dtype=np.uint8)
+        dev = torch.zeros((nbytes,), dtype=torch.uint8, device="cuda")
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rng = np.random.default_rng(nbytes)
+        for _ in range(2):
+            host[:] = rng.integers(0, 256, nbytes, dtype=np.uint8)
+            rc = lib.int4kv_stage_inputs(ctypes.c_void_p(dev.data_ptr()), ctypes.c_void_p(dptr),
+                                         nbytes, stream)
+            assert rc == 0, f"int4kv_stage_inputs: cudaError {rc}"
+            torch.cuda.synchronize()
+            assert np.array_equal(dev.cpu().numpy(), host)
+    finally:
+        rt.cudaFreeHost(hptr)
+
+
+def test_stage_inputs_rejects_unaligned_arguments():
+    pkg("_build").build()
+    lib = pkg("_lib").load()
+    err, hptr = rt.cudaHostAlloc(4096, rt.cudaHostAllocMapped)
+    assert err == rt.cudaError_t.cudaSuccess
+    try:
+        err, dptr = rt.cudaHostGetDevicePointer(hptr, 0)
+        assert err == rt.cudaError_t.cudaSuccess
+        dev = torch.full((4096,), 7, dtype=torch.uint8, device="cuda")
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        d = dev.data_ptr()
+        for dst, src, n in [(d, dptr, 40), (d + 8, dptr, 64), (d, dptr + 4, 64), (d, dptr, 0),
+                            (0, dptr, 64), (d, 0, 64)]:
+            rc = lib.int4kv_stage_inputs(ctypes.c_void_p(dst), ctypes.c_void_p(src), n, stream)
+            assert rc == 1  # cudaErrorInvalidValue, nothing launched
+        torch.cuda.synchronize()
+        assert bool((dev == 7).all())
+    finally:
+        rt.cudaFreeHost(hptr)
