@@ -298,10 +298,16 @@ def stream_gate(torch, out, query, cache, bt, sl, streams, group_q=1):
     return err
 
 
-def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, seed=0):
+def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, seed=0,
+                  b2b=False, copies=()):
     """CUDA-event time of the decode kernel alone (events recorded by the C ABI
     around the launch) on a built problem, L2 flushed before every launch,
-    behind a float64 gate on `gate_streams` seeded streams."""
+    behind a float64 gate on `gate_streams` seeded streams. With `b2b`, also K
+    launches back to back between one pair of events with no flush, rotating
+    over the problem and its `copies` (more problems of the same shape, each
+    gated the same way) so that the bytes a launch reads were last read
+    len(copies) launches earlier: the caller passes enough copies that this is
+    more than twice the L2."""
     import ctypes
     cache, query = prob["cache"], prob["query"]
     ids = list(range(shape.batch))
@@ -318,12 +324,18 @@ def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, 
         a.record()
         b.record()
 
-    def launch(e0=None, e1=None):
-        rc = lib.int4kv_paged_decode_ex(
-            query.data_ptr(), cache.k_pool.data_ptr(), cache.v_pool.data_ptr(), vk,
-            cache.sz_pool.data_ptr(), bt.data_ptr(), sl.data_ptr(), shape.batch, hq, h, d, 16,
-            shape.group_tokens, bt.shape[1], cache.num_pages, out.data_ptr(), ws.data_ptr(),
-            ws_bytes, None, stream.cuda_stream, e0, e1)
+    def args_of(p):
+        c, q = p["cache"], p["query"]
+        b_t, s_l = (bt, sl) if p is prob else c.block_table(ids)
+        return (q.data_ptr(), c.k_pool.data_ptr(), c.v_pool.data_ptr(), vk, c.sz_pool.data_ptr(),
+                b_t.data_ptr(), s_l.data_ptr(), shape.batch, hq, h, d, 16, shape.group_tokens,
+                b_t.shape[1], c.num_pages, out.data_ptr(), ws.data_ptr(), ws_bytes, None,
+                stream.cuda_stream), (b_t, s_l)
+
+    a0, _ = args_of(prob)
+
+    def launch(e0=None, e1=None, a=a0):
+        rc = lib.int4kv_paged_decode_ex(*a, e0, e1)
         if rc:
             raise RuntimeError(f"decode launch failed: cudaError {rc}")
 
@@ -343,8 +355,28 @@ def decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, gate_streams=4, 
         launch(ctypes.c_void_p(a.cuda_event), ctypes.c_void_p(b.cuda_event))
     torch.cuda.synchronize()
     us = [a.elapsed_time(b) * 1e3 for a, b in ev]
-    return {"kernel_us": round(sum(us) / K, 2), "kernel_us_p50": round(float(np.median(us)), 2),
-            "gate_streams": len(streams), "max_abs_vs_f64_arbiter": gate}
+    rec = {"kernel_us": round(sum(us) / K, 2), "kernel_us_p50": round(float(np.median(us)), 2),
+           "gate_streams": len(streams), "max_abs_vs_f64_arbiter": gate}
+    if b2b:
+        rot = [args_of(p) for p in (prob,) + tuple(copies)]  # keeps each copy's tables alive
+        for p, (a, (b_t, s_l)) in zip((prob,) + tuple(copies), rot):
+            launch(a=a)
+            torch.cuda.synchronize()
+            g = stream_gate(torch, out, p["query"], p["cache"], b_t, s_l, streams, hq // h)
+            if not (torch.isfinite(out).all() and g <= 1e-6):
+                raise RuntimeError(f"decode failed its correctness gate on a copy (max err {g})")
+            rec["max_abs_vs_f64_arbiter"] = max(rec["max_abs_vs_f64_arbiter"], g)
+        for i in range(max(3, len(rot))):  # untimed: the rotation once round
+            launch(a=rot[i % len(rot)][0])
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        for i in range(K):
+            launch(a=rot[i % len(rot)][0])
+        b1.record()
+        torch.cuda.synchronize()
+        rec["back_to_back_us"] = round(b0.elapsed_time(b1) * 1e3 / K, 2)
+        rec["back_to_back_problems"] = len(rot)
+    return rec
 
 
 def sweep_records(torch, lib, C, W, K, flush, peak):
@@ -362,13 +394,23 @@ def sweep_records(torch, lib, C, W, K, flush, peak):
         shape = W.config_shape(name)
         shape.value_bytes = 4 if vdtype == torch.float32 else 2
         prob = W.torch_build_cache(shape, seed=7, value_dtype=vdtype)
-        r = decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, seed=1)
         nbytes = shape.algorithmic_bytes()
+        # back to back: the problem alone when it is more than twice the 126 MB
+        # L2, else rotating over it and copies with other seeds, so that more
+        # than twice the L2 is read between two reads of the same bytes
+        l2x2 = 2 * 126_000_000
+        ncopy = 0 if nbytes > l2x2 else -(-l2x2 // nbytes)
+        copies = tuple(W.torch_build_cache(shape, seed=8 + i, value_dtype=vdtype)
+                       for i in range(ncopy))
+        r = decode_timing(torch, lib, C, shape, prob, vdtype, K, flush, seed=1, b2b=True,
+                          copies=copies)
         r.update({"algorithmic_bytes": nbytes,
                   "gbs": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9, 1),
-                  "frac": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9 / peak, 4)})
+                  "frac": round(nbytes / (r["kernel_us"] * 1e-6) / 1e9 / peak, 4),
+                  "back_to_back_frac": round(nbytes / (r["back_to_back_us"] * 1e-6) / 1e9 / peak,
+                                             4)})
         recs[label] = r
-        del prob
+        del prob, copies
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
     return recs
