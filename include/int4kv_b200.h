@@ -145,7 +145,12 @@ cudaError_t int4kv_cache_write(const float* k, const float* v, const int32_t* to
  * INT4KV_STATUS_* bits. `out` may also be the device pointer of mapped
  * pinned host memory (cudaHostAlloc with cudaHostAllocMapped): every output
  * row is stored once, with plain stores, so the result reaches the host
- * without a separate device-to-host copy. */
+ * without a separate device-to-host copy. The kernel is launched with
+ * programmatic stream serialization (programmatic dependent launch): its
+ * CTAs may become resident while the previous kernel on `stream` still runs,
+ * but each first waits for that kernel's completion and memory, so stream
+ * order is kept; it lets its own successor be dispatched once its page loops
+ * are done (a following decode or any kernel launched the same way). */
 cudaError_t int4kv_paged_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
                                                int head_dim, size_t* bytes);
 cudaError_t int4kv_paged_decode(const float* query, const uint8_t* k_pool, const float* v_pool,

@@ -107,6 +107,17 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s of w
 #define I4KV_PAIR_OWN_EIGHTHS_MH 3
 #endif
 
+// Programmatic dependent launch: the decode is launched with programmatic
+// stream serialization, so its CTAs may become resident while the kernel
+// before it on the stream is still running; every thread first waits for
+// that kernel's completion and memory (griddepcontrol.wait, a no-op when the
+// predecessor was not a kernel or the attribute is off), so nothing is read
+// early. Each thread signals its own dependents after its page loop, so a
+// following launch of this kernel can be dispatched while this one merges.
+#ifndef I4KV_DECODE_PDL
+#define I4KV_DECODE_PDL 1
+#endif
+
 // Minimum resident CTAs per SM the compiler plans registers for, for warps
 // serving several query heads over 16-bit value pools.
 #ifndef I4KV_MULTIHEAD16_MIN_CTAS
@@ -538,6 +549,7 @@ __global__ void __launch_bounds__(WARPS * 32, VK == 0 ? (D <= 128 ? (HW >= 4 ? 2
 paged_decode_kernel(DecodeArgs a) {
   using C = Cfg<D, WARPS, STAGES, VK>;
   constexpr int DPL = C::DPL;
+  if constexpr (I4KV_DECODE_PDL) grid_dependency_wait();  // the predecessor's writes are visible
   extern __shared__ __align__(128) char smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                 // WARPS*STAGES
   int* s_tmp = reinterpret_cast<int*>(smem + 8 * WARPS * STAGES);      // WARPS ints
@@ -1510,6 +1522,7 @@ paged_decode_kernel(DecodeArgs a) {
     }
   }
 
+  if constexpr (I4KV_DECODE_PDL) allow_dependent_launch();
   if (aborted) {
     // The group's leader drains what the ring still has in flight (bounded)
     // before leaving, so no bulk copy lands in shared memory after the CTA
@@ -1767,8 +1780,18 @@ cudaError_t launch_hw(const DecodeArgs& a, size_t ws_bytes, cudaStream_t stream,
   if (e != cudaSuccess) return e;
   if (ws_bytes < need) return cudaErrorInvalidValue;
   if (ev_before && (e = cudaEventRecord(ev_before, stream)) != cudaSuccess) return e;
-  paged_decode_kernel<D, kWarps, kStages, VK, HW>
-      <<<grid, kWarps * 32, dyn_smem<D, VK>(a.batch, a.gs, HW), stream>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = dyn_smem<D, VK>(a.batch, a.gs, HW);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = I4KV_DECODE_PDL ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<D, kWarps, kStages, VK, HW>, a);
+  if (e != cudaSuccess) return e;
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ev_after && (e = cudaEventRecord(ev_after, stream)) != cudaSuccess) return e;

@@ -22,6 +22,10 @@ constexpr long long kStageMaxBlocks = 1184;  // 8 per SM on a 148-SM B200; large
 // line of host memory cached on the device by an earlier call would be stale.
 __global__ void __launch_bounds__(kStageThreads)
 stage_host_kernel(uint4* __restrict__ dst, const uint4* src, long long n16) {
+  // a kernel launched after this one with programmatic stream serialization
+  // (the paged decode) may be dispatched at once; it waits for this grid's
+  // completion before it reads anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16;
        i += stride * kStageUnroll) {
