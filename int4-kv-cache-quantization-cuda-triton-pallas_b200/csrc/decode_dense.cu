@@ -275,6 +275,9 @@ __global__ void __launch_bounds__(kThreads)
 shared_stream_decode_kernel(DenseArgs a) {
   using Cf = DCfg<DP, PACKED, VK>;
   constexpr int QT = Cf::QT;
+  // launched with programmatic stream serialization: wait for the previous
+  // kernel on the stream (its completion and memory) before anything else
+  grid_dependency_wait();
   extern __shared__ __align__(128) char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int S = (int)cluster.num_blocks();
@@ -463,6 +466,7 @@ shared_stream_decode_kernel(DenseArgs a) {
   }
   cp_async_wait<0>();
 
+  allow_dependent_launch();  // a following launch may be dispatched during the merge
   // ---- merge the cluster's S partial states through distributed shared memory ----
   float* s_acc = reinterpret_cast<float*>(smem + Cf::OFF_V);  // [QT][DP], over the value stages
   __syncthreads();
@@ -553,13 +557,17 @@ cudaError_t launch_shared(const DenseArgs& a, cudaStream_t stream) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cf::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // programmatic dependent launch: dispatched while the previous kernel on
+  // the stream finishes; the kernel's first instruction waits for it
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, a);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -684,13 +684,17 @@ grouped_quant_loop_kernel(const float* __restrict__ kv, int N, int C, int R, Out
 //                           chunk is read again, from L2 when it fits there)
 //   4. legacy_params      : scale_out / zp_out <- scale, zp of each channel
 // Steps 2-4 call grid_dependency_wait() before they touch what the step before
-// wrote, so starting early never changes a result.
+// wrote, so starting early never changes a result. Step 1 is launched the same
+// way and waits first for whatever kernel precedes it on the stream (a
+// previous call's step 4 writes the same outputs); step 4 lets the next
+// call's step 1 be dispatched while it runs.
 constexpr int kLegWarps = 8;
 constexpr int kLegTile = 128;  // channels per CTA (32 lanes x 4)
 
 __global__ void __launch_bounds__(256)
 legacy_keys_init(float* __restrict__ scale_out, float* __restrict__ zp_out, int C) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  grid_dependency_wait();  // the previous kernel on the stream is done with the outputs
   if (c < C) {
     reinterpret_cast<uint32_t*>(scale_out)[c] = 0u;           // below the key of any float
     reinterpret_cast<uint32_t*>(zp_out)[c] = 0xffffffffu;     // above the key of any float
@@ -849,6 +853,7 @@ __global__ void __launch_bounds__(256)
 legacy_params(float* __restrict__ scale_out, float* __restrict__ zp_out, int C) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   grid_dependency_wait();  // every CTA of the codes step has read the keys
+  allow_dependent_launch();
   if (c < C) {
     const float mx = from_ordered_key(reinterpret_cast<const uint32_t*>(scale_out)[c]);
     const float mn = from_ordered_key(reinterpret_cast<const uint32_t*>(zp_out)[c]);
@@ -966,8 +971,7 @@ cudaError_t cu_quantize_int4(const float* kv, int num_rows, int num_channels, ui
   const bool vec = C % 4 == 0 && aligned16(kv) && (reinterpret_cast<uintptr_t>(q_out) & 3u) == 0;
   const dim3 grid(chunks, tiles), block(kLegWarps * 32);
   const dim3 pgrid((C + 255) / 256), pblock(256);
-  legacy_keys_init<<<pgrid, pblock, 0, stream>>>(scale_out, zp_out, C);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(legacy_keys_init, pgrid, pblock, stream, scale_out, zp_out, C);
   if (e != cudaSuccess) return e;
   e = vec ? launch_pdl(legacy_minmax<true>, grid, block, stream, kv, num_rows, C, chunk,
                        scale_out, zp_out)
