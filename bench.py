@@ -147,8 +147,10 @@ def workload_config(shape, name, world):
             "heads": shape.query_heads, "kv_heads": shape.heads, "head_dim": shape.head_dim,
             "seq_len": seq_len,
             "page_tokens": 16, "group_tokens": shape.group_tokens,
-            "l2": "flushed (256 MiB write + 256 MiB read, untimed) before every timed step; inputs "
-                  f"{shape.algorithmic_bytes() / 1e6:.1f} MB/GPU > 126 MB L2",
+            "l2": (f"not flushed between steps: inputs {shape.algorithmic_bytes() / 1e6:.1f} MB/GPU "
+                   "> 2 x 126 MB L2" if shape.algorithmic_bytes() > 2 * 126e6 else
+                   "flushed (256 MiB write + 256 MiB read, untimed) before every timed step; "
+                   f"inputs {shape.algorithmic_bytes() / 1e6:.1f} MB/GPU"),
             "parallelism": f"dp{world} (batch x heads sharded, no collective)"}
 
 
@@ -658,14 +660,15 @@ def run_ours(args):
     mean_step = _all_reduce_max(sum(step_ms) / K, world)
     mean_kern = _all_reduce_max(sum(kern_ms) / K, world)
 
-    # ---- back to back: K launches between one pair of events, no flush ----
-    # How the reference times its operators (src/_prepared.py:1-18: repeated
-    # calls on device-resident inputs) and what a serving loop of decode steps
-    # sees: the launch overhead of one event-bracketed launch (~5 us, the same
-    # for an empty kernel) is amortised. Only where the step's inputs are more
-    # than twice the 126 MB L2, so a launch cannot find the previous launch's
-    # bytes there (a streaming read that large evicts them before they are
-    # reached again; DRAM bytes per launch in this order are checked by ncu).
+    # ---- the headline: K steps back to back between one pair of events ----
+    # K steps bracketed by a barrier and a device synchronize, no flush between
+    # them: the benchmark contract's own procedure (and the reference's,
+    # benchmarks/bench_three_backend.py:273-291), valid here because the
+    # step's inputs are more than twice the 126 MB L2 -- a launch cannot find
+    # the previous launch's bytes there (a streaming read that large evicts
+    # them before they are reached again; ncu shows DRAM bytes per launch =
+    # algorithmic bytes in this order). Smaller configurations keep the
+    # flushed, event-bracketed step above as their headline.
     b2b = None
     bytes_step0 = shape.algorithmic_bytes()
     if bytes_step0 > 2 * 126e6:
@@ -684,10 +687,9 @@ def run_ours(args):
                 raise RuntimeError(f"decode launch failed: cudaError {rc}")
         b1.record()
         torch.cuda.synchronize()
-        b2b_ms = _all_reduce_max(b0.elapsed_time(b1) / K, world)
-        b2b = {"kernel_us": round(b2b_ms * 1e3, 2), "launches": K,
-               "achieved": round(bytes_step0 / (b2b_ms * 1e-3) / 1e9, 1),
-               "l2": f"not flushed: inputs {bytes_step0 / 1e6:.1f} MB/GPU > 2 x 126 MB L2"}
+        b2b_local = b0.elapsed_time(b1) / K
+        b2b_ms = _all_reduce_max(b2b_local, world)
+        b2b = {"kernel_us": round(b2b_ms * 1e3, 2), "launches": K, "ms": b2b_ms}
 
     # ---- end to end through the C ABI with host buffers ----
     # The step's inputs (query, block table, lengths) are staged in ONE mapped
@@ -736,11 +738,25 @@ def run_ours(args):
         if rc:
             raise RuntimeError(f"decode launch failed: cudaError {rc}")
     torch.cuda.synchronize()
+    e2e_b2b_ms = None
+    if b2b is not None:  # the same steps back to back (each still stages its inputs from host)
+        _barrier(world)
+        torch.cuda.synchronize()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record()
+        for i in range(KE):
+            rc = stage(*stage_args) or fn(*ea)
+            if rc:
+                raise RuntimeError(f"decode launch failed: cudaError {rc}")
+        x1.record()
+        torch.cuda.synchronize()
+        e2e_b2b_ms = _all_reduce_max(x0.elapsed_time(x1) / KE, world)
     t_wall1 = time.perf_counter()
     sampler.window = "timed loops (step, kernel-only, end-to-end)"
     sampler.mark(t_wall0, t_wall1)
     _barrier(world)
-    e2e_ms = _all_reduce_max(sum(a.elapsed_time(b) for a, b in ee) / KE, world)
+    e2e_flushed_ms = _all_reduce_max(sum(a.elapsed_time(b) for a, b in ee) / KE, world)
+    e2e_ms = e2e_b2b_ms if e2e_b2b_ms is not None else e2e_flushed_ms
     e2e_out = torch.from_numpy(out_map.array(np.float32).reshape(tuple(out.shape)).copy())
     e2e_diff = float((e2e_out - out.cpu()).abs().max())
     if not (torch.isfinite(e2e_out).all() and e2e_diff <= 1e-6):
@@ -776,9 +792,11 @@ def run_ours(args):
         reason_bits = sum(1 << i for i, n in enumerate(CLOCK_REASONS) if n in ck["reasons"])
         stats = gather_per_rank(torch, [sum(step_ms) / K * 1e3, sum(kern_ms) / K * 1e3, seed,
                                         float(ck["sm_mhz"] or 0), float(ck.get("mem_mhz") or 0),
-                                        float(reason_bits)], world)
-        per_rank = {"step_us": [round(x[0], 2) for x in stats],
-                    "kernel_us": [round(x[1], 2) for x in stats],
+                                        float(reason_bits),
+                                        b2b_local * 1e3 if b2b is not None else 0.0], world)
+        per_rank = {"step_us": [round(x[6] if b2b is not None else x[0], 2) for x in stats],
+                    "flushed_step_us": [round(x[0], 2) for x in stats],
+                    "flushed_kernel_us": [round(x[1], 2) for x in stats],
                     "seed": [int(x[2]) for x in stats],
                     "sm_mhz": [x[3] for x in stats], "mem_mhz": [x[4] for x in stats],
                     "clock_reasons": [[n for i, n in enumerate(CLOCK_REASONS) if int(x[5]) >> i & 1]
@@ -827,6 +845,23 @@ def run_ours(args):
                                                       for (b, hh), o in outs.items()))
 
     total_bytes = bytes_step * world
+    flushed = {"step_us": round(mean_step * 1e3, 2), "kernel_us": round(mean_kern * 1e3, 2),
+               "frac": round(bytes_step / (mean_kern * 1e-3) / 1e9 / peak, 4),
+               "step_us_percentiles": {k: round(float(np.percentile(step_ms, q)) * 1e3, 2)
+                                       for k, q in (("p10", 10), ("p50", 50), ("p90", 90),
+                                                    ("max", 100))},
+               "timing": "L2 flushed before every launch; step: CUDA events around the C-ABI "
+                         "call; kernel: events recorded by the C ABI around the launch",
+               "e2e_ms_per_step": round(e2e_flushed_ms, 5)}
+    if b2b is not None:  # headline: K steps back to back (inputs > 2 x L2)
+        mean_step = mean_kern = b2b["ms"]
+        timing = (f"K={K} steps back to back between one pair of CUDA events after a barrier + "
+                  f"synchronize, no flush: inputs {bytes_step / 1e6:.1f} MB/GPU > 2 x 126 MB L2 "
+                  "(ncu: DRAM bytes per launch = algorithmic bytes in this order, "
+                  "profiles/paged_decode_cfg0_back_to_back.md)")
+    else:
+        timing = ("L2 flushed (256 MiB write + 256 MiB read, untimed) before every timed step; "
+                  "CUDA events around each step")
     value = total_bytes / (mean_step * 1e-3) / 1e9
     achieved = bytes_step / (mean_kern * 1e-3) / 1e9
     traffic = profile_traffic() if args.config == "cfg0" else None
@@ -836,25 +871,27 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None,
         "dtype": f"fp32 (exact integer logits, fp64 recombination), int4 keys, {args.values} values",
         "data": "synthetic (seeded: q~N(0,1); keys N(0,1)*U(0.5,3)+N(0,2) per channel; v~N(0,1))",
+        "timing": timing,
         "config": dict(workload_config(shape, args.config, world),
                        problem_per_rank=("own seed per rank: 7 + 1000 * rank" if args.rank_seeds
                                          else "rank 0's seeded problem (seed 7) on every rank")),
         "decode_us": round(mean_step * 1e3, 2),
-        "step_us_percentiles": {k: round(float(np.percentile(step_ms, q)) * 1e3, 2)
-                                for k, q in (("p10", 10), ("p50", 50), ("p90", 90), ("max", 100))},
         "hbm_frac_of_peak": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": f"paged_decode_kernel<{d},4,2> (decode + fused combine)",
                      "kernel_us": round(mean_kern * 1e3, 2),
+                     "kernel_us_source": ("the back-to-back step: K launches between one pair "
+                                          "of events, the step is one launch" if b2b is not None
+                                          else "events recorded by the C ABI around the launch, "
+                                          "L2 flushed"),
                      "algorithmic_bytes_per_launch": bytes_step,
                      "traffic_source": ("profiles/paged_decode_cfg0.md: static, from one ncu "
                                         "capture of this kernel at this config (not this run)")
                      if traffic is not None else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
-                     "measured" else "fallback 6.65 TB/s",
-                     "back_to_back": dict(b2b, frac=round(b2b["achieved"] / peak, 4))
-                     if b2b is not None else None},
+                     "measured" else "fallback 6.65 TB/s"},
+        "flushed": flushed,
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5), "steps": KE,
                 "h2d_bytes_per_step": int(in_bytes),
