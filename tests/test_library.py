@@ -171,3 +171,24 @@ def test_benchmark_config_shapes():
     for bad in ("cfg2_512_gqa5", "cfg0_gqa3", "cfg9"):
         with pytest.raises(ValueError):
             W.config_shape(bad)
+
+
+def test_benchmark_headline_timing_follows_the_l2_rule():
+    """The bench times its headline step back to back (no flush) only where a
+    step's inputs are more than twice the 126 MB L2, and says so in `config`;
+    smaller configurations keep the L2 flush between steps."""
+    import importlib
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    bench = importlib.import_module("bench")
+    W = pkg("workloads")
+    for name in ("cfg0", "cfg2_8192", "cfg4_long"):
+        shape = W.config_shape(name)
+        assert shape.algorithmic_bytes() > 2 * 126e6
+        assert bench.workload_config(shape, name, 1)["l2"].startswith("not flushed")
+    for name in ("cfg2_512", "cfg0_gqa4", "cfg0_gqa8"):
+        shape = W.config_shape(name)
+        assert shape.algorithmic_bytes() <= 2 * 126e6
+        assert bench.workload_config(shape, name, 1)["l2"].startswith("flushed")
