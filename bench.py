@@ -8,7 +8,12 @@ scale/zp, fp32 values), inputs resident in HBM. With N GPUs every rank owns
 its own config-0 batch (batch x heads sharded, no collective): weak scaling.
 
 Prints ONE JSON line (rank 0). `value` = algorithmic HBM bytes of all ranks
-per step / step time (max over ranks), in GB/s.
+per step / step time (max over ranks), in GB/s. The step time is K steps back
+to back between one pair of CUDA events after a barrier and a synchronize,
+with no L2 flush where a step's inputs exceed twice the 126 MB L2 (config 0:
+306.5 MB); otherwise the L2 is flushed before every step and each step is
+timed with its own events. The flushed, per-launch figures are reported
+beside the headline under `flushed`.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
